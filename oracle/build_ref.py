@@ -1,0 +1,61 @@
+"""TEST INFRASTRUCTURE ONLY: compile the reference's own CPU op from its sources.
+
+Builds ``streamtopk_sae_native`` (CPU entry ``streamtopk_cpu_forward`` only)
+from the two reference source files where they lie:
+
+    <ref>/streamtopk_sae/csrc/bindings.cpp           (pybind module, WITH_CUDA unset)
+    <ref>/streamtopk_sae/csrc/cpu/streamtopk_cpu.cpp (process_row / dispatch_rows)
+
+with the reference's C++ flags (``setup.py:15-28``: -O3 -ffast-math), except
+that ``-march=native`` becomes ``-march=x86-64-v3`` so the object built here
+also runs on the GPU box's host CPU.  Output goes only to ``oracle/_ref/``
+(git-ignored; it travels to the GPU box with the snapshot).  No reference
+source is copied into this repository.
+
+Usage: python oracle/build_ref.py [--ref /path/to/reference]
+"""
+import argparse
+import os
+import shutil
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+OUT = os.path.join(HERE, "_ref")
+
+
+def build(ref_root: str, verbose: bool = False) -> str:
+    csrc = os.path.join(ref_root, "streamtopk_sae", "csrc")
+    sources = [os.path.join(csrc, "bindings.cpp"),
+               os.path.join(csrc, "cpu", "streamtopk_cpu.cpp")]
+    for s in sources:
+        if not os.path.isfile(s):
+            raise FileNotFoundError(s)
+    os.makedirs(OUT, exist_ok=True)
+    from torch.utils.cpp_extension import load
+    build_dir = os.path.join(OUT, "build")
+    os.makedirs(build_dir, exist_ok=True)
+    mod = load(name="streamtopk_sae_native", sources=sources,
+               extra_include_paths=[csrc],
+               extra_cflags=["-O3", "-march=x86-64-v3", "-ffast-math"],
+               build_directory=build_dir, verbose=verbose, with_cuda=False)
+    so = mod.__file__
+    dst = os.path.join(OUT, os.path.basename(so))
+    if os.path.abspath(so) != os.path.abspath(dst):
+        shutil.copy2(so, dst)
+    return dst
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("-v", action="store_true")
+    a = ap.parse_args()
+    if not os.path.isdir(a.ref):
+        print(f"reference tree {a.ref} absent; skipping oracle/_ref build")
+        return 0
+    print(build(a.ref, a.v))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
