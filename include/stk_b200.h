@@ -1,0 +1,135 @@
+/*
+ * stk_b200.h -- C ABI of the B200 (sm_100a) streaming top-k SAE encoder.
+ *
+ *   scores = X @ W_enc^T + b_enc        (B, F), never written to memory
+ *   V, I   = top_k(scores, k)           V fp32 (B, k) descending, I int32 (B, k)
+ *
+ * Plain pointers and sizes only; every pointer argument is device memory on
+ * the current CUDA device unless stated otherwise; `stream` is a cudaStream_t
+ * (NULL = legacy default stream).  All calls are asynchronous on `stream` and
+ * allocate nothing: scratch memory is caller-provided (`workspace`, sized by
+ * stk_workspace_bytes).
+ *
+ * Return value: STK_OK (0) or an STK_E* code; stk_last_error() gives the
+ * message of the last failing call on the calling thread.  Argument messages
+ * repeat the reference's TORCH_CHECK texts.
+ *
+ * Ties: among equal scores the smaller feature index ranks first, so results
+ * do not depend on how F is tiled, on the number of CTAs or on the number of
+ * GPUs.
+ */
+#ifndef STK_B200_H
+#define STK_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define STK_API __attribute__((visibility("default")))
+#else
+#define STK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum stk_status {
+  STK_OK = 0,
+  STK_EINVAL = 1,   /* bad argument (message in stk_last_error) */
+  STK_ECUDA = 2,    /* CUDA runtime / driver error */
+  STK_EDEVICE = 3,  /* a kernel reported a device-side error (bounded wait ran out) */
+  STK_ENOSPACE = 4  /* workspace too small */
+};
+
+enum stk_dtype { STK_F32 = 0, STK_F16 = 1, STK_BF16 = 2 };
+
+/* Flags for the *_forward calls. */
+enum stk_flags {
+  STK_FLAG_ANY_K = 1, /* accept any 1 <= k <= 128, not only {1,2,4,8,16,32,64,128} */
+  STK_FLAG_ANY_D = 2, /* lift the reference's d <= 4096 limit */
+  STK_FLAG_SIMT = 4   /* force the fp32 SIMT kernel (testing / comparison) */
+};
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+STK_API int stk_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+STK_API const char* stk_last_error(void);
+
+/* Length L of the per-row key lists used for a given k (32, 64 or 128; 0 if k > 128). */
+STK_API int stk_list_len(int64_t k);
+
+/*
+ * Bytes of device workspace stk_exact_forward / stk_approx_forward /
+ * stk_shard_forward need for this shape on the current device.
+ */
+STK_API int stk_workspace_bytes(int64_t B, int64_t d, int64_t F, int64_t k, int dtype, size_t* bytes);
+
+/*
+ * Exact streaming top-k encode.
+ * Replaces streamtopk_cuda_exact_forward(X, W_enc, b_enc, k)
+ *   (reference: streamtopk_sae/csrc/cuda/streamtopk_exact.cu:788-833, bound in
+ *    streamtopk_sae/csrc/bindings.cpp:33-34 and called from
+ *    streamtopk_sae/ops.py:43-57).
+ * X (B, d) and W (F, d) row-major in `dtype`; b (F,) fp32; V (B, k) fp32 and
+ * I (B, k) int32 outputs, each row descending.
+ */
+STK_API int stk_exact_forward(const void* X, const void* W, const float* b, float* V, int32_t* I, int64_t B, int64_t d,
+                      int64_t F, int64_t k, int dtype, int flags, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/*
+ * Approximate (per-128-feature-tile top-c candidates) encode, final top-k
+ * included.  Replaces streamtopk_cuda_approx_forward + the torch.topk/gather
+ * that follows it (reference: streamtopk_sae/csrc/cuda/streamtopk_approx.cu:
+ * 234-291 and streamtopk_sae/ops.py:60-83).  c must be in {16,32,64,128} and
+ * k <= c, as in the reference.  For k <= c the tile filter keeps every
+ * feature of the global top-k (a top-k feature ranks <= k <= c inside its
+ * tile), so the result equals stk_exact_forward's.
+ */
+STK_API int stk_approx_forward(const void* X, const void* W, const float* b, float* V, int32_t* I, int64_t B, int64_t d,
+                       int64_t F, int64_t k, int64_t c, int dtype, int flags, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/*
+ * Per-tile candidates of the approximate path: for every row and every
+ * 128-feature tile t, the tile's best c scores, descending, padded with
+ * (-FLT_MAX, -1) where the tile holds fewer than c features.
+ * cand_vals / cand_idxs: (B, ceil(F/128), c).  Replaces the candidate buffer
+ * written by streamtopk_approx_kernel (streamtopk_approx.cu:42-167).
+ */
+STK_API int stk_approx_candidates(const void* X, const void* W, const float* b, float* cand_vals, int32_t* cand_idxs,
+                          int64_t B, int64_t d, int64_t F, int64_t c, int dtype, void* stream);
+
+/*
+ * One F-shard of a multi-GPU encode: the best L = stk_list_len(k) keys per row
+ * of this shard, with feature indices offset by `index_offset`, written as
+ * sorted 64-bit keys to keys_out (B, L).  Keys from several shards are
+ * combined by stk_merge_keys.  (No reference counterpart: the reference has no
+ * multi-GPU path.)
+ */
+STK_API int stk_shard_forward(const void* X, const void* W_shard, const float* b_shard, uint64_t* keys_out, int64_t B,
+                      int64_t d, int64_t F_shard, int64_t k, int64_t index_offset, int dtype, int flags,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Final merge of n key lists per row: lists (n, B, L) as written by
+ * stk_shard_forward (e.g. after an all-gather), L = stk_list_len(k).
+ * Writes V (B, k) fp32 and I (B, k) int32.  Replaces the reference's merge
+ * pass (streamtopk_exact.cu:429-499) for the cross-GPU step.
+ */
+STK_API int stk_merge_keys(const uint64_t* lists, int64_t nlists, int64_t B, int64_t k, float* V, int32_t* I,
+                   void* stream);
+
+/*
+ * Synchronise `stream`, then read and clear the device error word of the
+ * current device.  *code = 0 if no kernel reported an error.
+ */
+STK_API int stk_device_error(void* stream, unsigned* code);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* STK_B200_H */

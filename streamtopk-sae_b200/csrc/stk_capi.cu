@@ -1,0 +1,347 @@
+// C ABI of the encoder (include/stk_b200.h): argument checks with the
+// reference's messages, path and tile selection, TMA descriptor encoding,
+// work decomposition and launches.  No allocation happens here: the caller
+// passes the workspace.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <numeric>
+#include <string>
+
+#include "../../include/stk_b200.h"
+#include "stk_kernels.cuh"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  g_err = std::string(where) + ": " + cudaGetErrorName(e) + ": " + cudaGetErrorString(e);
+  return STK_ECUDA;
+}
+
+constexpr int kMaxDevices = 64;
+struct DeviceInfo {
+  int sms = 0;
+};
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int device_sms(int* sms) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(STK_EINVAL, "device ordinal out of range");
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (g_dev[dev].sms == 0) {
+    int n = 0;
+    e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    g_dev[dev].sms = n;
+  }
+  *sms = g_dev[dev].sms;
+  return STK_OK;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D K-major tensor map over a (rows, d) row-major 16-bit matrix with a
+// (64 x box_rows) box and 128-byte swizzle; out-of-range elements read as 0.
+int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t d, int box_rows, bool bf16) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return fail(STK_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {(cuuint64_t)d, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)d * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[96];
+    std::snprintf(buf, sizeof buf, "cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
+    return fail(STK_ECUDA, buf);
+  }
+  return STK_OK;
+}
+
+int list_len(int64_t k) { return k <= 32 ? 32 : k <= 64 ? 64 : k <= 128 ? 128 : 0; }
+
+bool ref_k(int64_t k) {
+  return k == 1 || k == 2 || k == 4 || k == 8 || k == 16 || k == 32 || k == 64 || k == 128;
+}
+
+// Work decomposition: units = M tiles x feature ranges, sized so the
+// persistent grid (one CTA per SM) gets a whole number of units each.
+stk::UnitGrid make_grid(int64_t B, int64_t F, int sms) {
+  stk::UnitGrid g;
+  g.m_tiles = (int)((B + stk::kRows - 1) / stk::kRows);
+  g.nchunks = (F + 31) / 32;
+  int segs = sms / std::gcd(g.m_tiles, sms);
+  if (segs < 1) segs = 1;
+  if ((int64_t)segs > g.nchunks) segs = (int)g.nchunks;
+  g.segs = segs;
+  g.units = g.m_tiles * segs;
+  return g;
+}
+
+size_t partial_bytes(const stk::UnitGrid& g, int L) { return (size_t)g.units * stk::kRows * L * sizeof(uint64_t); }
+
+struct Plan {
+  bool tc;  // tcgen05 path
+  int L;
+  stk::UnitGrid grid;
+  int ctas;
+  size_t ws;
+};
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t k, int dtype, int flags, Plan* pl) {
+  int sms = 0;
+  int rc = device_sms(&sms);
+  if (rc) return rc;
+  pl->L = list_len(k);
+  pl->tc = (dtype == STK_BF16 || dtype == STK_F16) && (d % 8 == 0) && !(flags & STK_FLAG_SIMT) &&
+           (X == nullptr || aligned16(X)) && (W == nullptr || aligned16(W));
+  pl->grid = make_grid(B, F, sms);
+  pl->ctas = pl->grid.units < sms ? pl->grid.units : sms;
+  pl->ws = partial_bytes(pl->grid, pl->L);
+  return STK_OK;
+}
+
+// Optional override of the fused tile configuration, "L,NT,STAGES", for tuning.
+bool fused_override(int L, int* nt, int* stages) {
+  const char* s = std::getenv("STK_FUSED_CFG");
+  if (!s) return false;
+  int l = 0, n = 0, st = 0;
+  if (std::sscanf(s, "%d,%d,%d", &l, &n, &st) != 3 || l != L) return false;
+  *nt = n;
+  *stages = st;
+  return true;
+}
+
+int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint64_t* partials, int64_t B,
+              int64_t d, int64_t F, int64_t k, int dtype, uint32_t index_offset, cudaStream_t stream) {
+  int nt = pl.L == 128 ? 128 : 256;
+  int stages = pl.L == 32 ? 3 : 2;
+  fused_override(pl.L, &nt, &stages);
+  CUtensorMap tx, tw, tw32;
+  const bool bf16 = dtype == STK_BF16;
+  int rc = make_map(&tx, X, B, d, stk::kRows, bf16);
+  if (!rc) rc = make_map(&tw, W, F, d, nt, bf16);
+  if (!rc) rc = make_map(&tw32, W, F, d, 32, bf16);
+  if (rc) return rc;
+  stk::FusedParams p;
+  p.grid = pl.grid;
+  p.bias = b;
+  p.partials = partials;
+  p.B = B;
+  p.F = F;
+  p.k = (int)k;
+  p.num_kb = (int)((d + 63) / 64);
+  p.ab_format = bf16 ? 1 : 0;
+  p.w_evict_first = pl.grid.m_tiles == 1 ? 1 : 0;
+  p.index_offset = index_offset;
+  cudaError_t e = cudaErrorInvalidValue;
+#define STK_TRY_FUSED(Lc, NTc, Sc) \
+  if (pl.L == Lc && nt == NTc && stages == Sc) e = stk::launch_fused<Lc, NTc, Sc>(tx, tw, tw32, p, pl.ctas, stream);
+  STK_FUSED_CONFIGS(STK_TRY_FUSED)
+#undef STK_TRY_FUSED
+  if (e != cudaSuccess) return cuda_fail(e, "fused_topk_kernel launch");
+  return STK_OK;
+}
+
+int run_simt(const Plan& pl, const void* X, const void* W, const float* b, uint64_t* partials, int64_t B, int64_t d,
+             int64_t F, int64_t k, int dtype, uint32_t index_offset, cudaStream_t stream) {
+  stk::SimtParams p;
+  p.grid = pl.grid;
+  p.bias = b;
+  p.partials = partials;
+  p.B = B;
+  p.F = F;
+  p.d = d;
+  p.k = (int)k;
+  p.index_offset = index_offset;
+  cudaError_t e = cudaErrorInvalidValue;
+#define STK_SIMT_L(Lc)                                                                                     \
+  if (pl.L == Lc) {                                                                                        \
+    if (dtype == STK_F32) e = stk::launch_simt<float, Lc>(X, W, p, pl.ctas, stream);                      \
+    if (dtype == STK_F16) e = stk::launch_simt<__half, Lc>(X, W, p, pl.ctas, stream);                     \
+    if (dtype == STK_BF16) e = stk::launch_simt<__nv_bfloat16, Lc>(X, W, p, pl.ctas, stream);             \
+  }
+  STK_SIMT_L(32)
+  STK_SIMT_L(64)
+  STK_SIMT_L(128)
+#undef STK_SIMT_L
+  if (e != cudaSuccess) return cuda_fail(e, "simt_topk_kernel launch");
+  return STK_OK;
+}
+
+int run_merge(int L, const uint64_t* lists, int nlists, int64_t list_stride, int64_t rows, int64_t k, float* V,
+              int32_t* I, uint64_t* keys_out, cudaStream_t stream) {
+  cudaError_t e = cudaErrorInvalidValue;
+  if (L == 32) e = stk::launch_merge<32>(lists, nlists, list_stride, rows, (int)k, V, I, keys_out, stream);
+  if (L == 64) e = stk::launch_merge<64>(lists, nlists, list_stride, rows, (int)k, V, I, keys_out, stream);
+  if (L == 128) e = stk::launch_merge<128>(lists, nlists, list_stride, rows, (int)k, V, I, keys_out, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "merge_lists_kernel launch");
+  return STK_OK;
+}
+
+int check_common(const char* op, int64_t B, int64_t d, int64_t F, int dtype) {
+  if (dtype != STK_F32 && dtype != STK_F16 && dtype != STK_BF16)
+    return fail(STK_EINVAL, "X dtype must be fp32, fp16, or bf16");
+  if (B < 0 || d < 1 || F < 1) return fail(STK_EINVAL, std::string(op) + ": empty or negative shape");
+  if (F > 0x7fffffffLL) return fail(STK_EINVAL, std::string(op) + ": F must fit int32 indices");
+  return STK_OK;
+}
+
+// Scores + per-unit partial lists, then the merge of the units of each row.
+int encode(const void* X, const void* W, const float* b, float* V, int32_t* I, uint64_t* keys_out, int64_t B,
+           int64_t d, int64_t F, int64_t k, int dtype, int flags, uint32_t index_offset, void* workspace,
+           size_t workspace_bytes, cudaStream_t stream) {
+  Plan pl;
+  int rc = plan(X, W, B, d, F, k, dtype, flags, &pl);
+  if (rc) return rc;
+  if (B == 0) return STK_OK;
+  if (workspace_bytes < pl.ws || (pl.ws && workspace == nullptr))
+    return fail(STK_ENOSPACE, "workspace too small (need " + std::to_string(pl.ws) + " bytes)");
+  uint64_t* partials = static_cast<uint64_t*>(workspace);
+  rc = pl.tc ? run_fused(pl, X, W, b, partials, B, d, F, k, dtype, index_offset, stream)
+             : run_simt(pl, X, W, b, partials, B, d, F, k, dtype, index_offset, stream);
+  if (rc) return rc;
+  return run_merge(pl.L, partials, pl.grid.segs, (int64_t)pl.grid.m_tiles * stk::kRows, B, k, V, I, keys_out,
+                   stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+int stk_version(void) { return 100; }
+
+const char* stk_last_error(void) { return g_err.c_str(); }
+
+int stk_list_len(int64_t k) { return k >= 1 ? list_len(k) : 0; }
+
+int stk_workspace_bytes(int64_t B, int64_t d, int64_t F, int64_t k, int dtype, size_t* bytes) {
+  if (!bytes) return fail(STK_EINVAL, "bytes is NULL");
+  int rc = check_common("stk_workspace_bytes", B, d, F, dtype);
+  if (rc) return rc;
+  if (k < 1 || list_len(k) == 0) return fail(STK_EINVAL, "k out of range");
+  Plan pl;
+  rc = plan(nullptr, nullptr, B, d, F, k, dtype, 0, &pl);
+  if (rc) return rc;
+  *bytes = pl.ws;
+  return STK_OK;
+}
+
+int stk_exact_forward(const void* X, const void* W, const float* b, float* V, int32_t* I, int64_t B, int64_t d,
+                      int64_t F, int64_t k, int dtype, int flags, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  int rc = check_common("streamtopk_cuda_exact", B, d, F, dtype);
+  if (rc) return rc;
+  // streamtopk_exact.cu:812-813,818-830
+  if (!(k >= 1 && k <= F)) return fail(STK_EINVAL, "k out of range");
+  if (d > 4096 && !(flags & STK_FLAG_ANY_D)) return fail(STK_EINVAL, "d exceeds D_MAX=4096");
+  if (!(flags & STK_FLAG_ANY_K) && !ref_k(k))
+    return fail(STK_EINVAL, "streamtopk_cuda_exact: unsupported k=" + std::to_string(k) +
+                                ". Supported: 1,2,4,8,16,32,64,128.");
+  if (k > 128) return fail(STK_EINVAL, "streamtopk_cuda_exact: unsupported k=" + std::to_string(k) + " (k <= 128)");
+  return encode(X, W, b, V, I, nullptr, B, d, F, k, dtype, flags, 0u, workspace, workspace_bytes,
+                static_cast<cudaStream_t>(stream));
+}
+
+int stk_approx_forward(const void* X, const void* W, const float* b, float* V, int32_t* I, int64_t B, int64_t d,
+                       int64_t F, int64_t k, int64_t c, int dtype, int flags, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  int rc = check_common("streamtopk_cuda_approx", B, d, F, dtype);
+  if (rc) return rc;
+  // streamtopk_approx.cu:253,276-284
+  if (!(k >= 1 && k <= c)) return fail(STK_EINVAL, "k must be <= c");
+  if (!(c == 16 || c == 32 || c == 64 || c == 128))
+    return fail(STK_EINVAL,
+                "streamtopk_cuda_approx: unsupported c=" + std::to_string(c) + ". Supported: 16,32,64,128.");
+  return encode(X, W, b, V, I, nullptr, B, d, F, k, dtype, flags | STK_FLAG_ANY_D, 0u, workspace, workspace_bytes,
+                static_cast<cudaStream_t>(stream));
+}
+
+int stk_shard_forward(const void* X, const void* W_shard, const float* b_shard, uint64_t* keys_out, int64_t B,
+                      int64_t d, int64_t F_shard, int64_t k, int64_t index_offset, int dtype, int flags,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_common("stk_shard_forward", B, d, F_shard, dtype);
+  if (rc) return rc;
+  if (k < 1 || k > 128) return fail(STK_EINVAL, "k out of range");
+  if (index_offset < 0 || index_offset + F_shard > 0x7fffffffLL)
+    return fail(STK_EINVAL, "index_offset + F_shard must fit int32 indices");
+  if (!keys_out) return fail(STK_EINVAL, "keys_out is NULL");
+  // V/I of the shard-local merge are not needed; only the sorted keys.
+  const int L = list_len(k);
+  Plan pl;
+  rc = plan(X, W_shard, B, d, F_shard, k, dtype, flags, &pl);
+  if (rc) return rc;
+  if (B == 0) return STK_OK;
+  if (workspace_bytes < pl.ws || (pl.ws && workspace == nullptr))
+    return fail(STK_ENOSPACE, "workspace too small (need " + std::to_string(pl.ws) + " bytes)");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint64_t* partials = static_cast<uint64_t*>(workspace);
+  rc = pl.tc ? run_fused(pl, X, W_shard, b_shard, partials, B, d, F_shard, k, dtype, (uint32_t)index_offset, s)
+             : run_simt(pl, X, W_shard, b_shard, partials, B, d, F_shard, k, dtype, (uint32_t)index_offset, s);
+  if (rc) return rc;
+  return run_merge(L, partials, pl.grid.segs, (int64_t)pl.grid.m_tiles * stk::kRows, B, 0, nullptr, nullptr,
+                   keys_out, s);
+}
+
+int stk_merge_keys(const uint64_t* lists, int64_t nlists, int64_t B, int64_t k, float* V, int32_t* I,
+                   void* stream) {
+  if (k < 1 || k > 128) return fail(STK_EINVAL, "k out of range");
+  if (nlists < 1) return fail(STK_EINVAL, "nlists must be >= 1");
+  if (B < 0) return fail(STK_EINVAL, "B must be >= 0");
+  return run_merge(list_len(k), lists, (int)nlists, B, B, k, V, I, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int stk_approx_candidates(const void* X, const void* W, const float* b, float* cand_vals, int32_t* cand_idxs,
+                          int64_t B, int64_t d, int64_t F, int64_t c, int dtype, void* stream) {
+  (void)X; (void)W; (void)b; (void)cand_vals; (void)cand_idxs; (void)B; (void)d; (void)F; (void)c; (void)dtype;
+  (void)stream;
+  return fail(STK_EINVAL, "stk_approx_candidates: not built yet");
+}
+
+int stk_device_error(void* stream, unsigned* code) {
+  if (!code) return fail(STK_EINVAL, "code is NULL");
+  cudaError_t e = stk::read_and_clear_device_error(code, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "stk_device_error");
+  if (*code) {
+    char buf[96];
+    std::snprintf(buf, sizeof buf, "device error code %u (a bounded wait in a kernel ran out)", *code);
+    g_err = buf;
+    return STK_EDEVICE;
+  }
+  return STK_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,426 @@
+// Device-side building blocks for the B200 streaming top-k SAE encoder.
+//
+//   * 64-bit selection keys: (order-preserving float bits << 32) | ~feature.
+//     Larger key == larger score, and among equal scores the smaller feature
+//     index.  Keys are unique, so every selection below is deterministic and
+//     independent of tile order, CTA count and GPU count.  Key 0 means
+//     "empty" and sorts below every real score.
+//   * Per-thread bitonic networks over register arrays (one thread owns one
+//     batch row), used by the top-k accumulator.
+//   * Warp-cooperative bitonic merge over lists spread across a warp (merge
+//     kernel).
+//   * Thin inline-PTX wrappers for mbarrier, TMA, tcgen05 and TMEM.
+//
+// Semantics kept from the reference (streamtopk_sae/csrc/cuda/topk_buffer.cuh:
+// 9-81, streamtopk_exact.cu:137-148): a score enters the running top-k only
+// if it is strictly greater than the current k-th value; NaN never enters.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace stk {
+
+constexpr int kRows = 128;          // batch rows per M tile (tcgen05 M)
+constexpr int kAppend = 32;         // per-row append slots between merges
+constexpr uint64_t kEmptyKey = 0ull;
+// Upper bound for any single spin-wait on an mbarrier (nanoseconds).  A wait
+// that runs out sets the device error word and makes every role drain out.
+constexpr unsigned long long kWaitLimitNs = 4000000000ull;
+
+// Error codes written to the device error word (first one wins).
+constexpr unsigned kErrWaitTimeout = 1;
+constexpr unsigned kErrTmemAlloc = 2;
+
+__device__ __forceinline__ uint32_t float_order(float v) {
+  uint32_t u = __float_as_uint(v);
+  if ((u << 1) == 0) u = 0;  // -0.0 and +0.0 are the same score
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__device__ __forceinline__ float order_float(uint32_t o) {
+  uint32_t u = (o & 0x80000000u) ? (o & 0x7fffffffu) : ~o;
+  return __uint_as_float(u);
+}
+
+__device__ __forceinline__ uint64_t make_key(float v, uint32_t feature) {
+  return (uint64_t(float_order(v)) << 32) | uint64_t(~feature);
+}
+
+__device__ __forceinline__ float key_value(uint64_t key) {
+  return order_float(uint32_t(key >> 32));
+}
+
+__device__ __forceinline__ int32_t key_index(uint64_t key) {
+  return int32_t(~uint32_t(key));
+}
+
+__device__ __forceinline__ uint64_t kmax(uint64_t a, uint64_t b) { return a > b ? a : b; }
+__device__ __forceinline__ uint64_t kmin(uint64_t a, uint64_t b) { return a > b ? b : a; }
+
+// ---------------------------------------------------------------------------
+// Per-thread networks (N is a compile-time power of two; fully unrolled so the
+// arrays stay in registers).
+// ---------------------------------------------------------------------------
+template <int N>
+__device__ __forceinline__ void sort_desc(uint64_t (&a)[N]) {
+#pragma unroll
+  for (int size = 2; size <= N; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const bool desc = (i & size) == 0;
+          const uint64_t x = a[i], y = a[j];
+          const bool sw = desc ? (x < y) : (x > y);
+          a[i] = sw ? y : x;
+          a[j] = sw ? x : y;
+        }
+      }
+    }
+  }
+}
+
+// Turns a bitonic sequence into a descending one.
+template <int N>
+__device__ __forceinline__ void merge_desc(uint64_t (&a)[N]) {
+#pragma unroll
+  for (int stride = N >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      const int j = i ^ stride;
+      if (j > i) {
+        const uint64_t x = a[i], y = a[j];
+        a[i] = kmax(x, y);
+        a[j] = kmin(x, y);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Per-row top-L accumulator, one thread per batch row.
+//
+// Shared-memory layout (slot-major, row-minor so that the 32 threads of a warp
+// touch 32 consecutive 8-byte words):
+//   top[s * kRows + r], s < L : row r's best L keys, descending (0 = empty)
+//   app[s * kRows + r], s < 32: row r's unsorted survivors since last merge
+// ---------------------------------------------------------------------------
+// Merge row r's n waiting survivors (app, unsorted) into its sorted top list
+// and return the new threshold (value of the (kth+1)-th best key, or -inf).
+template <int L>
+__device__ __noinline__ float merge_survivors(uint64_t* top, const uint64_t* app, int r, int n, int kth) {
+  uint64_t a[32];
+#pragma unroll
+  for (int s = 0; s < 32; ++s) a[s] = (s < n) ? app[s * kRows + r] : kEmptyKey;
+  sort_desc<32>(a);
+  if constexpr (L == 32) {
+    // top-32 of two sorted lists: c[i] = max(top[i], a[31 - i]) is bitonic.
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint64_t lo = a[i], hi = a[31 - i];
+      a[i] = kmax(top[i * kRows + r], hi);
+      a[31 - i] = kmax(top[(31 - i) * kRows + r], lo);
+    }
+    merge_desc<32>(a);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) top[i * kRows + r] = a[i];
+  } else {
+    // Only the last 32 positions can change in c[i] = max(top[i], a'[L-1-i]).
+#pragma unroll
+    for (int q = 0; q < 32; ++q) {
+      uint64_t* p = &top[(L - 32 + q) * kRows + r];
+      *p = kmax(*p, a[31 - q]);
+    }
+    // Bitonic merge: strides >= 32 in shared memory, then 32-blocks in registers.
+#pragma unroll
+    for (int stride = L >> 1; stride >= 32; stride >>= 1) {
+#pragma unroll 8
+      for (int i = 0; i < L; ++i) {
+        if ((i & stride) == 0) {
+          uint64_t* pi = &top[i * kRows + r];
+          uint64_t* pj = &top[(i + stride) * kRows + r];
+          const uint64_t x = *pi, y = *pj;
+          *pi = kmax(x, y);
+          *pj = kmin(x, y);
+        }
+      }
+    }
+#pragma unroll 1
+    for (int blk = 0; blk < L / 32; ++blk) {
+#pragma unroll
+      for (int q = 0; q < 32; ++q) a[q] = top[(blk * 32 + q) * kRows + r];
+      merge_desc<32>(a);
+#pragma unroll
+      for (int q = 0; q < 32; ++q) top[(blk * 32 + q) * kRows + r] = a[q];
+    }
+  }
+  const uint64_t kk = top[kth * kRows + r];
+  return kk ? key_value(kk) : -__int_as_float(0x7f800000);
+}
+
+template <int L>
+struct RowTopK {
+  uint64_t* top;
+  uint64_t* app;
+  int r;        // row within the M tile
+  int cnt;      // survivors waiting in app
+  float thr;    // value of the k-th best key so far (-inf until k are held)
+  int kth;      // k - 1
+
+  __device__ __forceinline__ void init(uint64_t* top_, uint64_t* app_, int row, int k) {
+    top = top_;
+    app = app_;
+    r = row;
+    cnt = 0;
+    thr = -__int_as_float(0x7f800000);
+    kth = k - 1;
+#pragma unroll 4
+    for (int s = 0; s < L; ++s) top[s * kRows + r] = kEmptyKey;
+  }
+
+  __device__ __forceinline__ void flush() {
+    thr = merge_survivors<L>(top, app, r, cnt, kth);
+    cnt = 0;
+  }
+
+  // Offer one chunk of 32 scores (vals[j] is feature f0 + j).  valid_mask
+  // marks real features (tail of F, rows beyond B).  All 32 lanes of the warp
+  // must call this together: a merge runs for every lane as soon as one lane
+  // would overflow its append slots.
+  __device__ __forceinline__ void offer(const float (&vals)[32], uint32_t f0, uint32_t valid_mask) {
+    uint32_t mask = 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) mask |= (vals[j] > thr) ? (1u << j) : 0u;
+    mask &= valid_mask;
+    if (__any_sync(0xffffffffu, cnt + __popc(mask) > kAppend)) {
+      flush();
+      mask = 0;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) mask |= (vals[j] > thr) ? (1u << j) : 0u;
+      mask &= valid_mask;
+    }
+    if (mask) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        if ((mask >> (8 * g)) & 0xffu) {
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            const int j = 8 * g + jj;
+            if (mask & (1u << j)) {
+              app[cnt * kRows + r] = make_key(vals[j], f0 + uint32_t(j));
+              ++cnt;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  __device__ __forceinline__ void finish() {
+    if (__any_sync(0xffffffffu, cnt > 0)) flush();
+  }
+};
+
+// ---------------------------------------------------------------------------
+// Warp-cooperative lists: element i = e * 32 + lane, E = L / 32 per lane.
+// ---------------------------------------------------------------------------
+template <int E>
+__device__ __forceinline__ void warp_merge_desc(uint64_t (&a)[E], int lane) {
+#pragma unroll
+  for (int stride = E * 16; stride > 0; stride >>= 1) {
+    if (stride >= 32) {
+      const int s = stride >> 5;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        if ((e & s) == 0) {
+          const uint64_t x = a[e], y = a[e | s];
+          a[e] = kmax(x, y);
+          a[e | s] = kmin(x, y);
+        }
+      }
+    } else {
+      const bool lower = (lane & stride) == 0;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const uint64_t y = __shfl_xor_sync(0xffffffffu, a[e], stride);
+        a[e] = lower ? kmax(a[e], y) : kmin(a[e], y);
+      }
+    }
+  }
+}
+
+// t <- best L of (t u u), both descending lists of L = 32 * E keys.
+template <int E>
+__device__ __forceinline__ void warp_merge_lists(uint64_t (&t)[E], const uint64_t (&u)[E], int lane) {
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const uint64_t y = __shfl_sync(0xffffffffu, u[E - 1 - e], 31 - lane);
+    t[e] = kmax(t[e], y);
+  }
+  warp_merge_desc<E>(t, lane);
+}
+
+// ---------------------------------------------------------------------------
+// PTX wrappers.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long global_timer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity.  Returns false if the
+// wait ran out, or if abort is given and another role already gave up
+// (*abort != 0).  Drain waits pass abort = nullptr and end on time only.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_try_wait(a, parity)) return true;
+  const unsigned long long t0 = global_timer_ns();
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(a, parity)) return true;
+    if (abort != nullptr && *abort) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const void* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// 2-D tiled TMA load (no multicast) into this CTA's shared memory; completion
+// is signalled as transaction bytes on the mbarrier.
+__device__ __forceinline__ void tma_load_2d(const void* map, uint64_t* bar, void* dst, int x, int y,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Warp-wide TMEM allocation; the base address is written to *dst (shared).
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (bf16 or fp16 in, fp32 accumulate).
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on the mbarrier once all previously issued tcgen05.mma of this thread complete.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns: thread t of the warp gets lane
+// (base lane + t), columns [col, col + 32).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32"
+      " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15,"
+      " %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+        "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
+        "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
+        "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor for a K-major tile written by TMA with
+// 128-byte swizzle: rows of 128 B, 8-row atoms of 1024 B (stride byte offset),
+// version 1 (sm_100), layout type 2 (SWIZZLE_128B).  The tile base must be
+// 1024-byte aligned; advancing K by 16 elements adds 32 B to the start address.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr & 0x3ffffu) >> 4);         // start address
+  d |= uint64_t(1) << 16;                          // leading byte offset (ignored for swizzled K-major)
+  d |= uint64_t(1024 >> 4) << 32;                  // stride byte offset
+  d |= uint64_t(1) << 46;                          // descriptor version
+  d |= uint64_t(2) << 61;                          // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16, fp32 accumulate, A and B K-major.
+// ab_format: 0 = fp16, 1 = bf16.
+__host__ __device__ constexpr uint32_t make_idesc_f16(uint32_t ab_format, uint32_t m, uint32_t n) {
+  return (1u << 4) | (ab_format << 7) | (ab_format << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+}  // namespace stk

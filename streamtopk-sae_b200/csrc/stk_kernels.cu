@@ -1,0 +1,506 @@
+// Kernels of the B200 streaming top-k SAE encoder.
+//
+//   fused_topk_kernel  scores = X @ W^T + b on tcgen05 (TMEM accumulators, TMA
+//                      + mbarrier pipeline), bias add and running per-row top-k
+//                      in the epilogue; the (B, F) score matrix never leaves
+//                      the SM.  Replaces the reference's pass-1 tile kernels
+//                      (streamtopk_sae/csrc/cuda/streamtopk_exact.cu:58-187,
+//                      208-411) and single-pass kernel (:506-638).
+//   simt_topk_kernel   the same contract with fp32 SIMT FMA: fp32 inputs and
+//                      shapes TMA cannot describe (d not a multiple of 8,
+//                      unaligned bases).
+//   merge_lists_kernel per-row top-k of several sorted key lists (CTA partials,
+//                      or the lists all-gathered from other GPUs).  Replaces
+//                      the reference's pass-2 merge (streamtopk_exact.cu:429-499).
+//
+// Work decomposition shared by the two score kernels: the batch is cut into
+// M tiles of 128 rows; F is cut into `segs` contiguous feature ranges whose
+// bounds are multiples of 32.  A unit is (range, M tile); persistent CTAs walk
+// units u = blockIdx.x, blockIdx.x + gridDim.x, ... with
+// range = u / m_tiles, M tile = u % m_tiles, so CTAs running at the same time
+// read the same W rows (L2 reuse across M tiles).  Each unit writes its best
+// L keys per row to partials[u][row][0..L).
+#include "stk_kernels.cuh"
+
+namespace stk {
+
+__device__ unsigned int g_device_error = 0;
+
+__device__ __forceinline__ void raise_device_error(unsigned code) { atomicCAS(&g_device_error, 0u, code); }
+
+__device__ __forceinline__ void unit_range(const UnitGrid& g, int u, int& m, int64_t& f_begin, int64_t& f_end) {
+  const int seg = u / g.m_tiles;
+  m = u - seg * g.m_tiles;
+  const int64_t c0 = (int64_t)seg * g.nchunks / g.segs;
+  const int64_t c1 = (int64_t)(seg + 1) * g.nchunks / g.segs;
+  f_begin = c0 * 32;
+  f_end = c1 * 32;  // may pass F by < 32 on the last range; masked in the epilogue
+}
+
+// Loads the bias for 32 consecutive features starting at f (zero past F).
+__device__ __forceinline__ void load_bias32(const float* __restrict__ bias, int64_t f, int64_t F, bool vec_ok,
+                                            float (&bv)[32]) {
+  if (vec_ok && f + 32 <= F) {
+    const float4* p = reinterpret_cast<const float4*>(bias + f);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 t = __ldg(p + q);
+      bv[4 * q + 0] = t.x;
+      bv[4 * q + 1] = t.y;
+      bv[4 * q + 2] = t.z;
+      bv[4 * q + 3] = t.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) bv[j] = (f + j < F) ? __ldg(bias + f + j) : 0.f;
+  }
+}
+
+__device__ __forceinline__ uint32_t feature_mask(int64_t f, int64_t F) {
+  const int64_t n = F - f;
+  return n >= 32 ? 0xffffffffu : (n <= 0 ? 0u : ((1u << n) - 1u));
+}
+
+// Writes row r's top list (warp-cooperative, coalesced) for the 32 rows of this warp.
+template <int L>
+__device__ __forceinline__ void store_partials(const uint64_t* top, uint64_t* __restrict__ out_unit, int warp_row0,
+                                               int lane) {
+  __syncwarp();
+#pragma unroll 1
+  for (int rr = 0; rr < 32; ++rr) {
+    const int r = warp_row0 + rr;
+#pragma unroll
+    for (int e = 0; e < L / 32; ++e) out_unit[(int64_t)r * L + e * 32 + lane] = top[(e * 32 + lane) * kRows + r];
+  }
+  __syncwarp();
+}
+
+// ---------------------------------------------------------------------------
+// Fused tcgen05 kernel.
+//   warp 0: TMA producer        warp 1: TMEM owner + MMA issuer
+//   warps 2..5: epilogue, warp w reads TMEM lanes 32*(w%4)..+31 (= batch rows)
+// ---------------------------------------------------------------------------
+template <int L, int NT, int STAGES>
+__global__ void __launch_bounds__(kFusedThreads, 1)
+    fused_topk_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                      const __grid_constant__ CUtensorMap tmap_w32, const FusedParams p) {
+  using Cfg = FusedCfg<L, NT, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* top = reinterpret_cast<uint64_t*>(smem + Cfg::kTopOff);
+  uint64_t* app = reinterpret_cast<uint64_t*>(smem + Cfg::kAppOff);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOff);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* acc_full = bars + 2 * STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* mma_done = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], kEpilogueWarps);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmap_x);
+    tma_prefetch_desc(&tmap_w);
+    tma_prefetch_desc(&tmap_w32);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const UnitGrid& g = p.grid;
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol_x = l2_policy_evict_last();
+      const uint64_t pol_w = p.w_evict_first ? l2_policy_evict_first() : l2_policy_evict_normal();
+      uint32_t it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < g.units && ok; u += gridDim.x) {
+        int m;
+        int64_t fb, fe;
+        unit_range(g, u, m, fb, fe);
+        for (int64_t ft = fb; ft < fe && ok; ft += NT) {
+          const int w = (int)min((int64_t)NT, fe - ft);
+          const uint32_t bytes = Cfg::kXBytes + (uint32_t)w * 128u;
+          for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+            const int s = it % STAGES;
+            if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag)) {
+              ok = false;
+              break;
+            }
+            uint8_t* sx = smem + s * Cfg::kStageBytes;
+            uint8_t* sw = sx + Cfg::kXBytes;
+            mbar_arrive_expect_tx(&full[s], bytes);
+            tma_load_2d(&tmap_x, &full[s], sx, kb * 64, m * kRows, pol_x);
+            if (w == NT) {
+              tma_load_2d(&tmap_w, &full[s], sw, kb * 64, (int)ft, pol_w);
+            } else {
+              for (int q = 0; q < w / 32; ++q)
+                tma_load_2d(&tmap_w32, &full[s], sw + q * 32 * 128, kb * 64, (int)ft + 32 * q, pol_w);
+            }
+          }
+        }
+      }
+      if (!ok) {
+        raise_device_error(kErrWaitTimeout);
+        *abort_flag = 1;
+        // Let the copies already issued land before the CTA can exit.
+        const uint32_t n = it < (uint32_t)STAGES ? it : (uint32_t)STAGES;
+        for (uint32_t j = 0; j < n; ++j) {
+          const uint32_t i = it - 1 - j;
+          mbar_wait(&full[i % STAGES], (i / STAGES) & 1, nullptr);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t it = 0, tile = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < g.units && ok; u += gridDim.x) {
+        int m;
+        int64_t fb, fe;
+        unit_range(g, u, m, fb, fe);
+        for (int64_t ft = fb; ft < fe && ok; ft += NT, ++tile) {
+          const int w = (int)min((int64_t)NT, fe - ft);
+          const int a = tile & 1;
+          if (!mbar_wait(&acc_empty[a], ((tile >> 1) & 1) ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + (uint32_t)(a * NT);
+          const uint32_t idesc = make_idesc_f16((uint32_t)p.ab_format, 128u, (uint32_t)w);
+          for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+            const int s = it % STAGES;
+            if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t sx = smem_u32(smem + s * Cfg::kStageBytes);
+            const uint64_t dx = smem_desc_sw128(sx);
+            const uint64_t dw = smem_desc_sw128(sx + Cfg::kXBytes);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              umma_f16(d_tmem, dx + 2 * kk, dw + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+            umma_commit(&empty[s]);
+          }
+          if (ok) umma_commit(&acc_full[a]);
+        }
+      }
+      if (!ok) {
+        raise_device_error(kErrWaitTimeout);
+        *abort_flag = 1;
+      }
+      // Every MMA issued above has completed once this barrier flips.
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, nullptr);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
+    const bool vec_bias = (reinterpret_cast<uintptr_t>(p.bias) & 15) == 0;
+    RowTopK<L> acc;
+    uint32_t tile = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < g.units && ok; u += gridDim.x) {
+      int m;
+      int64_t fb, fe;
+      unit_range(g, u, m, fb, fe);
+      const bool row_ok = (int64_t)m * kRows + r < p.B;
+      acc.init(top, app, r, p.k);
+      for (int64_t ft = fb; ft < fe; ft += NT, ++tile) {
+        const int w = (int)min((int64_t)NT, fe - ft);
+        const int a = tile & 1;
+        // Warp-uniform wait: lane 0 polls, the others follow its verdict.
+        int got = 1;
+        if (lane == 0) got = mbar_wait(&acc_full[a], (tile >> 1) & 1, abort_flag) ? 1 : 0;
+        got = __shfl_sync(0xffffffffu, got, 0);
+        if (!got) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int nchunk = w / 32;
+#pragma unroll 1
+        for (int c = 0; c < nchunk; ++c) {
+          uint32_t v[32];
+          tmem_ld32(t_lane + (uint32_t)(a * NT + c * 32), v);
+          tmem_wait_ld();
+          if (c == nchunk - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[a]);
+          }
+          const int64_t f = ft + c * 32;
+          float bv[32];
+          load_bias32(p.bias, f, p.F, vec_bias, bv);
+          float vals[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) vals[j] = __uint_as_float(v[j]) + bv[j];
+          const uint32_t valid = row_ok ? feature_mask(f, p.F) : 0u;
+          acc.offer(vals, p.index_offset + (uint32_t)f, valid);
+        }
+      }
+      if (!ok) break;
+      acc.finish();
+      store_partials<L>(top, p.partials + (int64_t)u * kRows * L, q * 32, lane);
+    }
+    if (!ok && lane == 0) {
+      raise_device_error(kErrWaitTimeout);
+      *abort_flag = 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// SIMT kernel: 256 threads compute a 128 x 128 score tile with fp32 FMA
+// (8 x 8 per thread), stage it in shared memory, then threads 0..127 (one per
+// batch row) feed it to the same top-k accumulator.
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T, int L>
+__global__ void __launch_bounds__(kSimtThreads, 1) simt_topk_kernel(const T* __restrict__ X, const T* __restrict__ W,
+                                                                    const SimtParams p) {
+  using Cfg = SimtCfg<L>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 15) & ~uintptr_t(15));
+  float* xs = reinterpret_cast<float*>(smem + Cfg::kXsOff);        // [kKc][129] rows
+  float* ws = reinterpret_cast<float*>(smem + Cfg::kWsOff);        // [kKc][129] features
+  float* sc = reinterpret_cast<float*>(smem + Cfg::kScOff);        // [128 rows][129]
+  uint64_t* top = reinterpret_cast<uint64_t*>(smem + Cfg::kTopOff);
+  uint64_t* app = reinterpret_cast<uint64_t*>(smem + Cfg::kAppOff);
+
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int lane = tid & 31;
+  const UnitGrid& g = p.grid;
+  RowTopK<L> acc;
+  const bool vec_bias = (reinterpret_cast<uintptr_t>(p.bias) & 15) == 0;
+
+  for (int u = blockIdx.x; u < g.units; u += gridDim.x) {
+    int m;
+    int64_t fb, fe;
+    unit_range(g, u, m, fb, fe);
+    const int64_t row0 = (int64_t)m * kRows;
+    if (tid < kRows) acc.init(top, app, tid, p.k);
+    for (int64_t ft = fb; ft < fe; ft += Cfg::kNT) {
+      const int w = (int)min((int64_t)Cfg::kNT, fe - ft);
+      float c[8][8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) c[i][j] = 0.f;
+      for (int64_t k0 = 0; k0 < p.d; k0 += Cfg::kKc) {
+        __syncthreads();
+        // Stage X[row0 + i][k0 + kk] -> xs[kk][i], W[ft + n][k0 + kk] -> ws[kk][n].
+        for (int e = tid; e < Cfg::kKc * kRows; e += kSimtThreads) {
+          const int i = e / Cfg::kKc, kk = e % Cfg::kKc;
+          const int64_t row = row0 + i, col = k0 + kk;
+          xs[kk * (kRows + 1) + i] = (row < p.B && col < p.d) ? to_f32(X[row * p.d + col]) : 0.f;
+          const int64_t fr = ft + i;
+          ws[kk * (kRows + 1) + i] = (i < w && fr < p.F && col < p.d) ? to_f32(W[fr * p.d + col]) : 0.f;
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int kk = 0; kk < Cfg::kKc; ++kk) {
+          float xa[8], wb[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) xa[i] = xs[kk * (kRows + 1) + ty + 16 * i];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) wb[j] = ws[kk * (kRows + 1) + tx + 16 * j];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) c[i][j] = fmaf(xa[i], wb[j], c[i][j]);
+        }
+      }
+      __syncthreads();  // the score tile aliases the staging buffers
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) sc[(ty + 16 * i) * (kRows + 1) + tx + 16 * j] = c[i][j];
+      __syncthreads();
+      if (tid < kRows) {
+        const bool row_ok = row0 + tid < p.B;
+        for (int cc = 0; cc < w / 32; ++cc) {
+          const int64_t f = ft + cc * 32;
+          float bv[32];
+          load_bias32(p.bias, f, p.F, vec_bias, bv);
+          float vals[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) vals[j] = sc[tid * (kRows + 1) + cc * 32 + j] + bv[j];
+          const uint32_t valid = row_ok ? feature_mask(f, p.F) : 0u;
+          acc.offer(vals, p.index_offset + (uint32_t)f, valid);
+        }
+      }
+    }
+    if (tid < kRows) {
+      acc.finish();
+      store_partials<L>(top, p.partials + (int64_t)u * kRows * L, tid & ~31, lane);
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Merge kernel: one CTA (8 warps) per row.  List s of row b starts at
+// lists[(s * list_stride + b) * L]; each list holds L keys, descending.
+// ---------------------------------------------------------------------------
+template <int L>
+__global__ void __launch_bounds__(256) merge_lists_kernel(const uint64_t* __restrict__ lists, int nlists,
+                                                           int64_t list_stride, int64_t rows, int k,
+                                                           float* __restrict__ V, int32_t* __restrict__ I,
+                                                           uint64_t* __restrict__ keys_out) {
+  constexpr int E = L / 32;
+  __shared__ uint64_t red[8][L];
+  const int64_t b = blockIdx.x;
+  if (b >= rows) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t acc[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) acc[e] = kEmptyKey;
+  if (warp < nlists) {
+    const uint64_t* p0 = lists + ((int64_t)warp * list_stride + b) * L;
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[e] = p0[e * 32 + lane];
+    uint64_t nxt[E];
+    int s = warp + 8;
+    if (s < nlists) {
+      const uint64_t* p1 = lists + ((int64_t)s * list_stride + b) * L;
+#pragma unroll
+      for (int e = 0; e < E; ++e) nxt[e] = p1[e * 32 + lane];
+    }
+    for (; s < nlists; s += 8) {
+      uint64_t cur[E];
+#pragma unroll
+      for (int e = 0; e < E; ++e) cur[e] = nxt[e];
+      if (s + 8 < nlists) {
+        const uint64_t* p1 = lists + ((int64_t)(s + 8) * list_stride + b) * L;
+#pragma unroll
+        for (int e = 0; e < E; ++e) nxt[e] = p1[e * 32 + lane];
+      }
+      warp_merge_lists<E>(acc, cur, lane);
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) red[warp][e * 32 + lane] = acc[e];
+  __syncthreads();
+  if (warp == 0) {
+    for (int w = 1; w < 8; ++w) {
+      uint64_t cur[E];
+#pragma unroll
+      for (int e = 0; e < E; ++e) cur[e] = red[w][e * 32 + lane];
+      warp_merge_lists<E>(acc, cur, lane);
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const int i = e * 32 + lane;
+      const uint64_t key = acc[e];
+      if (i < k) {
+        V[b * k + i] = key ? key_value(key) : -3.402823466e+38f;
+        I[b * k + i] = key ? key_index(key) : -1;
+      }
+      if (keys_out) keys_out[b * L + i] = key;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Explicit instantiations and launch helpers (host side of this TU).
+// ---------------------------------------------------------------------------
+template <int L, int NT, int STAGES>
+cudaError_t launch_fused(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tw32, const FusedParams& p,
+                         int grid, cudaStream_t stream) {
+  using Cfg = FusedCfg<L, NT, STAGES>;
+  auto kern = fused_topk_kernel<L, NT, STAGES>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, kFusedThreads, Cfg::kSmemBytes, stream>>>(tx, tw, tw32, p);
+  return cudaGetLastError();
+}
+
+template <typename T, int L>
+cudaError_t launch_simt(const void* X, const void* W, const SimtParams& p, int grid, cudaStream_t stream) {
+  using Cfg = SimtCfg<L>;
+  auto kern = simt_topk_kernel<T, L>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, kSimtThreads, Cfg::kSmemBytes, stream>>>(static_cast<const T*>(X), static_cast<const T*>(W), p);
+  return cudaGetLastError();
+}
+
+template <int L>
+cudaError_t launch_merge(const uint64_t* lists, int nlists, int64_t list_stride, int64_t rows, int k, float* V,
+                         int32_t* I, uint64_t* keys_out, cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  merge_lists_kernel<L><<<(unsigned)rows, 256, 0, stream>>>(lists, nlists, list_stride, rows, k, V, I, keys_out);
+  return cudaGetLastError();
+}
+
+#define STK_INST_FUSED(L, NT, S)                                                                                  \
+  template cudaError_t launch_fused<L, NT, S>(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, \
+                                              const FusedParams&, int, cudaStream_t);
+STK_FUSED_CONFIGS(STK_INST_FUSED)
+
+#define STK_INST_SIMT(L)                                                                                         \
+  template cudaError_t launch_simt<float, L>(const void*, const void*, const SimtParams&, int, cudaStream_t);   \
+  template cudaError_t launch_simt<__half, L>(const void*, const void*, const SimtParams&, int, cudaStream_t);  \
+  template cudaError_t launch_simt<__nv_bfloat16, L>(const void*, const void*, const SimtParams&, int,          \
+                                                     cudaStream_t);                                             \
+  template cudaError_t launch_merge<L>(const uint64_t*, int, int64_t, int64_t, int, float*, int32_t*, uint64_t*, \
+                                       cudaStream_t);
+STK_INST_SIMT(32)
+STK_INST_SIMT(64)
+STK_INST_SIMT(128)
+
+cudaError_t read_and_clear_device_error(unsigned* out, cudaStream_t stream) {
+  unsigned zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(out, g_device_error, sizeof(unsigned), 0, cudaMemcpyDeviceToHost, stream);
+  if (e != cudaSuccess) return e;
+  e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return e;
+  if (*out) e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(unsigned));
+  return e;
+}
+
+}  // namespace stk

@@ -1,0 +1,100 @@
+// Shared declarations of the encoder kernels: tile configurations, shared-
+// memory layouts, launch parameters and the launch helpers defined in
+// stk_kernels.cu.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "stk_device.cuh"
+
+namespace stk {
+
+constexpr int kEpilogueWarps = 4;
+constexpr int kFusedThreads = 64 + 32 * kEpilogueWarps;  // producer, MMA, 4 epilogue warps
+constexpr int kSimtThreads = 256;
+
+// Units of work (see stk_kernels.cu header comment).
+struct UnitGrid {
+  int m_tiles;      // ceil(B / 128)
+  int segs;         // feature ranges
+  int units;        // m_tiles * segs
+  int64_t nchunks;  // ceil(F / 32)
+};
+
+struct FusedParams {
+  UnitGrid grid;
+  const float* bias;
+  uint64_t* partials;  // [units][128][L] keys
+  int64_t B, F;
+  int k;
+  int num_kb;          // ceil(d / 64)
+  int ab_format;       // 0 fp16, 1 bf16
+  int w_evict_first;   // W is read once (single M tile): stream it past L2
+  uint32_t index_offset;
+};
+
+struct SimtParams {
+  UnitGrid grid;
+  const float* bias;
+  uint64_t* partials;
+  int64_t B, F, d;
+  int k;
+  uint32_t index_offset;
+};
+
+// Shared-memory plan of the fused kernel: STAGES x (X tile 128x64, W tile
+// NTx64, both K-major 128-byte swizzled), the per-row top lists and append
+// buffers, then the mbarriers.
+template <int L, int NT, int STAGES>
+struct FusedCfg {
+  static constexpr int kXBytes = kRows * 64 * 2;
+  static constexpr int kWBytes = NT * 64 * 2;
+  static constexpr int kStageBytes = kXBytes + kWBytes;
+  static constexpr int kTopOff = STAGES * kStageBytes;
+  static constexpr int kAppOff = kTopOff + L * kRows * 8;
+  static constexpr int kBarOff = kAppOff + kAppend * kRows * 8;
+  static constexpr int kSmemBytes = 1024 + kBarOff + 256;
+  static constexpr int kTmemCols = (2 * NT <= 32) ? 32 : (2 * NT <= 64) ? 64 : (2 * NT <= 128) ? 128 : (2 * NT <= 256) ? 256 : 512;
+  static_assert(NT % 32 == 0 && NT >= 32 && NT <= 256, "tile width");
+  static_assert(kStageBytes % 1024 == 0, "stage alignment");
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+// Shared-memory plan of the SIMT kernel: score tile (aliased by the GEMM
+// staging buffers), top lists, append buffers.
+template <int L>
+struct SimtCfg {
+  static constexpr int kNT = 128;
+  static constexpr int kKc = 32;
+  static constexpr int kXsOff = 0;
+  static constexpr int kWsOff = kKc * (kRows + 1) * 4;
+  static constexpr int kScOff = 0;
+  static constexpr int kScBytes = kRows * (kRows + 1) * 4;
+  static constexpr int kTopOff = (kScBytes + 15) & ~15;
+  static constexpr int kAppOff = kTopOff + L * kRows * 8;
+  static constexpr int kSmemBytes = 16 + kAppOff + kAppend * kRows * 8;
+  static_assert(kWsOff + kKc * (kRows + 1) * 4 <= kScBytes, "staging must fit in the score tile");
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+// (L, NT, STAGES) instantiated for the fused kernel.
+#define STK_FUSED_CONFIGS(X) \
+  X(32, 256, 3)              \
+  X(64, 256, 2)              \
+  X(64, 128, 4)              \
+  X(128, 128, 2)
+
+template <int L, int NT, int STAGES>
+cudaError_t launch_fused(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tw32, const FusedParams& p,
+                         int grid, cudaStream_t stream);
+
+template <typename T, int L>
+cudaError_t launch_simt(const void* X, const void* W, const SimtParams& p, int grid, cudaStream_t stream);
+
+template <int L>
+cudaError_t launch_merge(const uint64_t* lists, int nlists, int64_t list_stride, int64_t rows, int k, float* V,
+                         int32_t* I, uint64_t* keys_out, cudaStream_t stream);
+
+cudaError_t read_and_clear_device_error(unsigned* out, cudaStream_t stream);
+
+}  // namespace stk

@@ -1,0 +1,19 @@
+"""StreamTopK-SAE for B200: streaming fused top-k SAE encoder on sm_100a.
+
+Drop-in for the reference package's op API (streamtopk_sae/__init__.py in
+ayushimehrotra/streamtopk-sae): ``topk_sae_cuda_exact`` and
+``topk_sae_cuda_approx`` compute top_k(X @ W_enc.T + b_enc, k) without
+materialising the (B, F) score matrix, on tcgen05 tensor cores with the top-k
+selection fused into the GEMM epilogue.  ``shard`` adds the multi-GPU
+F-sharded encoder (one process per GPU, NCCL all-gather + merge).
+"""
+from streamtopk_sae.ops import topk_sae_cpu, topk_sae_cuda_approx, topk_sae_cuda_exact
+from streamtopk_sae.utils import make_inputs, recall_at_k
+
+__all__ = [
+    "topk_sae_cpu",
+    "topk_sae_cuda_exact",
+    "topk_sae_cuda_approx",
+    "recall_at_k",
+    "make_inputs",
+]

@@ -1,0 +1,92 @@
+"""ctypes binding of libstk_b200.so (C ABI: include/stk_b200.h).
+
+The library is the only compute path: if it is missing, every op raises.
+There is no CPU or PyTorch fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libstk_b200.so")
+
+STK_OK, STK_EINVAL, STK_ECUDA, STK_EDEVICE, STK_ENOSPACE = 0, 1, 2, 3, 4
+STK_F32, STK_F16, STK_BF16 = 0, 1, 2
+STK_FLAG_ANY_K, STK_FLAG_ANY_D, STK_FLAG_SIMT = 1, 2, 4
+
+EXPORTS = (
+    "stk_version", "stk_last_error", "stk_list_len", "stk_workspace_bytes",
+    "stk_exact_forward", "stk_approx_forward", "stk_approx_candidates",
+    "stk_shard_forward", "stk_merge_keys", "stk_device_error",
+)
+
+_lib = None
+_lock = threading.Lock()
+
+
+class NativeLibraryMissing(RuntimeError):
+    pass
+
+
+def load():
+    """Load and type the library (once)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.isfile(LIB_PATH):
+            raise NativeLibraryMissing(
+                f"streamtopk_sae native library not built ({LIB_PATH} missing). "
+                "Run: make -C streamtopk-sae_b200")
+        L = ctypes.CDLL(LIB_PATH)
+        i64, i32, vp, sz = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t
+        L.stk_version.restype = i32
+        L.stk_version.argtypes = []
+        L.stk_last_error.restype = ctypes.c_char_p
+        L.stk_last_error.argtypes = []
+        L.stk_list_len.restype = i32
+        L.stk_list_len.argtypes = [i64]
+        L.stk_workspace_bytes.restype = i32
+        L.stk_workspace_bytes.argtypes = [i64, i64, i64, i64, i32, ctypes.POINTER(sz)]
+        L.stk_exact_forward.restype = i32
+        L.stk_exact_forward.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, i64, i32, i32, vp, sz, vp]
+        L.stk_approx_forward.restype = i32
+        L.stk_approx_forward.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32, vp, sz, vp]
+        L.stk_approx_candidates.restype = i32
+        L.stk_approx_candidates.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, i64, i32, vp]
+        L.stk_shard_forward.restype = i32
+        L.stk_shard_forward.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32, vp, sz, vp]
+        L.stk_merge_keys.restype = i32
+        L.stk_merge_keys.argtypes = [vp, i64, i64, i64, vp, vp, vp]
+        L.stk_device_error.restype = i32
+        L.stk_device_error.argtypes = [vp, ctypes.POINTER(ctypes.c_uint)]
+        _lib = L
+    return _lib
+
+
+def check(rc: int) -> None:
+    """Raise RuntimeError with the library's message for a non-zero status."""
+    if rc != STK_OK:
+        msg = load().stk_last_error().decode(errors="replace")
+        raise RuntimeError(msg)
+
+
+def workspace_bytes(B: int, d: int, F: int, k: int, dtype_code: int) -> int:
+    out = ctypes.c_size_t(0)
+    check(load().stk_workspace_bytes(B, d, F, k, dtype_code, ctypes.byref(out)))
+    return int(out.value)
+
+
+def list_len(k: int) -> int:
+    return int(load().stk_list_len(k))
+
+
+def device_error(stream_handle: int) -> int:
+    """Synchronise the stream; raise if a kernel reported a device-side error."""
+    code = ctypes.c_uint(0)
+    check(load().stk_device_error(stream_handle, ctypes.byref(code)))
+    return int(code.value)
