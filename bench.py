@@ -1,0 +1,425 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 streaming top-k SAE encoder (driver contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 2|3|4|5]
+
+One step = one exact top-k encode of one batch (B rows) over all F features.
+Default workload (the north-star target):
+exact bf16, B=128, d=2048, F=262144, k=64, X ~ N(0,1), W_enc rows N(0,1)
+scaled to unit L2 norm, b_enc ~ N(0, 0.01) (std 0.1); W_enc is 1 GiB, larger
+than L2, so no L2 flush is needed between steps.  With N > 1 (torchrun, one
+process per GPU, NCCL) W_enc is sharded along F: each rank encodes its shard,
+an NCCL all-gather of the (B, L) key lists and a merge kernel finish the step
+(strong scaling: total work fixed).
+
+Printed on rank 0: one JSON line with the contract's keys, plus
+  roofline      the fused tcgen05 kernel's algorithmic bytes / its CUDA-event
+                time measured over the timed region, against the measured HBM
+                copy bandwidth (MEASURED_PEAKS.json);
+  cpu_baseline  the reference's own CPU op (compiled from its sources into
+                oracle/_ref) on a bounded sample, rank 0 at N=1 only;
+  e2e           the same metric through the public API with pinned host X in
+                and host V/I out every step;
+  clocks        nvidia-smi samples taken during the timed region.
+--impl reference times the reference's CPU implementation (oracle/_ref, all
+host cores through a process pool) on the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "streamtopk-sae_b200"))
+
+METRIC = "SAE encode rows/sec & % of HBM/tensor roofline at B,d,F,k; 1/2/4/8 B200"
+CONFIGS = {
+    2: dict(B=128, d=768, F=65536, k=32, dtype="bf16", w_init="normal_1_over_d", mode="exact"),
+    3: dict(B=128, d=2048, F=262144, k=64, dtype="bf16", w_init="unit_rows", mode="exact"),
+    4: dict(B=128, d=2048, F=1048576, k=32, dtype="bf16", w_init="unit_rows", mode="approx", c=32),
+    5: dict(B=4096, d=4096, F=262144, k=128, dtype="fp16", w_init="normal_1_over_d", mode="exact"),
+}
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def esize(dtype):
+    return 4 if dtype == "fp32" else 2
+
+
+def alg_bytes(B, d, F, k, dtype):
+    """Algorithmic bytes per encode (reference bench/run_bandwidth.py:73-78)."""
+    return B * d * esize(dtype) + F * d * esize(dtype) + 4 * F + 8 * B * k
+
+
+def load_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), float(j.get("bf16_tflops_sustained", j["bf16_tflops"])), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, 1400.0, "fallback"
+
+
+def profiled_traffic(config_id, n_gpus):
+    """DRAM bytes per fused-kernel launch from the committed ncu summary, if any."""
+    p = os.path.join(REPO, "profiles", f"fused_topk_kernel_cfg{config_id}.txt")
+    try:
+        for line in open(p):
+            if line.startswith(f"traffic_bytes_per_launch_n{n_gpus}:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi samples of one GPU while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, local_rank):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        self.gpu = vis.split(",")[local_rank] if vis else str(local_rank)
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+        return False
+
+    def summary(self):
+        rows = [r for r in csv.reader(io.StringIO(self.out)) if len(r) >= 9]
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU reference arm / baseline (the reference's own CPU op from oracle/_ref).
+# ---------------------------------------------------------------------------
+
+def _ref_worker_init():
+    import torch
+    torch.set_num_threads(1)
+    sys.path.insert(0, REPO)
+    from oracle import oracle
+    oracle._ref_mod()
+
+
+def _ref_worker(args):
+    X, W, b, k = args
+    from oracle import oracle
+    oracle.ref_cpu_topk(X, W, b, k)
+    return X.shape[0]
+
+
+def reference_inputs(cfg, f_sample, seed=0):
+    """fp32 CPU inputs with the config's distributions, F cut to f_sample."""
+    import torch
+    g = torch.Generator()
+    g.manual_seed(seed)
+    dt = torch.bfloat16 if cfg["dtype"] == "bf16" else (torch.float16 if cfg["dtype"] == "fp16" else torch.float32)
+    X = torch.randn(cfg["B"], cfg["d"], generator=g).to(dt).float()
+    W = torch.randn(f_sample, cfg["d"], generator=g)
+    if cfg["w_init"] == "unit_rows":
+        W = W / W.norm(dim=1, keepdim=True).clamp_min(1e-8)
+    else:
+        W = W / cfg["d"] ** 0.5
+    W = W.to(dt).float()
+    b = torch.randn(f_sample, generator=g) * 0.1
+    return X.contiguous(), W.contiguous(), b.contiguous()
+
+
+def time_reference_single(cfg, budget_s=10.0):
+    """1-thread reference CPU op on (all rows) x (F sample); rows/s scaled to full F."""
+    sys.path.insert(0, REPO)
+    from oracle import oracle
+    if not oracle.ref_available():
+        return None
+    k = cfg["k"]
+    calib_f = 2048
+    X, W, b = reference_inputs(cfg, calib_f)
+    t0 = time.perf_counter()
+    oracle.ref_cpu_topk(X, W, b, k)
+    per_feature = (time.perf_counter() - t0) / calib_f
+    f_s = int(min(cfg["F"], max(4096, (budget_s / 3) / per_feature)) // 512 * 512)
+    X, W, b = reference_inputs(cfg, f_s)
+    oracle.ref_cpu_topk(X, W, b, k)
+    ts = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        oracle.ref_cpu_topk(X, W, b, k)
+        ts.append(time.perf_counter() - t0)
+    t = statistics.median(ts)
+    rows_s = cfg["B"] / t * (f_s / cfg["F"])
+    return {"value": rows_s, "unit": "rows/s", "cores": 1, "kind": "reference",
+            "sample": f"reference topk_sae_cpu (oracle/_ref, 1 thread as shipped: no OpenMP) on all "
+                      f"{cfg['B']} rows x {f_s} of {cfg['F']} features, fp32 upcast, median of 3; "
+                      f"rows/s scaled by F_sample/F (cost is linear in F); host has {os.cpu_count()} cores"}
+
+
+def run_reference(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    sys.path.insert(0, REPO)
+    from oracle import oracle
+    if not oracle.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built (python oracle/build_ref.py)"}))
+        return 0
+    import torch
+    import torch.multiprocessing as mp
+    procs = max(1, min(os.cpu_count() or 1, cfg["B"]))
+    # Size each step so that warmup + steps take about a minute in total.
+    X, W, b = reference_inputs(cfg, 2048)
+    t0 = time.perf_counter()
+    oracle.ref_cpu_topk(X, W, b, cfg["k"])
+    per_feature_all_rows = (time.perf_counter() - t0) / 2048
+    total_budget = 60.0
+    step_budget = total_budget / max(1, args.steps + args.warmup)
+    f_s = int(step_budget * procs / per_feature_all_rows)
+    f_s = max(512, min(cfg["F"], f_s // 512 * 512))
+    X, W, b = reference_inputs(cfg, f_s)
+    W.share_memory_()
+    X.share_memory_()
+    b.share_memory_()
+    bounds = [cfg["B"] * i // procs for i in range(procs + 1)]
+    work = [(X[bounds[i]:bounds[i + 1]], W, b, cfg["k"]) for i in range(procs) if bounds[i + 1] > bounds[i]]
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(len(work), initializer=_ref_worker_init) as pool:
+        for _ in range(args.warmup):
+            pool.map(_ref_worker, work)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            pool.map(_ref_worker, work)
+        el = time.perf_counter() - t0
+    ms_step = el / args.steps * 1e3
+    value = cfg["B"] / (el / args.steps) * (f_s / cfg["F"])
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": config_dict(args, cfg),
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": len(work), "kind": "reference",
+                         "sample": f"reference topk_sae_cpu (compiled from its sources into oracle/_ref) in "
+                                   f"{len(work)} spawned processes, each on a row shard, all {cfg['B']} rows x "
+                                   f"{f_s} of {cfg['F']} features per step (fp32 upcast); rows/s scaled by "
+                                   f"F_sample/F (cost is linear in F)"},
+        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def config_dict(args, cfg):
+    tag = f"cfg{args.config}" + (" (shape override)" if args.shape else "")
+    d = {"workload": (f"{tag}: {cfg['mode']} {cfg['dtype']} B={cfg['B']} d={cfg['d']} F={cfg['F']} "
+                      f"k={cfg['k']}" + (f" c={cfg['c']}" if cfg["mode"] == "approx" else "") +
+                      (f", W_enc F-sharded over {args.gpus} GPUs" if args.gpus > 1 else "")),
+         "B": cfg["B"], "d": cfg["d"], "F": cfg["F"], "k": cfg["k"], "global_batch": cfg["B"],
+         "parallelism": f"F-shard{args.gpus}" if args.gpus > 1 else "single-gpu",
+         "l2": "inputs larger than L2: each rank streams >= 128 MiB of W_enc per step"}
+    return d
+
+
+# ---------------------------------------------------------------------------
+# B200 arm.
+# ---------------------------------------------------------------------------
+
+def run_b200(args, cfg):
+    import torch
+    import torch.distributed as dist
+    import streamtopk_sae as stk
+    from streamtopk_sae import _capi
+    from streamtopk_sae import shard as stk_shard
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    B, d, F, k = cfg["B"], cfg["d"], cfg["F"], cfg["k"]
+    dtype = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}[cfg["dtype"]]
+    X, W, b = stk.make_inputs(B, d, F, dtype=dtype, seed=0, device=dev, w_init=cfg["w_init"])
+    f0, f1 = stk_shard.shard_bounds(F, world, rank)
+    if world > 1:
+        W = W[f0:f1].clone()
+        b = b[f0:f1].clone()
+        torch.cuda.empty_cache()
+        enc = stk_shard.ShardedEncoder(W, b, F, f0, k, mode=cfg["mode"], c=cfg.get("c"))
+        step = enc.encode
+    elif cfg["mode"] == "approx":
+        step = lambda x: stk.topk_sae_cuda_approx(x, W, b, k, cfg["c"])  # noqa: E731
+    else:
+        step = lambda x: stk.topk_sae_cuda_exact(x, W, b, k)  # noqa: E731
+
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for _ in range(max(args.warmup, 3)):
+        step(X)
+    torch.cuda.synchronize(dev)
+    assert _capi.device_error(stream.cuda_stream) == 0
+
+    # ---------------- timed region (device-resident inputs)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clk:
+        with _capi.KernelTimer(max_launches=args.steps * 4 + 16) as kt:
+            e0.record(stream)
+            for _ in range(args.steps):
+                step(X)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+    barrier()
+    el_ms = e0.elapsed_time(e1)
+    assert _capi.device_error(stream.cuda_stream) == 0
+    t = torch.tensor([el_ms], device=dev, dtype=torch.float64)
+    fused_ms = kt.ms["fused_topk_kernel"] + kt.ms["simt_topk_kernel"]
+    fused_n = kt.launches["fused_topk_kernel"] + kt.launches["simt_topk_kernel"]
+    launches = sum(kt.launches.values())
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    el_ms = float(t.item())
+    value = B * args.steps / (el_ms / 1e3)
+
+    # ---------------- end to end through the public API, host buffers
+    Xh = X.cpu().pin_memory()
+    Vh = torch.empty((B, k), dtype=torch.float32).pin_memory()
+    Ih = torch.empty((B, k), dtype=torch.int32).pin_memory()
+    Xd = torch.empty_like(X)
+    e2e_steps = max(1, min(args.steps, 2000))
+
+    def e2e_step():
+        Xd.copy_(Xh, non_blocking=True)
+        V, I = step(Xd)
+        Vh.copy_(V, non_blocking=True)
+        Ih.copy_(I, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    t2 = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+    e2e_value = B * e2e_steps / (float(t2.item()) / 1e3)
+
+    # ---------------- roofline of the dominant kernel (this rank's shard)
+    hbm, tf, tf_sus, src = load_peaks()
+    Fs = f1 - f0
+    fused_avg_ms = fused_ms / max(fused_n, 1)
+    if cfg["mode"] != "exact" or cfg["B"] <= 256:
+        per_launch = alg_bytes(B, d, Fs, k, cfg["dtype"])
+        achieved = per_launch / (fused_avg_ms / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                "traffic": profiled_traffic(args.config, world),
+                "kernel": "fused_topk_kernel", "kernel_ms": fused_avg_ms,
+                "algorithmic_bytes_per_launch": per_launch,
+                "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else "fallback"}
+    else:
+        flops = 2.0 * B * d * Fs
+        achieved = flops / (fused_avg_ms / 1e3) / 1e12
+        peak = tf_sus
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "traffic": profiled_traffic(args.config, world), "kernel": "fused_topk_kernel",
+                "kernel_ms": fused_avg_ms, "algorithmic_flops_per_launch": flops,
+                "peak_source": f"{src} bf16_tflops_sustained (fp16 assumed equal)"}
+
+    line = None
+    if rank == 0:
+        cpu = time_reference_single(cfg) if world == 1 else None
+        line = {
+            "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": el_ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": cfg["dtype"],
+            "data": "synthetic (seeded Gaussian, BASELINE.json distributions)",
+            "config": config_dict(args, cfg), "roofline": roof, "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": Xh.numel() * Xh.element_size() * world,
+                    "d2h_bytes_per_step": (Vh.numel() * 4 + Ih.numel() * 4) * world,
+                    "path": "streamtopk_sae.topk_sae_cuda_exact" if world == 1 else "streamtopk_sae.shard.ShardedEncoder.encode"},
+            "gpu_launches": launches, "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS))
+    ap.add_argument("--shape", default=None,
+                    help="B,d,F,k override of the config's shape (small cases for ncu captures)")
+    args = ap.parse_args()
+    cfg = dict(CONFIGS[args.config])
+    if args.shape:
+        cfg["B"], cfg["d"], cfg["F"], cfg["k"] = (int(v) for v in args.shape.split(","))
+    if args.impl == "reference":
+        return run_reference(args, cfg)
+    return run_b200(args, cfg)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

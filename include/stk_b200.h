@@ -48,7 +48,8 @@ enum stk_dtype { STK_F32 = 0, STK_F16 = 1, STK_BF16 = 2 };
 enum stk_flags {
   STK_FLAG_ANY_K = 1, /* accept any 1 <= k <= 128, not only {1,2,4,8,16,32,64,128} */
   STK_FLAG_ANY_D = 2, /* lift the reference's d <= 4096 limit */
-  STK_FLAG_SIMT = 4   /* force the fp32 SIMT kernel (testing / comparison) */
+  STK_FLAG_SIMT = 4,    /* force the fp32 SIMT kernel (testing / comparison) */
+  STK_FLAG_NO_PILOT = 8 /* skip the sampled threshold floor (testing / comparison) */
 };
 
 /* Library version (major * 10000 + minor * 100 + patch). */
@@ -127,6 +128,17 @@ STK_API int stk_merge_keys(const uint64_t* lists, int64_t nlists, int64_t B, int
  * current device.  *code = 0 if no kernel reported an error.
  */
 STK_API int stk_device_error(void* stream, unsigned* code);
+
+/*
+ * Profiling hook (no reference counterpart).  stk_profile_begin arms CUDA
+ * events around each kernel launched by the calls that follow (up to
+ * max_launches launches, any thread); stk_profile_end synchronises them and
+ * returns, per kernel kind (0 fused tcgen05 score kernel, 1 SIMT score
+ * kernel, 2 merge kernel, 3 unused), the summed device time in ms and the
+ * number of launches.  No work is skipped or reordered.
+ */
+STK_API int stk_profile_begin(int64_t max_launches);
+STK_API int stk_profile_end(double* ms_by_kind /* [4] */, int64_t* launches_by_kind /* [4] */);
 
 #ifdef __cplusplus
 }

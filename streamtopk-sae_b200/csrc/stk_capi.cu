@@ -5,12 +5,14 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <numeric>
 #include <string>
+#include <vector>
 
 #include "../../include/stk_b200.h"
 #include "stk_kernels.cuh"
@@ -51,6 +53,36 @@ int device_sms(int* sms) {
   *sms = g_dev[dev].sms;
   return STK_OK;
 }
+
+// Optional per-launch CUDA-event timing (stk_profile_begin/end): events are
+// recorded on the launching stream around each kernel, nothing is skipped.
+enum ProfKind { kProfFused = 0, kProfSimt = 1, kProfMerge = 2, kProfKinds = 4 };
+struct ProfState {
+  std::mutex mu;
+  std::atomic<bool> on{false};
+  std::vector<cudaEvent_t> ev;
+  std::vector<int> kind;
+  size_t used = 0;
+};
+ProfState g_prof;
+
+struct ProfScope {
+  cudaStream_t s;
+  cudaEvent_t e1 = nullptr;
+  ProfScope(int kind, cudaStream_t stream) : s(stream) {
+    if (!g_prof.on) return;
+    std::lock_guard<std::mutex> lk(g_prof.mu);
+    if (!g_prof.on || g_prof.used + 2 > g_prof.ev.size()) return;
+    cudaEvent_t e0 = g_prof.ev[g_prof.used];
+    e1 = g_prof.ev[g_prof.used + 1];
+    g_prof.kind[g_prof.used / 2] = kind;
+    g_prof.used += 2;
+    cudaEventRecord(e0, s);
+  }
+  ~ProfScope() {
+    if (e1) cudaEventRecord(e1, s);
+  }
+};
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -116,6 +148,10 @@ struct Plan {
   int L;
   stk::UnitGrid grid;
   int ctas;
+  bool pilot;
+  size_t ws_partials;
+  size_t ws_app;
+  size_t ws_pilot;
   size_t ws;
 };
 
@@ -130,7 +166,16 @@ int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t 
            (X == nullptr || aligned16(X)) && (W == nullptr || aligned16(W));
   pl->grid = make_grid(B, F, sms);
   pl->ctas = pl->grid.units < sms ? pl->grid.units : sms;
-  pl->ws = partial_bytes(pl->grid, pl->L);
+  // partial lists, then one append buffer per CTA, then (optionally) the
+  // pilot histogram, row maxima and arrival counter (256-byte aligned parts)
+  pl->ws_partials = (partial_bytes(pl->grid, pl->L) + 255) & ~size_t(255);
+  pl->ws_app = ((size_t)pl->ctas * stk::kAppendBytesPerCta + 255) & ~size_t(255);
+  // The sample step needs one unit per CTA (all CTAs resident together) and
+  // pays off when each CTA streams several chunks after its sample.
+  pl->pilot = pl->tc && pl->grid.units <= pl->ctas && pl->grid.m_tiles <= 2 &&
+              pl->grid.nchunks >= 4 * (int64_t)pl->grid.segs && !(flags & STK_FLAG_NO_PILOT);
+  pl->ws_pilot = pl->pilot ? (size_t)pl->grid.m_tiles * stk::kRows * (stk::kPilotBins + 1) * 4 + 256 : 0;
+  pl->ws = pl->ws_partials + pl->ws_app + pl->ws_pilot;
   return STK_OK;
 }
 
@@ -145,10 +190,10 @@ bool fused_override(int L, int* nt, int* stages) {
   return true;
 }
 
-int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint64_t* partials, int64_t B,
-              int64_t d, int64_t F, int64_t k, int dtype, uint32_t index_offset, cudaStream_t stream) {
-  int nt = pl.L == 128 ? 128 : 256;
-  int stages = pl.L == 32 ? 3 : 2;
+int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint64_t* partials, uint64_t* app,
+              int64_t B, int64_t d, int64_t F, int64_t k, int dtype, uint32_t index_offset, cudaStream_t stream) {
+  int nt = 256;
+  int stages = pl.L == 32 ? 4 : pl.L == 64 ? 3 : 2;
   fused_override(pl.L, &nt, &stages);
   CUtensorMap tx, tw, tw32;
   const bool bf16 = dtype == STK_BF16;
@@ -160,6 +205,7 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   p.grid = pl.grid;
   p.bias = b;
   p.partials = partials;
+  p.app = app;
   p.B = B;
   p.F = F;
   p.k = (int)k;
@@ -167,7 +213,19 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   p.ab_format = bf16 ? 1 : 0;
   p.w_evict_first = pl.grid.m_tiles == 1 ? 1 : 0;
   p.index_offset = index_offset;
+  p.pilot_hist = nullptr;
+  p.pilot_rowmax = nullptr;
+  p.pilot_count = nullptr;
+  if (pl.pilot) {
+    uint8_t* base = reinterpret_cast<uint8_t*>(partials) + pl.ws_partials + pl.ws_app;
+    p.pilot_hist = reinterpret_cast<uint32_t*>(base);
+    p.pilot_rowmax = p.pilot_hist + (size_t)pl.grid.m_tiles * stk::kRows * stk::kPilotBins;
+    p.pilot_count = p.pilot_rowmax + (size_t)pl.grid.m_tiles * stk::kRows;
+    cudaError_t me = cudaMemsetAsync(base, 0, pl.ws_pilot, stream);
+    if (me != cudaSuccess) return cuda_fail(me, "cudaMemsetAsync(pilot)");
+  }
   cudaError_t e = cudaErrorInvalidValue;
+  ProfScope prof(kProfFused, stream);
 #define STK_TRY_FUSED(Lc, NTc, Sc) \
   if (pl.L == Lc && nt == NTc && stages == Sc) e = stk::launch_fused<Lc, NTc, Sc>(tx, tw, tw32, p, pl.ctas, stream);
   STK_FUSED_CONFIGS(STK_TRY_FUSED)
@@ -176,18 +234,20 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   return STK_OK;
 }
 
-int run_simt(const Plan& pl, const void* X, const void* W, const float* b, uint64_t* partials, int64_t B, int64_t d,
-             int64_t F, int64_t k, int dtype, uint32_t index_offset, cudaStream_t stream) {
+int run_simt(const Plan& pl, const void* X, const void* W, const float* b, uint64_t* partials, uint64_t* app,
+             int64_t B, int64_t d, int64_t F, int64_t k, int dtype, uint32_t index_offset, cudaStream_t stream) {
   stk::SimtParams p;
   p.grid = pl.grid;
   p.bias = b;
   p.partials = partials;
+  p.app = app;
   p.B = B;
   p.F = F;
   p.d = d;
   p.k = (int)k;
   p.index_offset = index_offset;
   cudaError_t e = cudaErrorInvalidValue;
+  ProfScope prof(kProfSimt, stream);
 #define STK_SIMT_L(Lc)                                                                                     \
   if (pl.L == Lc) {                                                                                        \
     if (dtype == STK_F32) e = stk::launch_simt<float, Lc>(X, W, p, pl.ctas, stream);                      \
@@ -205,6 +265,7 @@ int run_simt(const Plan& pl, const void* X, const void* W, const float* b, uint6
 int run_merge(int L, const uint64_t* lists, int nlists, int64_t list_stride, int64_t rows, int64_t k, float* V,
               int32_t* I, uint64_t* keys_out, cudaStream_t stream) {
   cudaError_t e = cudaErrorInvalidValue;
+  ProfScope prof(kProfMerge, stream);
   if (L == 32) e = stk::launch_merge<32>(lists, nlists, list_stride, rows, (int)k, V, I, keys_out, stream);
   if (L == 64) e = stk::launch_merge<64>(lists, nlists, list_stride, rows, (int)k, V, I, keys_out, stream);
   if (L == 128) e = stk::launch_merge<128>(lists, nlists, list_stride, rows, (int)k, V, I, keys_out, stream);
@@ -231,8 +292,9 @@ int encode(const void* X, const void* W, const float* b, float* V, int32_t* I, u
   if (workspace_bytes < pl.ws || (pl.ws && workspace == nullptr))
     return fail(STK_ENOSPACE, "workspace too small (need " + std::to_string(pl.ws) + " bytes)");
   uint64_t* partials = static_cast<uint64_t*>(workspace);
-  rc = pl.tc ? run_fused(pl, X, W, b, partials, B, d, F, k, dtype, index_offset, stream)
-             : run_simt(pl, X, W, b, partials, B, d, F, k, dtype, index_offset, stream);
+  uint64_t* app = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + pl.ws_partials);
+  rc = pl.tc ? run_fused(pl, X, W, b, partials, app, B, d, F, k, dtype, index_offset, stream)
+             : run_simt(pl, X, W, b, partials, app, B, d, F, k, dtype, index_offset, stream);
   if (rc) return rc;
   return run_merge(pl.L, partials, pl.grid.segs, (int64_t)pl.grid.m_tiles * stk::kRows, B, k, V, I, keys_out,
                    stream);
@@ -309,8 +371,9 @@ int stk_shard_forward(const void* X, const void* W_shard, const float* b_shard, 
     return fail(STK_ENOSPACE, "workspace too small (need " + std::to_string(pl.ws) + " bytes)");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint64_t* partials = static_cast<uint64_t*>(workspace);
-  rc = pl.tc ? run_fused(pl, X, W_shard, b_shard, partials, B, d, F_shard, k, dtype, (uint32_t)index_offset, s)
-             : run_simt(pl, X, W_shard, b_shard, partials, B, d, F_shard, k, dtype, (uint32_t)index_offset, s);
+  uint64_t* app = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + pl.ws_partials);
+  rc = pl.tc ? run_fused(pl, X, W_shard, b_shard, partials, app, B, d, F_shard, k, dtype, (uint32_t)index_offset, s)
+             : run_simt(pl, X, W_shard, b_shard, partials, app, B, d, F_shard, k, dtype, (uint32_t)index_offset, s);
   if (rc) return rc;
   return run_merge(L, partials, pl.grid.segs, (int64_t)pl.grid.m_tiles * stk::kRows, B, 0, nullptr, nullptr,
                    keys_out, s);
@@ -329,6 +392,49 @@ int stk_approx_candidates(const void* X, const void* W, const float* b, float* c
   (void)X; (void)W; (void)b; (void)cand_vals; (void)cand_idxs; (void)B; (void)d; (void)F; (void)c; (void)dtype;
   (void)stream;
   return fail(STK_EINVAL, "stk_approx_candidates: not built yet");
+}
+
+int stk_profile_begin(int64_t max_launches) {
+  if (max_launches < 1) return fail(STK_EINVAL, "max_launches must be >= 1");
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  for (cudaEvent_t e : g_prof.ev) cudaEventDestroy(e);
+  g_prof.ev.assign((size_t)max_launches * 2, nullptr);
+  g_prof.kind.assign((size_t)max_launches, 0);
+  for (auto& e : g_prof.ev) {
+    cudaError_t r = cudaEventCreate(&e);
+    if (r != cudaSuccess) return cuda_fail(r, "cudaEventCreate");
+  }
+  g_prof.used = 0;
+  g_prof.on = true;
+  return STK_OK;
+}
+
+int stk_profile_end(double* ms_by_kind, int64_t* launches_by_kind) {
+  if (!ms_by_kind || !launches_by_kind) return fail(STK_EINVAL, "null output");
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  for (int i = 0; i < kProfKinds; ++i) {
+    ms_by_kind[i] = 0.0;
+    launches_by_kind[i] = 0;
+  }
+  int rc = STK_OK;
+  for (size_t j = 0; j < g_prof.used; j += 2) {
+    cudaError_t r = cudaEventSynchronize(g_prof.ev[j + 1]);
+    float ms = 0.f;
+    if (r == cudaSuccess) r = cudaEventElapsedTime(&ms, g_prof.ev[j], g_prof.ev[j + 1]);
+    if (r != cudaSuccess) {
+      rc = cuda_fail(r, "stk_profile_end");
+      break;
+    }
+    const int k = g_prof.kind[j / 2];
+    ms_by_kind[k] += ms;
+    launches_by_kind[k] += 1;
+  }
+  for (cudaEvent_t e : g_prof.ev) cudaEventDestroy(e);
+  g_prof.ev.clear();
+  g_prof.kind.clear();
+  g_prof.used = 0;
+  g_prof.on = false;
+  return rc;
 }
 
 int stk_device_error(void* stream, unsigned* code) {

@@ -103,86 +103,100 @@ __device__ __forceinline__ void merge_desc(uint64_t (&a)[N]) {
 // ---------------------------------------------------------------------------
 // Per-row top-L accumulator, one thread per batch row.
 //
-// Shared-memory layout (slot-major, row-minor so that the 32 threads of a warp
-// touch 32 consecutive 8-byte words):
-//   top[s * kRows + r], s < L : row r's best L keys, descending (0 = empty)
-//   app[s * kRows + r], s < 32: row r's unsorted survivors since last merge
+// Layout (slot-major, row-minor, so the 32 threads of a warp touch 32
+// consecutive 8-byte words):
+//   top[s * kRows + r], s < L : row r's best L keys, descending (0 = empty);
+//                               shared memory, addressed by its 32-bit
+//                               shared-window offset
+//   app[s * kRows + r], s < 32: row r's unsorted survivors since the last
+//                               merge; global memory (L2-resident workspace
+//                               slice of this CTA), written and read back by
+//                               the same thread only
 // ---------------------------------------------------------------------------
+// Dynamic shared memory of every kernel in this library.  Per-row lists are
+// addressed by byte offset from this symbol so that code outside the kernel
+// body still compiles to shared-memory instructions.
+extern __shared__ __align__(16) uint8_t stk_smem[];
+
+__device__ __forceinline__ uint64_t* smem_keys(uint32_t off) { return reinterpret_cast<uint64_t*>(stk_smem + off); }
+
 // Merge row r's n waiting survivors (app, unsorted) into its sorted top list
-// and return the new threshold (value of the (kth+1)-th best key, or -inf).
+// and return the new threshold: the value of the (kth+1)-th best key, never
+// below floor_thr (a lower bound known from elsewhere, -inf if none).
+// Kept out of line: it runs rarely and is large.
 template <int L>
-__device__ __noinline__ float merge_survivors(uint64_t* top, const uint64_t* app, int r, int n, int kth) {
+__device__ __noinline__ float merge_survivors(uint32_t top_off, const uint64_t* __restrict__ app, int r, int n,
+                                              int kth, float floor_thr) {
+  uint64_t* top = smem_keys(top_off) + r;  // top[s * kRows] is slot s of row r
   uint64_t a[32];
 #pragma unroll
-  for (int s = 0; s < 32; ++s) a[s] = (s < n) ? app[s * kRows + r] : kEmptyKey;
+  for (int s = 0; s < 32; ++s)
+    a[s] = (s < n) ? (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(app + s * kRows + r)) : kEmptyKey;
   sort_desc<32>(a);
   if constexpr (L == 32) {
     // top-32 of two sorted lists: c[i] = max(top[i], a[31 - i]) is bitonic.
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const uint64_t lo = a[i], hi = a[31 - i];
-      a[i] = kmax(top[i * kRows + r], hi);
-      a[31 - i] = kmax(top[(31 - i) * kRows + r], lo);
+      a[i] = kmax(top[i * kRows], hi);
+      a[31 - i] = kmax(top[(31 - i) * kRows], lo);
     }
     merge_desc<32>(a);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) top[i * kRows + r] = a[i];
+    for (int i = 0; i < 32; ++i) top[i * kRows] = a[i];
   } else {
     // Only the last 32 positions can change in c[i] = max(top[i], a'[L-1-i]).
 #pragma unroll
-    for (int q = 0; q < 32; ++q) {
-      uint64_t* p = &top[(L - 32 + q) * kRows + r];
-      *p = kmax(*p, a[31 - q]);
-    }
+    for (int q = 0; q < 32; ++q) top[(L - 32 + q) * kRows] = kmax(top[(L - 32 + q) * kRows], a[31 - q]);
     // Bitonic merge: strides >= 32 in shared memory, then 32-blocks in registers.
 #pragma unroll
     for (int stride = L >> 1; stride >= 32; stride >>= 1) {
-#pragma unroll 8
+#pragma unroll 16
       for (int i = 0; i < L; ++i) {
         if ((i & stride) == 0) {
-          uint64_t* pi = &top[i * kRows + r];
-          uint64_t* pj = &top[(i + stride) * kRows + r];
-          const uint64_t x = *pi, y = *pj;
-          *pi = kmax(x, y);
-          *pj = kmin(x, y);
+          const uint64_t x = top[i * kRows], y = top[(i + stride) * kRows];
+          top[i * kRows] = kmax(x, y);
+          top[(i + stride) * kRows] = kmin(x, y);
         }
       }
     }
 #pragma unroll 1
     for (int blk = 0; blk < L / 32; ++blk) {
 #pragma unroll
-      for (int q = 0; q < 32; ++q) a[q] = top[(blk * 32 + q) * kRows + r];
+      for (int q = 0; q < 32; ++q) a[q] = top[(blk * 32 + q) * kRows];
       merge_desc<32>(a);
 #pragma unroll
-      for (int q = 0; q < 32; ++q) top[(blk * 32 + q) * kRows + r] = a[q];
+      for (int q = 0; q < 32; ++q) top[(blk * 32 + q) * kRows] = a[q];
     }
   }
-  const uint64_t kk = top[kth * kRows + r];
-  return kk ? key_value(kk) : -__int_as_float(0x7f800000);
+  const uint64_t kk = top[kth * kRows];
+  return kk ? fmaxf(key_value(kk), floor_thr) : floor_thr;
 }
 
 template <int L>
 struct RowTopK {
-  uint64_t* top;
-  uint64_t* app;
-  int r;        // row within the M tile
-  int cnt;      // survivors waiting in app
-  float thr;    // value of the k-th best key so far (-inf until k are held)
-  int kth;      // k - 1
+  uint32_t top;   // byte offset of top[0] from stk_smem
+  uint64_t* app;  // global
+  int r;          // row within the M tile
+  int cnt;        // survivors waiting in app
+  float thr;      // value of the k-th best key so far (-inf until k are held)
+  float floor_thr;  // known lower bound of the row's k-th score (-inf if none)
+  int kth;        // k - 1
 
-  __device__ __forceinline__ void init(uint64_t* top_, uint64_t* app_, int row, int k) {
+  __device__ __forceinline__ void init(uint32_t top_, uint64_t* app_, int row, int k) {
     top = top_;
     app = app_;
     r = row;
     cnt = 0;
     thr = -__int_as_float(0x7f800000);
+    floor_thr = thr;
     kth = k - 1;
 #pragma unroll 4
-    for (int s = 0; s < L; ++s) top[s * kRows + r] = kEmptyKey;
+    for (int s = 0; s < L; ++s) smem_keys(top)[s * kRows + r] = kEmptyKey;
   }
 
   __device__ __forceinline__ void flush() {
-    thr = merge_survivors<L>(top, app, r, cnt, kth);
+    thr = merge_survivors<L>(top, app, r, cnt, kth, floor_thr);
     cnt = 0;
   }
 
@@ -210,13 +224,22 @@ struct RowTopK {
           for (int jj = 0; jj < 8; ++jj) {
             const int j = 8 * g + jj;
             if (mask & (1u << j)) {
-              app[cnt * kRows + r] = make_key(vals[j], f0 + uint32_t(j));
+              __stcg(reinterpret_cast<unsigned long long*>(app + cnt * kRows + r),
+                     (unsigned long long)make_key(vals[j], f0 + uint32_t(j)));
               ++cnt;
             }
           }
         }
       }
     }
+  }
+
+  // Raise the filter to a lower bound of the row's k-th score obtained from a
+  // sample (scores strictly below `lb` can never be in the row's top-k).
+  __device__ __forceinline__ void set_floor(float lb) {
+    const float t = nextafterf(lb, -__int_as_float(0x7f800000));  // keep scores == lb
+    floor_thr = fmaxf(floor_thr, t);
+    thr = fmaxf(thr, floor_thr);
   }
 
   __device__ __forceinline__ void finish() {
@@ -294,14 +317,18 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// One try_wait that may suspend the thread for up to kSuspendNs (the thread
+// is woken early when the phase completes), so waiting warps do not spin and
+// steal issue slots from the epilogue warps sharing their scheduler.
+constexpr uint32_t kSuspendNs = 200000;
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}\n"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(kSuspendNs)
       : "memory");
   return ok != 0;
 }
@@ -314,9 +341,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   if (mbar_try_wait(a, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   for (;;) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(a, parity)) return true;
+    if (mbar_try_wait(a, parity)) return true;
     if (abort != nullptr && *abort) return false;
     if (global_timer_ns() - t0 > kWaitLimitNs) return false;
   }
@@ -402,6 +427,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Wait for outstanding TMEM loads and tie the destination registers of the
+// last load to the wait, so no use of them is scheduled before it.
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+        "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15]),
+        "+r"(v[16]), "+r"(v[17]), "+r"(v[18]), "+r"(v[19]), "+r"(v[20]), "+r"(v[21]), "+r"(v[22]), "+r"(v[23]),
+        "+r"(v[24]), "+r"(v[25]), "+r"(v[26]), "+r"(v[27]), "+r"(v[28]), "+r"(v[29]), "+r"(v[30]), "+r"(v[31])
+      :
+      : "memory");
+}
 
 // Shared-memory matrix descriptor for a K-major tile written by TMA with
 // 128-byte swizzle: rows of 128 B, 8-row atoms of 1024 B (stride byte offset),

@@ -61,18 +61,105 @@ __device__ __forceinline__ uint32_t feature_mask(int64_t f, int64_t F) {
   return n >= 32 ? 0xffffffffu : (n <= 0 ? 0u : ((1u << n) - 1u));
 }
 
-// Writes row r's top list (warp-cooperative, coalesced) for the 32 rows of this warp.
+// Writes the top lists of the 32 rows of this warp (warp-cooperative, coalesced).
 template <int L>
-__device__ __forceinline__ void store_partials(const uint64_t* top, uint64_t* __restrict__ out_unit, int warp_row0,
+__device__ __forceinline__ void store_partials(uint32_t top, uint64_t* __restrict__ out_unit, int warp_row0,
                                                int lane) {
   __syncwarp();
 #pragma unroll 1
   for (int rr = 0; rr < 32; ++rr) {
     const int r = warp_row0 + rr;
 #pragma unroll
-    for (int e = 0; e < L / 32; ++e) out_unit[(int64_t)r * L + e * 32 + lane] = top[(e * 32 + lane) * kRows + r];
+    for (int e = 0; e < L / 32; ++e)
+      out_unit[(int64_t)r * L + e * 32 + lane] = smem_keys(top)[(e * 32 + lane) * kRows + r];
   }
   __syncwarp();
+}
+
+// Walks the tiles of this CTA: units u = blockIdx.x, +gridDim.x, ...; tiles
+// of NT features within each unit's range.
+template <int NT>
+struct TileWalk {
+  int u, m;
+  int64_t fb, fe, ft;
+  __device__ __forceinline__ void start(const UnitGrid& g) {
+    u = blockIdx.x;
+    if (u < g.units) {
+      unit_range(g, u, m, fb, fe);
+      ft = fb;
+    }
+  }
+  __device__ __forceinline__ bool valid(const UnitGrid& g) const { return u < g.units; }
+  __device__ __forceinline__ bool first_of_unit() const { return ft == fb; }
+  __device__ __forceinline__ bool last_of_unit() const { return ft + NT >= fe; }
+  __device__ __forceinline__ int width() const { return (int)min((int64_t)NT, fe - ft); }
+  __device__ __forceinline__ void next(const UnitGrid& g) {
+    ft += NT;
+    if (ft >= fe) {
+      u += gridDim.x;
+      if (u < g.units) {
+        unit_range(g, u, m, fb, fe);
+        ft = fb;
+      }
+    }
+  }
+};
+
+__device__ __forceinline__ void epilogue_bar() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kEpilogueWarps * 32) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Lower bound of a row's k-th largest sampled score from its histogram:
+// the lower edge of the highest bin at which the count from the top reaches
+// k.  Returns false when fewer than k samples lie within 256 bins of the top.
+__device__ __forceinline__ bool pilot_bound(const uint32_t* __restrict__ hist, uint32_t top_bin, int k, float& lb) {
+  uint32_t total = 0;
+#pragma unroll 1
+  for (int round = 0; round < 8; ++round) {
+    uint32_t c[32];
+#pragma unroll
+    for (int q = 0; q < 32; ++q) {
+      const int bin = (int)top_bin - 32 * round - q;
+      c[q] = bin >= 0 ? __ldcg(hist + bin) : 0u;
+    }
+#pragma unroll
+    for (int q = 0; q < 32; ++q) {
+      total += c[q];
+      if (total >= (uint32_t)k) {
+        const uint32_t bin = top_bin - 32 * round - q;
+        lb = order_float(bin << (32 - kPilotBits));
+        return true;
+      }
+    }
+    if ((int)top_bin - 32 * round - 31 <= 0) break;
+  }
+  return false;
+}
+
+// b[i] for a runtime i < N without dynamic register indexing.
+template <int N>
+__device__ __forceinline__ float pick(const float (&b)[N], int i) {
+  float v = b[0];
+#pragma unroll
+  for (int c = 1; c < N; ++c) v = (i == c) ? b[c] : v;
+  return v;
+}
+
+// Bias of one tile: lane l holds bias[ft + 32 c + l] for chunk c (0 past F).
+template <int NT>
+__device__ __forceinline__ void load_bias_tile(const float* __restrict__ bias, int64_t ft, int w, int64_t F, int lane,
+                                               float (&b)[NT / 32]) {
+#pragma unroll
+  for (int c = 0; c < NT / 32; ++c) {
+    const int64_t f = ft + 32 * c + lane;
+    b[c] = (32 * c < w && f < F) ? __ldg(bias + f) : 0.f;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -85,10 +172,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     fused_topk_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                       const __grid_constant__ CUtensorMap tmap_w32, const FusedParams p) {
   using Cfg = FusedCfg<L, NT, STAGES>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = stk_smem + ((1024u - (smem_u32(stk_smem) & 1023u)) & 1023u);
   uint64_t* top = reinterpret_cast<uint64_t*>(smem + Cfg::kTopOff);
-  uint64_t* app = reinterpret_cast<uint64_t*>(smem + Cfg::kAppOff);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOff);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
@@ -97,9 +182,13 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   uint64_t* mma_done = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* pilot_flag = abort_flag + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // The merge kernel that follows waits for this grid's completion itself
+  // (griddepcontrol.wait), so it may be scheduled right away.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -223,52 +312,102 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     const int q = warp & 3;
     const int r = q * 32 + lane;
     const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
-    const bool vec_bias = (reinterpret_cast<uintptr_t>(p.bias) & 15) == 0;
+    const uint32_t top_s = (uint32_t)(reinterpret_cast<uint8_t*>(top) - stk_smem);
+    uint64_t* app_cta = p.app + (size_t)blockIdx.x * (kAppend * kRows);
     RowTopK<L> acc;
     uint32_t tile = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < g.units && ok; u += gridDim.x) {
-      int m;
-      int64_t fb, fe;
-      unit_range(g, u, m, fb, fe);
-      const bool row_ok = (int64_t)m * kRows + r < p.B;
-      acc.init(top, app, r, p.k);
-      for (int64_t ft = fb; ft < fe; ft += NT, ++tile) {
-        const int w = (int)min((int64_t)NT, fe - ft);
-        const int a = tile & 1;
-        // Warp-uniform wait: lane 0 polls, the others follow its verdict.
-        int got = 1;
-        if (lane == 0) got = mbar_wait(&acc_full[a], (tile >> 1) & 1, abort_flag) ? 1 : 0;
-        got = __shfl_sync(0xffffffffu, got, 0);
-        if (!got) {
-          ok = false;
-          break;
+    TileWalk<NT> cur;
+    cur.start(g);
+    float bcur[NT / 32], bnext[NT / 32];
+    if (cur.valid(g)) load_bias_tile<NT>(p.bias, cur.ft, cur.width(), p.F, lane, bcur);
+    while (cur.valid(g)) {
+      TileWalk<NT> nxt = cur;
+      nxt.next(g);
+      if (nxt.valid(g)) load_bias_tile<NT>(p.bias, nxt.ft, nxt.width(), p.F, lane, bnext);
+      if (cur.first_of_unit()) acc.init(top_s, app_cta, r, p.k);
+      const bool row_ok = (int64_t)cur.m * kRows + r < p.B;
+      const int w = cur.width();
+      const int a = tile & 1;
+      // Warp-uniform wait: lane 0 polls, the others follow its verdict.
+      int got = 1;
+      if (lane == 0) got = mbar_wait(&acc_full[a], (tile >> 1) & 1, abort_flag) ? 1 : 0;
+      got = __shfl_sync(0xffffffffu, got, 0);
+      if (!got) {
+        if (p.pilot_hist != nullptr && cur.first_of_unit()) {
+          // Match the two epilogue barriers of the sample step so the other
+          // epilogue warps cannot wait on this one forever.
+          epilogue_bar();
+          if (warp == 2 && lane == 0) *pilot_flag = 0;
+          epilogue_bar();
         }
-        tc_fence_after();
-        const int nchunk = w / 32;
-#pragma unroll 1
-        for (int c = 0; c < nchunk; ++c) {
-          uint32_t v[32];
-          tmem_ld32(t_lane + (uint32_t)(a * NT + c * 32), v);
-          tmem_wait_ld();
-          if (c == nchunk - 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[a]);
-          }
-          const int64_t f = ft + c * 32;
-          float bv[32];
-          load_bias32(p.bias, f, p.F, vec_bias, bv);
-          float vals[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) vals[j] = __uint_as_float(v[j]) + bv[j];
-          const uint32_t valid = row_ok ? feature_mask(f, p.F) : 0u;
-          acc.offer(vals, p.index_offset + (uint32_t)f, valid);
-        }
+        ok = false;
+        break;
       }
-      if (!ok) break;
-      acc.finish();
-      store_partials<L>(top, p.partials + (int64_t)u * kRows * L, q * 32, lane);
+      tc_fence_after();
+      const int nchunk = w / 32;
+      const uint32_t tcol = t_lane + (uint32_t)(a * NT);
+#pragma unroll 1
+      for (int c = 0; c < nchunk; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tcol + (uint32_t)(c * 32), v);
+        tmem_wait_ld(v);
+        if (c == nchunk - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[a]);
+        }
+        const int64_t f = cur.ft + 32 * c;
+        const float bl = pick<NT / 32>(bcur, c);
+        float vals[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) vals[j] = __uint_as_float(v[j]) + __shfl_sync(0xffffffffu, bl, j);
+        const uint32_t valid = row_ok ? feature_mask(f, p.F) : 0u;
+        if (p.pilot_hist != nullptr && c == 0 && cur.first_of_unit()) {
+          // Sample: histogram this chunk, meet the other CTAs, read back a floor.
+          uint32_t* h = p.pilot_hist + ((size_t)cur.m * kRows + r) * kPilotBins;
+          uint32_t bmax = 0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (valid & (1u << j)) {
+              const uint32_t bin = float_order(vals[j]) >> (32 - kPilotBits);
+              atomicAdd(h + bin, 1u);
+              bmax = max(bmax, bin);
+            }
+          }
+          if (valid) atomicMax(p.pilot_rowmax + (size_t)cur.m * kRows + r, bmax);
+          __threadfence();
+          epilogue_bar();
+          if (warp == 2 && lane == 0) {
+            atomicAdd(p.pilot_count, 1u);
+            const unsigned long long t0 = global_timer_ns();
+            int ok_all = 1;
+            while (ld_acquire_u32(p.pilot_count) < gridDim.x) {
+              if (global_timer_ns() - t0 > kPilotWaitNs) {
+                ok_all = 0;
+                break;
+              }
+              __nanosleep(256);
+            }
+            *pilot_flag = ok_all;
+          }
+          epilogue_bar();
+          if (*pilot_flag && row_ok) {
+            const uint32_t tb = __ldcg(p.pilot_rowmax + (size_t)cur.m * kRows + r);
+            float lb;
+            if (pilot_bound(h, tb, p.k, lb)) acc.set_floor(lb);
+          }
+        }
+        acc.offer(vals, p.index_offset + (uint32_t)f, valid);
+      }
+      if (cur.last_of_unit()) {
+        acc.finish();
+        store_partials<L>(top_s, p.partials + (int64_t)cur.u * kRows * L, q * 32, lane);
+      }
+#pragma unroll
+      for (int c = 0; c < NT / 32; ++c) bcur[c] = bnext[c];
+      cur = nxt;
+      ++tile;
     }
     if (!ok && lane == 0) {
       raise_device_error(kErrWaitTimeout);
@@ -302,13 +441,12 @@ template <typename T, int L>
 __global__ void __launch_bounds__(kSimtThreads, 1) simt_topk_kernel(const T* __restrict__ X, const T* __restrict__ W,
                                                                     const SimtParams p) {
   using Cfg = SimtCfg<L>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 15) & ~uintptr_t(15));
+  uint8_t* smem = stk_smem;
   float* xs = reinterpret_cast<float*>(smem + Cfg::kXsOff);        // [kKc][129] rows
   float* ws = reinterpret_cast<float*>(smem + Cfg::kWsOff);        // [kKc][129] features
   float* sc = reinterpret_cast<float*>(smem + Cfg::kScOff);        // [128 rows][129]
-  uint64_t* top = reinterpret_cast<uint64_t*>(smem + Cfg::kTopOff);
-  uint64_t* app = reinterpret_cast<uint64_t*>(smem + Cfg::kAppOff);
+  const uint32_t top_s = (uint32_t)Cfg::kTopOff;
+  uint64_t* app_cta = p.app + (size_t)blockIdx.x * (kAppend * kRows);
 
   const int tid = threadIdx.x;
   const int tx = tid & 15, ty = tid >> 4;
@@ -322,7 +460,7 @@ __global__ void __launch_bounds__(kSimtThreads, 1) simt_topk_kernel(const T* __r
     int64_t fb, fe;
     unit_range(g, u, m, fb, fe);
     const int64_t row0 = (int64_t)m * kRows;
-    if (tid < kRows) acc.init(top, app, tid, p.k);
+    if (tid < kRows) acc.init(top_s, app_cta, tid, p.k);
     for (int64_t ft = fb; ft < fe; ft += Cfg::kNT) {
       const int w = (int)min((int64_t)Cfg::kNT, fe - ft);
       float c[8][8];
@@ -376,23 +514,30 @@ __global__ void __launch_bounds__(kSimtThreads, 1) simt_topk_kernel(const T* __r
     }
     if (tid < kRows) {
       acc.finish();
-      store_partials<L>(top, p.partials + (int64_t)u * kRows * L, tid & ~31, lane);
+      store_partials<L>(top_s, p.partials + (int64_t)u * kRows * L, tid & ~31, lane);
     }
     __syncthreads();
   }
 }
 
 // ---------------------------------------------------------------------------
-// Merge kernel: one CTA (8 warps) per row.  List s of row b starts at
+// Merge kernel: one CTA (16 warps) per row.  List s of row b starts at
 // lists[(s * list_stride + b) * L]; each list holds L keys, descending.
+// Warp w folds lists w, w+16, ... (next list prefetched), then a 4-level tree
+// in shared memory folds the 16 warp results.  Launched with programmatic
+// dependent launch after the score kernel: griddepcontrol.wait blocks until
+// that grid has completed and its writes are visible (a no-op otherwise).
 // ---------------------------------------------------------------------------
+constexpr int kMergeWarps = 16;
+
 template <int L>
-__global__ void __launch_bounds__(256) merge_lists_kernel(const uint64_t* __restrict__ lists, int nlists,
-                                                           int64_t list_stride, int64_t rows, int k,
-                                                           float* __restrict__ V, int32_t* __restrict__ I,
-                                                           uint64_t* __restrict__ keys_out) {
+__global__ void __launch_bounds__(kMergeWarps * 32) merge_lists_kernel(const uint64_t* __restrict__ lists, int nlists,
+                                                                        int64_t list_stride, int64_t rows, int k,
+                                                                        float* __restrict__ V, int32_t* __restrict__ I,
+                                                                        uint64_t* __restrict__ keys_out) {
   constexpr int E = L / 32;
-  __shared__ uint64_t red[8][L];
+  __shared__ uint64_t red[kMergeWarps][L];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int64_t b = blockIdx.x;
   if (b >= rows) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -402,22 +547,22 @@ __global__ void __launch_bounds__(256) merge_lists_kernel(const uint64_t* __rest
   if (warp < nlists) {
     const uint64_t* p0 = lists + ((int64_t)warp * list_stride + b) * L;
 #pragma unroll
-    for (int e = 0; e < E; ++e) acc[e] = p0[e * 32 + lane];
+    for (int e = 0; e < E; ++e) acc[e] = __ldcg(reinterpret_cast<const unsigned long long*>(p0 + e * 32 + lane));
     uint64_t nxt[E];
-    int s = warp + 8;
+    int s = warp + kMergeWarps;
     if (s < nlists) {
       const uint64_t* p1 = lists + ((int64_t)s * list_stride + b) * L;
 #pragma unroll
-      for (int e = 0; e < E; ++e) nxt[e] = p1[e * 32 + lane];
+      for (int e = 0; e < E; ++e) nxt[e] = __ldcg(reinterpret_cast<const unsigned long long*>(p1 + e * 32 + lane));
     }
-    for (; s < nlists; s += 8) {
+    for (; s < nlists; s += kMergeWarps) {
       uint64_t cur[E];
 #pragma unroll
       for (int e = 0; e < E; ++e) cur[e] = nxt[e];
-      if (s + 8 < nlists) {
-        const uint64_t* p1 = lists + ((int64_t)(s + 8) * list_stride + b) * L;
+      if (s + kMergeWarps < nlists) {
+        const uint64_t* p1 = lists + ((int64_t)(s + kMergeWarps) * list_stride + b) * L;
 #pragma unroll
-        for (int e = 0; e < E; ++e) nxt[e] = p1[e * 32 + lane];
+        for (int e = 0; e < E; ++e) nxt[e] = __ldcg(reinterpret_cast<const unsigned long long*>(p1 + e * 32 + lane));
       }
       warp_merge_lists<E>(acc, cur, lane);
     }
@@ -425,13 +570,19 @@ __global__ void __launch_bounds__(256) merge_lists_kernel(const uint64_t* __rest
 #pragma unroll
   for (int e = 0; e < E; ++e) red[warp][e * 32 + lane] = acc[e];
   __syncthreads();
-  if (warp == 0) {
-    for (int w = 1; w < 8; ++w) {
+#pragma unroll
+  for (int half = kMergeWarps / 2; half >= 1; half >>= 1) {
+    if (warp < half) {
       uint64_t cur[E];
 #pragma unroll
-      for (int e = 0; e < E; ++e) cur[e] = red[w][e * 32 + lane];
+      for (int e = 0; e < E; ++e) cur[e] = red[warp + half][e * 32 + lane];
       warp_merge_lists<E>(acc, cur, lane);
+#pragma unroll
+      for (int e = 0; e < E; ++e) red[warp][e * 32 + lane] = acc[e];
     }
+    __syncthreads();
+  }
+  if (warp == 0) {
 #pragma unroll
     for (int e = 0; e < E; ++e) {
       const int i = e * 32 + lane;
@@ -473,8 +624,17 @@ template <int L>
 cudaError_t launch_merge(const uint64_t* lists, int nlists, int64_t list_stride, int64_t rows, int k, float* V,
                          int32_t* I, uint64_t* keys_out, cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
-  merge_lists_kernel<L><<<(unsigned)rows, 256, 0, stream>>>(lists, nlists, list_stride, rows, k, V, I, keys_out);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)rows);
+  cfg.blockDim = dim3(kMergeWarps * 32);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, merge_lists_kernel<L>, lists, nlists, list_stride, rows, k, V, I, keys_out);
 }
 
 #define STK_INST_FUSED(L, NT, S)                                                                                  \

@@ -21,10 +21,25 @@ struct UnitGrid {
   int64_t nchunks;  // ceil(F / 32)
 };
 
+// Per-CTA append buffers live in the workspace: [gridDim.x][kAppend][kRows] keys.
+constexpr size_t kAppendBytesPerCta = (size_t)kAppend * kRows * 8;
+
+// Pilot threshold: every CTA histograms the scores of its first 32 features
+// per row (bins = top kPilotBits of the order-preserving key), the CTAs meet
+// at a bounded grid barrier, and each row starts with the lower edge of the
+// bin that holds its k-th largest sampled score as filter floor.
+constexpr int kPilotBits = 12;
+constexpr int kPilotBins = 1 << kPilotBits;
+constexpr unsigned long long kPilotWaitNs = 200000;  // give up (no floor) after 200 us
+
 struct FusedParams {
   UnitGrid grid;
   const float* bias;
   uint64_t* partials;  // [units][128][L] keys
+  uint64_t* app;       // [gridDim.x][kAppend][128] keys
+  uint32_t* pilot_hist;    // [m_tiles][128][kPilotBins] counts, zeroed by the host; null = no pilot
+  uint32_t* pilot_rowmax;  // [m_tiles][128] highest bin seen per row
+  uint32_t* pilot_count;   // CTAs that finished their sample
   int64_t B, F;
   int k;
   int num_kb;          // ceil(d / 64)
@@ -37,22 +52,22 @@ struct SimtParams {
   UnitGrid grid;
   const float* bias;
   uint64_t* partials;
+  uint64_t* app;
   int64_t B, F, d;
   int k;
   uint32_t index_offset;
 };
 
 // Shared-memory plan of the fused kernel: STAGES x (X tile 128x64, W tile
-// NTx64, both K-major 128-byte swizzled), the per-row top lists and append
-// buffers, then the mbarriers.
+// NTx64, both K-major 128-byte swizzled), the per-row top lists, then the
+// mbarriers.
 template <int L, int NT, int STAGES>
 struct FusedCfg {
   static constexpr int kXBytes = kRows * 64 * 2;
   static constexpr int kWBytes = NT * 64 * 2;
   static constexpr int kStageBytes = kXBytes + kWBytes;
   static constexpr int kTopOff = STAGES * kStageBytes;
-  static constexpr int kAppOff = kTopOff + L * kRows * 8;
-  static constexpr int kBarOff = kAppOff + kAppend * kRows * 8;
+  static constexpr int kBarOff = kTopOff + L * kRows * 8;
   static constexpr int kSmemBytes = 1024 + kBarOff + 256;
   static constexpr int kTmemCols = (2 * NT <= 32) ? 32 : (2 * NT <= 64) ? 64 : (2 * NT <= 128) ? 128 : (2 * NT <= 256) ? 256 : 512;
   static_assert(NT % 32 == 0 && NT >= 32 && NT <= 256, "tile width");
@@ -61,7 +76,7 @@ struct FusedCfg {
 };
 
 // Shared-memory plan of the SIMT kernel: score tile (aliased by the GEMM
-// staging buffers), top lists, append buffers.
+// staging buffers), top lists.
 template <int L>
 struct SimtCfg {
   static constexpr int kNT = 128;
@@ -71,18 +86,19 @@ struct SimtCfg {
   static constexpr int kScOff = 0;
   static constexpr int kScBytes = kRows * (kRows + 1) * 4;
   static constexpr int kTopOff = (kScBytes + 15) & ~15;
-  static constexpr int kAppOff = kTopOff + L * kRows * 8;
-  static constexpr int kSmemBytes = 16 + kAppOff + kAppend * kRows * 8;
+  static constexpr int kSmemBytes = 16 + kTopOff + L * kRows * 8;
   static_assert(kWsOff + kKc * (kRows + 1) * 4 <= kScBytes, "staging must fit in the score tile");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
 // (L, NT, STAGES) instantiated for the fused kernel.
 #define STK_FUSED_CONFIGS(X) \
+  X(32, 256, 4)              \
   X(32, 256, 3)              \
-  X(64, 256, 2)              \
-  X(64, 128, 4)              \
-  X(128, 128, 2)
+  X(64, 256, 3)              \
+  X(64, 128, 5)              \
+  X(128, 256, 2)             \
+  X(128, 128, 3)
 
 template <int L, int NT, int STAGES>
 cudaError_t launch_fused(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tw32, const FusedParams& p,

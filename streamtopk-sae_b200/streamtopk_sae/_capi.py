@@ -14,12 +14,13 @@ LIB_PATH = os.path.join(_HERE, "libstk_b200.so")
 
 STK_OK, STK_EINVAL, STK_ECUDA, STK_EDEVICE, STK_ENOSPACE = 0, 1, 2, 3, 4
 STK_F32, STK_F16, STK_BF16 = 0, 1, 2
-STK_FLAG_ANY_K, STK_FLAG_ANY_D, STK_FLAG_SIMT = 1, 2, 4
+STK_FLAG_ANY_K, STK_FLAG_ANY_D, STK_FLAG_SIMT, STK_FLAG_NO_PILOT = 1, 2, 4, 8
 
 EXPORTS = (
     "stk_version", "stk_last_error", "stk_list_len", "stk_workspace_bytes",
     "stk_exact_forward", "stk_approx_forward", "stk_approx_candidates",
     "stk_shard_forward", "stk_merge_keys", "stk_device_error",
+    "stk_profile_begin", "stk_profile_end",
 )
 
 _lib = None
@@ -62,6 +63,10 @@ def load():
         L.stk_shard_forward.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32, vp, sz, vp]
         L.stk_merge_keys.restype = i32
         L.stk_merge_keys.argtypes = [vp, i64, i64, i64, vp, vp, vp]
+        L.stk_profile_begin.restype = i32
+        L.stk_profile_begin.argtypes = [i64]
+        L.stk_profile_end.restype = i32
+        L.stk_profile_end.argtypes = [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]
         L.stk_device_error.restype = i32
         L.stk_device_error.argtypes = [vp, ctypes.POINTER(ctypes.c_uint)]
         _lib = L
@@ -90,3 +95,31 @@ def device_error(stream_handle: int) -> int:
     code = ctypes.c_uint(0)
     check(load().stk_device_error(stream_handle, ctypes.byref(code)))
     return int(code.value)
+
+
+PROFILE_KINDS = ("fused_topk_kernel", "simt_topk_kernel", "merge_lists_kernel", "unused")
+
+
+class KernelTimer:
+    """CUDA-event timing of every library kernel launched inside the block.
+
+    >>> with KernelTimer(max_launches=10000) as kt: ...
+    >>> kt.ms["fused_topk_kernel"], kt.launches["fused_topk_kernel"]
+    """
+
+    def __init__(self, max_launches=100000):
+        self.max_launches = max_launches
+        self.ms = {}
+        self.launches = {}
+
+    def __enter__(self):
+        check(load().stk_profile_begin(self.max_launches))
+        return self
+
+    def __exit__(self, *exc):
+        ms = (ctypes.c_double * 4)()
+        n = (ctypes.c_int64 * 4)()
+        check(load().stk_profile_end(ms, n))
+        self.ms = {k: float(ms[i]) for i, k in enumerate(PROFILE_KINDS)}
+        self.launches = {k: int(n[i]) for i, k in enumerate(PROFILE_KINDS)}
+        return False

@@ -1,0 +1,117 @@
+"""Multi-GPU encoder: W_enc sharded along F, one process per GPU.
+
+Each rank holds the contiguous feature range [f0, f1) of W_enc / b_enc
+(``shard_bounds``).  One encode:
+
+  1. ``stk_shard_forward`` on the local shard: fused tcgen05 scores + top-k,
+     then the local merge of the CTA lists; writes this rank's best L keys per
+     row (L = 32/64/128 for k <= 32/64/128) with global feature indices
+     (local index + f0).
+  2. ``all_gather_into_tensor`` of the (B, L) int64 key lists over the process
+     group (NCCL over NVLink on B200; gloo works for host-side tests).
+  3. ``stk_merge_keys`` on every rank: top-k of world * L keys per row.
+
+Keys order by (score desc, feature index asc), so the result is identical to
+the single-GPU encode for any world size.  The reference has no multi-GPU
+path; the shard / all-gather / merge scheme follows BASELINE.json's north
+star.  The kernels are pluggable (``shard_fn`` / ``merge_fn``) so that the
+collective plumbing can be tested on CPU ranks with gloo.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import _capi
+from .native import _DTYPE_CODE, _require
+
+ALIGN = 128  # shard bounds are multiples of 128 features
+
+
+def shard_bounds(F: int, world: int, rank: int):
+    """Contiguous, 128-aligned feature range [f0, f1) of `rank` (last rank takes the tail)."""
+    per = -(-F // world)
+    per = -(-per // ALIGN) * ALIGN
+    f0 = min(F, rank * per)
+    f1 = min(F, (rank + 1) * per)
+    return f0, f1
+
+
+def _cuda_shard_fn(X, W_shard, b_shard, k, f_offset, out_keys):
+    B, d = X.shape
+    Fs = W_shard.shape[0]
+    lib = _capi.load()
+    with torch.cuda.device(X.device):
+        nbytes = _capi.workspace_bytes(B, d, Fs, k, _DTYPE_CODE[X.dtype])
+        ws = torch.empty(max(nbytes, 8), dtype=torch.uint8, device=X.device)
+        stream = torch.cuda.current_stream(X.device).cuda_stream
+        _capi.check(lib.stk_shard_forward(X.data_ptr(), W_shard.data_ptr(), b_shard.data_ptr(),
+                                          out_keys.data_ptr(), B, d, Fs, k, f_offset, _DTYPE_CODE[X.dtype],
+                                          _capi.STK_FLAG_ANY_K | _capi.STK_FLAG_ANY_D, ws.data_ptr(), nbytes,
+                                          stream))
+    return out_keys
+
+
+def _cuda_merge_fn(gathered, k):
+    P, B, L = gathered.shape
+    V = torch.empty((B, k), dtype=torch.float32, device=gathered.device)
+    I = torch.empty((B, k), dtype=torch.int32, device=gathered.device)
+    with torch.cuda.device(gathered.device):
+        stream = torch.cuda.current_stream(gathered.device).cuda_stream
+        _capi.check(_capi.load().stk_merge_keys(gathered.data_ptr(), P, B, k, V.data_ptr(), I.data_ptr(), stream))
+    return V, I
+
+
+class ShardedEncoder:
+    """F-sharded exact (or approx, c >= k) top-k encoder for one rank.
+
+    W_shard / b_shard: this rank's rows [f_offset, f_offset + F_shard) of
+    W_enc / b_enc; F_total: the full F; k: top-k.  ``encode(X)`` takes the
+    replicated (B, d) batch and returns (values fp32 (B, k), indices int32
+    (B, k)), identical on every rank.
+    """
+
+    def __init__(self, W_shard, b_shard, F_total, f_offset, k, group=None, mode="exact", c=None,
+                 shard_fn=None, merge_fn=None):
+        k = int(k)
+        _require(1 <= k <= 128, "k out of range")
+        _require(mode in ("exact", "approx"), "mode must be 'exact' or 'approx'")
+        if mode == "approx":
+            _require(c in (16, 32, 64, 128), f"streamtopk_cuda_approx: unsupported c={c}. Supported: 16,32,64,128.")
+            _require(k <= c, "k must be <= c")
+        _require(k <= F_total, "k out of range")
+        _require(W_shard.dim() == 2 and b_shard.dim() == 1 and b_shard.shape[0] == W_shard.shape[0],
+                 "b_enc F-dim mismatch")
+        self.W = W_shard.contiguous()
+        self.b = b_shard.float().contiguous()
+        self.F_total = int(F_total)
+        self.f_offset = int(f_offset)
+        self.k = k
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.L = _capi.list_len(k) if shard_fn is None else (32 if k <= 32 else 64 if k <= 64 else 128)
+        self.shard_fn = shard_fn or _cuda_shard_fn
+        self.merge_fn = merge_fn or _cuda_merge_fn
+
+    def encode(self, X):
+        X = X.contiguous()
+        _require(X.dim() == 2 and X.shape[1] == self.W.shape[1], "W_enc d-dim mismatch")
+        _require(X.dtype == self.W.dtype, "W_enc dtype must match X")
+        B = X.shape[0]
+        keys = torch.empty((B, self.L), dtype=torch.int64, device=X.device)
+        if self.W.shape[0] > 0:
+            self.shard_fn(X, self.W, self.b, self.k, self.f_offset, keys)
+        else:
+            keys.zero_()
+        if self.world > 1:
+            flat = torch.empty((self.world * B, self.L), dtype=torch.int64, device=X.device)
+            dist.all_gather_into_tensor(flat, keys, group=self.group)
+            gathered = flat.view(self.world, B, self.L)
+        else:
+            gathered = keys.unsqueeze(0)
+        return self.merge_fn(gathered, self.k)
+
+
+def topk_sae_cuda_exact_sharded(X, W_shard, b_shard, k, F_total, f_offset, group=None):
+    """One-shot sharded exact encode (see ShardedEncoder)."""
+    return ShardedEncoder(W_shard, b_shard, F_total, f_offset, k, group=group).encode(X)

@@ -199,3 +199,20 @@ def test_bias_cast_and_noncontiguous_inputs():
     Wnc = Wt.t().contiguous().t()
     V, I = stk.topk_sae_cuda_exact(Xt, Wnc, bt.double(), 16)
     check(V, I, Xr, Wr, br, 16, RTOL["bf16"])
+
+
+@pytest.mark.parametrize("B,d,F,k", [(128, 256, 65536, 64), (96, 512, 40000, 32), (200, 128, 30000, 128),
+                                     (128, 64, 300000, 16)])
+def test_sampled_floor_changes_nothing(B, d, F, k):
+    """The sampled threshold floor only skips work: results are bitwise equal
+    with and without it (keys are unique, so the top-k is unique)."""
+    from streamtopk_sae import _capi, native
+    X, W, b = oracle.gaussian_inputs(B, d, F, seed=F % 1000)
+    Xt, Wt, bt, Xr, Wr, br = device_inputs(X, W, b, "bf16")
+    V1, I1 = native.streamtopk_cuda_exact_forward(Xt, Wt, bt, k)
+    V2, I2 = native.streamtopk_cuda_exact_forward(Xt, Wt, bt, k, flags=_capi.STK_FLAG_NO_PILOT)
+    torch.cuda.synchronize()
+    no_device_error()
+    assert torch.equal(V1, V2) and torch.equal(I1, I2)
+    if F <= 70000:
+        check(V1, I1, Xr, Wr, br, k, RTOL["bf16"])
