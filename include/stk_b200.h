@@ -130,6 +130,21 @@ STK_API int stk_merge_keys(const uint64_t* lists, int64_t nlists, int64_t B, int
 STK_API int stk_device_error(void* stream, unsigned* code);
 
 /*
+ * Exact encode that allocates nothing and takes no workspace (no counterpart in
+ * the reference).  For callers that cannot allocate device memory (allocator
+ * hooks, plugins whose host owns all allocations, fixed-memory embedded or
+ * real-time code).  Same arguments and results as stk_exact_forward, minus the
+ * workspace: scratch comes from a 24 MiB array built into the library, which
+ * every GPU that loads the library holds until the process exits.  Shapes that
+ * need more scratch (more than one 128-row M tile, or k > 64 at large F) return
+ * STK_ENOSPACE.  The first call on a device looks up the array's device address
+ * (make it before any stream capture).  All calls share the array: calls that
+ * overlap on the GPU race and must be serialised by the caller.
+ */
+STK_API int stk_exact_forward_noalloc(const void* X, const void* W, const float* b, float* V, int32_t* I, int64_t B,
+                                      int64_t d, int64_t F, int64_t k, int dtype, int flags, void* stream);
+
+/*
  * Profiling hook (no reference counterpart).  stk_profile_begin arms CUDA
  * events around each kernel launched by the calls that follow (up to
  * max_launches launches, any thread); stk_profile_end synchronises them and

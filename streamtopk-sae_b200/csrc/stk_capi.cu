@@ -451,3 +451,70 @@ int stk_device_error(void* stream, unsigned* code) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Exact encode without any allocation, for callers that cannot allocate device
+// memory at all: code that runs inside another allocator's hooks, plugins whose
+// host process owns every allocation, and embedded / real-time callers whose
+// memory is fixed up front.  Instead of a caller-provided workspace it uses the
+// built-in scratch array below.
+//
+//  * Size: kNoAllocScratchBytes (24 MiB).  That covers one M tile (B <= 128)
+//    with k <= 64 at any F and d on a 148-SM B200; larger shapes are rejected
+//    with STK_ENOSPACE and a message giving both sizes.
+//  * The array is a file-scope __device__ variable, so every GPU on which this
+//    library's module is loaded holds its 24 MiB until the process exits.
+//  * Host code cannot use the array's name as a device address; its address is
+//    looked up with cudaGetSymbolAddress once per device, with that device
+//    current, on the first call made on that device (so make that first call
+//    before any stream capture).
+//  * All calls share the one array, which keeps the last call's contents: the
+//    parts that must start at zero are cleared by the call itself (a
+//    cudaMemsetAsync on the caller's stream), everything else is written before
+//    it is read.  Calls whose kernels overlap on the GPU (two streams, or two
+//    threads) race on the array; serialise them.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr size_t kNoAllocScratchBytes = size_t(24) << 20;
+}  // namespace
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+void* g_noalloc_ptr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+// Device address of g_noalloc_scratch on the current device (set up once).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(STK_EINVAL, "device ordinal out of range");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return STK_OK;
+}
+}  // namespace
+
+extern "C" int stk_exact_forward_noalloc(const void* X, const void* W, const float* b, float* V, int32_t* I,
+                                         int64_t B, int64_t d, int64_t F, int64_t k, int dtype, int flags,
+                                         void* stream) {
+  size_t need = 0;
+  if (stk_workspace_bytes(B, d, F, k, dtype, &need) == STK_OK && need > kNoAllocScratchBytes) {
+    return fail(STK_ENOSPACE, "stk_exact_forward_noalloc: this shape needs " + std::to_string(need) +
+                                  " bytes of scratch; the built-in scratch holds " +
+                                  std::to_string(kNoAllocScratchBytes) +
+                                  " bytes (use stk_exact_forward with a caller-allocated workspace)");
+  }
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  // Argument errors are reported by stk_exact_forward with the usual messages.
+  return stk_exact_forward(X, W, b, V, I, B, d, F, k, dtype, flags, scratch, kNoAllocScratchBytes, stream);
+}

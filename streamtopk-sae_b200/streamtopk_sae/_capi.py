@@ -20,7 +20,7 @@ EXPORTS = (
     "stk_version", "stk_last_error", "stk_list_len", "stk_workspace_bytes",
     "stk_exact_forward", "stk_approx_forward", "stk_approx_candidates",
     "stk_shard_forward", "stk_merge_keys", "stk_device_error",
-    "stk_profile_begin", "stk_profile_end",
+    "stk_profile_begin", "stk_profile_end", "stk_exact_forward_noalloc",
 )
 
 _lib = None
@@ -63,6 +63,8 @@ def load():
         L.stk_shard_forward.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32, vp, sz, vp]
         L.stk_merge_keys.restype = i32
         L.stk_merge_keys.argtypes = [vp, i64, i64, i64, vp, vp, vp]
+        L.stk_exact_forward_noalloc.restype = i32
+        L.stk_exact_forward_noalloc.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, i64, i32, i32, vp]
         L.stk_profile_begin.restype = i32
         L.stk_profile_begin.argtypes = [i64]
         L.stk_profile_end.restype = i32
