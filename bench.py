@@ -300,6 +300,7 @@ def run_b200(args, cfg):
         step = lambda x: stk.topk_sae_cuda_exact(x, W, b, k)  # noqa: E731
 
     stream = torch.cuda.current_stream(dev)
+    from streamtopk_sae.graph import CapturedEncode
 
     def barrier():
         if world > 1:
@@ -313,22 +314,47 @@ def run_b200(args, cfg):
     # ---------------- timed region (device-resident inputs)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize(dev)
-    with ClockSampler(local) as clk:
+    if world == 1:
+        # One GPU: the host enqueues a step far faster than the GPU runs it, so
+        # steps are launched eagerly; CUDA events around every library kernel.
+        G = 1
+        barrier()
+        torch.cuda.synchronize(dev)
         with _capi.KernelTimer(max_launches=args.steps * 4 + 16) as kt:
-            e0.record(stream)
-            for _ in range(args.steps):
-                step(X)
-            e1.record(stream)
+            with ClockSampler(local) as clk:
+                e0.record(stream)
+                for _ in range(args.steps):
+                    step(X)
+                e1.record(stream)
+                torch.cuda.synchronize(dev)
+        el_ms = e0.elapsed_time(e1)
+        launches = sum(kt.launches.values())
+    else:
+        # N GPUs: per-rank GPU time per step is small enough that host launch
+        # work (checks, ctypes, NCCL enqueue) would dominate, so each timed
+        # iteration replays a CUDA graph of G encode steps (memset, kernels,
+        # NCCL all-gather), as a serving loop would.
+        G = next(g for g in (8, 4, 2, 1) if args.steps % g == 0)
+        with _capi.KernelTimer(max_launches=G * 4 + 16) as kt:
+            timed = CapturedEncode(step, X, steps=G, warmup=0)   # event nodes around each library kernel
+            barrier()
             torch.cuda.synchronize(dev)
-    barrier()
-    el_ms = e0.elapsed_time(e1)
+            with ClockSampler(local) as clk:
+                e0.record(stream)
+                for _ in range(args.steps // G):
+                    timed.replay()
+                e1.record(stream)
+                torch.cuda.synchronize(dev)
+            barrier()
+            el_ms = e0.elapsed_time(e1)
+            del timed
+            torch.cuda.synchronize(dev)
+        # kt holds the G steps of the last replay (event nodes re-record per replay)
+        launches = sum(kt.launches.values()) // G * args.steps
     assert _capi.device_error(stream.cuda_stream) == 0
     t = torch.tensor([el_ms], device=dev, dtype=torch.float64)
     fused_ms = kt.ms["fused_topk_kernel"] + kt.ms["simt_topk_kernel"]
     fused_n = kt.launches["fused_topk_kernel"] + kt.launches["simt_topk_kernel"]
-    launches = sum(kt.launches.values())
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     el_ms = float(t.item())
@@ -338,12 +364,20 @@ def run_b200(args, cfg):
     Xh = X.cpu().pin_memory()
     Vh = torch.empty((B, k), dtype=torch.float32).pin_memory()
     Ih = torch.empty((B, k), dtype=torch.int32).pin_memory()
-    Xd = torch.empty_like(X)
     e2e_steps = max(1, min(args.steps, 2000))
+    if world == 1:
+        Xd = torch.empty_like(X)
+
+        def e2e_call(xh):
+            Xd.copy_(xh, non_blocking=True)
+            return step(Xd)
+        e2e = None
+    else:
+        e2e = CapturedEncode(step, X, steps=1, warmup=1)
+        e2e_call = e2e      # pinned host X -> static device buffer, replay
 
     def e2e_step():
-        Xd.copy_(Xh, non_blocking=True)
-        V, I = step(Xd)
+        V, I = e2e_call(Xh)
         Vh.copy_(V, non_blocking=True)
         Ih.copy_(I, non_blocking=True)
 
@@ -360,6 +394,8 @@ def run_b200(args, cfg):
     if world > 1:
         dist.all_reduce(t2, op=dist.ReduceOp.MAX)
     e2e_value = B * e2e_steps / (float(t2.item()) / 1e3)
+    del e2e
+    torch.cuda.synchronize(dev)
 
     # ---------------- roofline of the dominant kernel (this rank's shard)
     hbm, tf, tf_sus, src = load_peaks()
@@ -393,8 +429,9 @@ def run_b200(args, cfg):
             "config": config_dict(args, cfg), "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": Xh.numel() * Xh.element_size() * world,
                     "d2h_bytes_per_step": (Vh.numel() * 4 + Ih.numel() * 4) * world,
-                    "path": "streamtopk_sae.topk_sae_cuda_exact" if world == 1 else "streamtopk_sae.shard.ShardedEncoder.encode"},
-            "gpu_launches": launches, "clocks": clk.summary(),
+                    "path": ("streamtopk_sae.topk_sae_cuda_exact" if world == 1 else
+                             "streamtopk_sae.shard.ShardedEncoder.encode in a CUDA graph (graph.CapturedEncode)")},
+            "gpu_launches": launches, "graph_steps": G, "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -410,12 +447,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS))
+    ap.add_argument("--dtype", default=None, choices=["bf16", "fp16", "fp32"],
+                    help="input dtype override (config 2 is a dtype sweep)")
     ap.add_argument("--shape", default=None,
                     help="B,d,F,k override of the config's shape (small cases for ncu captures)")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     if args.shape:
         cfg["B"], cfg["d"], cfg["F"], cfg["k"] = (int(v) for v in args.shape.split(","))
+    if args.dtype:
+        cfg["dtype"] = args.dtype
     if args.impl == "reference":
         return run_reference(args, cfg)
     return run_b200(args, cfg)

@@ -66,6 +66,16 @@ struct ProfState {
 };
 ProfState g_prof;
 
+// Inside a stream capture the records become event-record nodes of the graph
+// (cudaEventRecordExternal), re-recorded at every replay.
+void prof_record(cudaEvent_t e, cudaStream_t s) {
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &st) == cudaSuccess && st == cudaStreamCaptureStatusActive)
+    cudaEventRecordWithFlags(e, s, cudaEventRecordExternal);
+  else
+    cudaEventRecord(e, s);
+}
+
 struct ProfScope {
   cudaStream_t s;
   cudaEvent_t e1 = nullptr;
@@ -77,10 +87,10 @@ struct ProfScope {
     e1 = g_prof.ev[g_prof.used + 1];
     g_prof.kind[g_prof.used / 2] = kind;
     g_prof.used += 2;
-    cudaEventRecord(e0, s);
+    prof_record(e0, s);
   }
   ~ProfScope() {
-    if (e1) cudaEventRecord(e1, s);
+    if (e1) prof_record(e1, s);
   }
 };
 
