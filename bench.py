@@ -347,8 +347,8 @@ def run_b200(args, cfg):
                 torch.cuda.synchronize(dev)
             barrier()
             el_ms = e0.elapsed_time(e1)
+            timed.close()
             del timed
-            torch.cuda.synchronize(dev)
         # kt holds the G steps of the last replay (event nodes re-record per replay)
         launches = sum(kt.launches.values()) // G * args.steps
     assert _capi.device_error(stream.cuda_stream) == 0
@@ -394,7 +394,9 @@ def run_b200(args, cfg):
     if world > 1:
         dist.all_reduce(t2, op=dist.ReduceOp.MAX)
     e2e_value = B * e2e_steps / (float(t2.item()) / 1e3)
-    del e2e
+    if e2e is not None:
+        e2e.close()
+    e2e = e2e_call = None
     torch.cuda.synchronize(dev)
 
     # ---------------- roofline of the dominant kernel (this rank's shard)
@@ -436,7 +438,13 @@ def run_b200(args, cfg):
         print(json.dumps(line), flush=True)
     if world > 1:
         barrier()
-        dist.destroy_process_group()
+        torch.cuda.synchronize(dev)
+        sys.stdout.flush()
+        sys.stderr.flush()
+        # Every graph holding NCCL work is released above; still, end the rank
+        # without the NCCL teardown so a stuck communicator can never keep the
+        # process (and its GPU) alive after the result is printed.
+        os._exit(0)
     return 0
 
 

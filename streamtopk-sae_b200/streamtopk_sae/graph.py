@@ -44,6 +44,18 @@ class CapturedEncode:
         self.graph.replay()
         return self.V, self.I
 
+    def close(self):
+        """Release the graph (and any NCCL work captured in it).
+
+        Graphs that hold NCCL collectives must be released before the process
+        group is destroyed, or the teardown waits for them forever.
+        """
+        if self.graph is not None:
+            torch.cuda.synchronize(self.X.device)
+            self.graph.reset()
+            self.graph = None
+        self.V = self.I = None
+
     def __call__(self, X=None):
         if X is not None:
             self.X.copy_(X, non_blocking=True)
