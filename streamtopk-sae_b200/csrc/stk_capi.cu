@@ -189,22 +189,28 @@ int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t 
   return STK_OK;
 }
 
-// Optional override of the fused tile configuration, "L,NT,STAGES", for tuning.
-bool fused_override(int L, int* nt, int* stages) {
+// Optional override of the fused tile configuration, "L,NT,STAGES,A,APP_SMEM",
+// for tuning.
+bool fused_override(int L, int* nt, int* stages, int* app, int* app_smem) {
   const char* s = std::getenv("STK_FUSED_CFG");
   if (!s) return false;
-  int l = 0, n = 0, st = 0;
-  if (std::sscanf(s, "%d,%d,%d", &l, &n, &st) != 3 || l != L) return false;
+  int l = 0, n = 0, st = 0, a = 0, sm = 0;
+  if (std::sscanf(s, "%d,%d,%d,%d,%d", &l, &n, &st, &a, &sm) != 5 || l != L) return false;
   *nt = n;
   *stages = st;
+  *app = a;
+  *app_smem = sm;
   return true;
 }
 
 int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint64_t* partials, uint64_t* app,
               int64_t B, int64_t d, int64_t F, int64_t k, int dtype, uint32_t index_offset, cudaStream_t stream) {
+  // Defaults: append slots in shared memory where 3 pipeline stages still fit.
   int nt = 256;
-  int stages = pl.L == 32 ? 4 : pl.L == 64 ? 3 : 2;
-  fused_override(pl.L, &nt, &stages);
+  int stages = pl.L == 128 ? 2 : 3;
+  int nslots = pl.L == 64 ? 16 : 32;
+  int app_smem = pl.L == 128 ? 0 : 1;
+  fused_override(pl.L, &nt, &stages, &nslots, &app_smem);
   CUtensorMap tx, tw, tw32;
   const bool bf16 = dtype == STK_BF16;
   int rc = make_map(&tx, X, B, d, stk::kRows, bf16);
@@ -236,8 +242,9 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   }
   cudaError_t e = cudaErrorInvalidValue;
   ProfScope prof(kProfFused, stream);
-#define STK_TRY_FUSED(Lc, NTc, Sc) \
-  if (pl.L == Lc && nt == NTc && stages == Sc) e = stk::launch_fused<Lc, NTc, Sc>(tx, tw, tw32, p, pl.ctas, stream);
+#define STK_TRY_FUSED(Lc, NTc, Sc, Ac, SMc)                                                  \
+  if (pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc)       \
+    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc>(tx, tw, tw32, p, pl.ctas, stream);
   STK_FUSED_CONFIGS(STK_TRY_FUSED)
 #undef STK_TRY_FUSED
   if (e != cudaSuccess) return cuda_fail(e, "fused_topk_kernel launch");

@@ -22,7 +22,7 @@
 namespace stk {
 
 constexpr int kRows = 128;          // batch rows per M tile (tcgen05 M)
-constexpr int kAppend = 32;         // per-row append slots between merges
+constexpr int kAppendMax = 32;      // most per-row append slots between merges
 constexpr uint64_t kEmptyKey = 0ull;
 // Upper bound for any single spin-wait on an mbarrier (nanoseconds).  A wait
 // that runs out sets the device error word and makes every role drain out.
@@ -58,6 +58,20 @@ __device__ __forceinline__ int32_t key_index(uint64_t key) {
 __device__ __forceinline__ uint64_t kmax(uint64_t a, uint64_t b) { return a > b ? a : b; }
 __device__ __forceinline__ uint64_t kmin(uint64_t a, uint64_t b) { return a > b ? b : a; }
 
+// Compare-exchange of two keys: a <- max, b <- min.  Written as one 64-bit
+// setp and two selp so the compiler emits predicated selects (no branches).
+__device__ __forceinline__ void cx(uint64_t& a, uint64_t& b) {
+  uint64_t mx, mn;
+  asm("{\n\t.reg .pred p;\n\t"
+      "setp.gt.u64 p, %2, %3;\n\t"
+      "selp.b64 %0, %2, %3, p;\n\t"
+      "selp.b64 %1, %3, %2, p;\n\t}\n"
+      : "=l"(mx), "=l"(mn)
+      : "l"(a), "l"(b));
+  a = mx;
+  b = mn;
+}
+
 // ---------------------------------------------------------------------------
 // Per-thread networks (N is a compile-time power of two; fully unrolled so the
 // arrays stay in registers).
@@ -72,11 +86,10 @@ __device__ __forceinline__ void sort_desc(uint64_t (&a)[N]) {
       for (int i = 0; i < N; ++i) {
         const int j = i ^ stride;
         if (j > i) {
-          const bool desc = (i & size) == 0;
-          const uint64_t x = a[i], y = a[j];
-          const bool sw = desc ? (x < y) : (x > y);
-          a[i] = sw ? y : x;
-          a[j] = sw ? x : y;
+          if ((i & size) == 0)
+            cx(a[i], a[j]);  // descending block
+          else
+            cx(a[j], a[i]);  // ascending block
         }
       }
     }
@@ -91,11 +104,7 @@ __device__ __forceinline__ void merge_desc(uint64_t (&a)[N]) {
 #pragma unroll
     for (int i = 0; i < N; ++i) {
       const int j = i ^ stride;
-      if (j > i) {
-        const uint64_t x = a[i], y = a[j];
-        a[i] = kmax(x, y);
-        a[j] = kmin(x, y);
-      }
+      if (j > i) cx(a[i], a[j]);
     }
   }
 }
@@ -105,12 +114,12 @@ __device__ __forceinline__ void merge_desc(uint64_t (&a)[N]) {
 //
 // Layout (slot-major, row-minor, so the 32 threads of a warp touch 32
 // consecutive 8-byte words):
-//   top[s * kRows + r], s < L : row r's best L keys, descending (0 = empty);
-//                               shared memory, addressed by its 32-bit
-//                               shared-window offset
-//   app[s * kRows + r], s < 32: row r's unsorted survivors since the last
-//                               merge; global memory (L2-resident workspace
-//                               slice of this CTA), written and read back by
+//   top[s * kRows + r], s < L : row r's best L keys, descending (0 = empty),
+//                               shared memory
+//   app[s * kRows + r], s < A : row r's unsorted survivors since the last
+//                               merge, in shared memory or (when shared
+//                               memory is short) in an L2-resident workspace
+//                               slice of this CTA, written and read back by
 //                               the same thread only
 // ---------------------------------------------------------------------------
 // Dynamic shared memory of every kernel in this library.  Per-row lists are
@@ -120,72 +129,84 @@ extern __shared__ __align__(16) uint8_t stk_smem[];
 
 __device__ __forceinline__ uint64_t* smem_keys(uint32_t off) { return reinterpret_cast<uint64_t*>(stk_smem + off); }
 
-// Merge row r's n waiting survivors (app, unsorted) into its sorted top list
-// and return the new threshold: the value of the (kth+1)-th best key, never
-// below floor_thr (a lower bound known from elsewhere, -inf if none).
-// Kept out of line: it runs rarely and is large.
-template <int L>
-__device__ __noinline__ float merge_survivors(uint32_t top_off, const uint64_t* __restrict__ app, int r, int n,
-                                              int kth, float floor_thr) {
+// Merge row r's n waiting survivors (A append slots, unsorted) into its sorted
+// top list and return the new threshold: the value of the (kth+1)-th best key,
+// never below floor_thr (a lower bound known from elsewhere, -inf if none).
+// The append slots are in shared memory (APP_SMEM, app_off = byte offset from
+// stk_smem) or in global memory (app_g).  Kept out of line: it runs rarely and
+// is large.
+template <int L, int A, bool APP_SMEM>
+__device__ __noinline__ float merge_survivors(uint32_t top_off, uint32_t app_off, const uint64_t* __restrict__ app_g,
+                                              int r, int n, int kth, float floor_thr) {
+  static_assert(A == 16 || A == 32, "append slots");
   uint64_t* top = smem_keys(top_off) + r;  // top[s * kRows] is slot s of row r
-  uint64_t a[32];
+  uint64_t a[A];
 #pragma unroll
-  for (int s = 0; s < 32; ++s)
-    a[s] = (s < n) ? (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(app + s * kRows + r)) : kEmptyKey;
-  sort_desc<32>(a);
+  for (int s = 0; s < A; ++s) {
+    if constexpr (APP_SMEM)
+      a[s] = (s < n) ? smem_keys(app_off)[s * kRows + r] : kEmptyKey;
+    else
+      a[s] = (s < n) ? (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(app_g + s * kRows + r))
+                     : kEmptyKey;
+  }
+  sort_desc<A>(a);
   if constexpr (L == 32) {
-    // top-32 of two sorted lists: c[i] = max(top[i], a[31 - i]) is bitonic.
+    // top-32 of two sorted lists: c[i] = max(top[i], a'[31 - i]) is bitonic
+    // (a' = a padded with empty keys; only the last A positions change).
+    uint64_t c[32];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const uint64_t lo = a[i], hi = a[31 - i];
-      a[i] = kmax(top[i * kRows], hi);
-      a[31 - i] = kmax(top[(31 - i) * kRows], lo);
-    }
-    merge_desc<32>(a);
+    for (int i = 0; i < 32; ++i) c[i] = top[i * kRows];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) top[i * kRows] = a[i];
+    for (int q = 0; q < A; ++q) c[32 - A + q] = kmax(c[32 - A + q], a[A - 1 - q]);
+    merge_desc<32>(c);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) top[i * kRows] = c[i];
   } else {
-    // Only the last 32 positions can change in c[i] = max(top[i], a'[L-1-i]).
+    // Only the last A positions can change in c[i] = max(top[i], a'[L-1-i]).
 #pragma unroll
-    for (int q = 0; q < 32; ++q) top[(L - 32 + q) * kRows] = kmax(top[(L - 32 + q) * kRows], a[31 - q]);
+    for (int q = 0; q < A; ++q) top[(L - A + q) * kRows] = kmax(top[(L - A + q) * kRows], a[A - 1 - q]);
     // Bitonic merge: strides >= 32 in shared memory, then 32-blocks in registers.
 #pragma unroll
     for (int stride = L >> 1; stride >= 32; stride >>= 1) {
 #pragma unroll 16
       for (int i = 0; i < L; ++i) {
         if ((i & stride) == 0) {
-          const uint64_t x = top[i * kRows], y = top[(i + stride) * kRows];
-          top[i * kRows] = kmax(x, y);
-          top[(i + stride) * kRows] = kmin(x, y);
+          uint64_t x = top[i * kRows], y = top[(i + stride) * kRows];
+          cx(x, y);
+          top[i * kRows] = x;
+          top[(i + stride) * kRows] = y;
         }
       }
     }
 #pragma unroll 1
     for (int blk = 0; blk < L / 32; ++blk) {
+      uint64_t c[32];
 #pragma unroll
-      for (int q = 0; q < 32; ++q) a[q] = top[(blk * 32 + q) * kRows];
-      merge_desc<32>(a);
+      for (int q = 0; q < 32; ++q) c[q] = top[(blk * 32 + q) * kRows];
+      merge_desc<32>(c);
 #pragma unroll
-      for (int q = 0; q < 32; ++q) top[(blk * 32 + q) * kRows] = a[q];
+      for (int q = 0; q < 32; ++q) top[(blk * 32 + q) * kRows] = c[q];
     }
   }
   const uint64_t kk = top[kth * kRows];
   return kk ? fmaxf(key_value(kk), floor_thr) : floor_thr;
 }
 
-template <int L>
+template <int L, int A, bool APP_SMEM>
 struct RowTopK {
-  uint32_t top;   // byte offset of top[0] from stk_smem
-  uint64_t* app;  // global
-  int r;          // row within the M tile
-  int cnt;        // survivors waiting in app
-  float thr;      // value of the k-th best key so far (-inf until k are held)
+  uint32_t top;     // byte offset of top[0] from stk_smem
+  uint32_t app_s;   // byte offset of the shared append slots (APP_SMEM)
+  uint64_t* app_g;  // global append slots (!APP_SMEM)
+  int r;            // row within the M tile
+  int cnt;          // survivors waiting in the append slots
+  float thr;        // value of the k-th best key so far (-inf until k are held)
   float floor_thr;  // known lower bound of the row's k-th score (-inf if none)
-  int kth;        // k - 1
+  int kth;          // k - 1
 
-  __device__ __forceinline__ void init(uint32_t top_, uint64_t* app_, int row, int k) {
+  __device__ __forceinline__ void init(uint32_t top_, uint32_t app_s_, uint64_t* app_g_, int row, int k) {
     top = top_;
-    app = app_;
+    app_s = app_s_;
+    app_g = app_g_;
     r = row;
     cnt = 0;
     thr = -__int_as_float(0x7f800000);
@@ -196,37 +217,47 @@ struct RowTopK {
   }
 
   __device__ __forceinline__ void flush() {
-    thr = merge_survivors<L>(top, app, r, cnt, kth, floor_thr);
+    thr = merge_survivors<L, A, APP_SMEM>(top, app_s, app_g, r, cnt, kth, floor_thr);
     cnt = 0;
+  }
+
+  __device__ __forceinline__ void push(uint64_t key) {
+    if constexpr (APP_SMEM)
+      smem_keys(app_s)[cnt * kRows + r] = key;
+    else
+      __stcg(reinterpret_cast<unsigned long long*>(app_g + cnt * kRows + r), (unsigned long long)key);
+    ++cnt;
   }
 
   // Offer one chunk of 32 scores (vals[j] is feature f0 + j).  valid_mask
   // marks real features (tail of F, rows beyond B).  All 32 lanes of the warp
   // must call this together: a merge runs for every lane as soon as one lane
-  // would overflow its append slots.
+  // would overflow its append slots.  A chunk may bring more survivors than
+  // A, so the chunk is taken in (at most 32 / A) passes of A candidates.
   __device__ __forceinline__ void offer(const float (&vals)[32], uint32_t f0, uint32_t valid_mask) {
     uint32_t mask = 0;
 #pragma unroll
     for (int j = 0; j < 32; ++j) mask |= (vals[j] > thr) ? (1u << j) : 0u;
     mask &= valid_mask;
-    if (__any_sync(0xffffffffu, cnt + __popc(mask) > kAppend)) {
-      flush();
-      mask = 0;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) mask |= (vals[j] > thr) ? (1u << j) : 0u;
-      mask &= valid_mask;
-    }
-    if (mask) {
+    for (int part = 0; part < 32 / A; ++part) {
+      const uint32_t pmask = mask & (A == 32 ? 0xffffffffu : (0xffffu << (16 * part)));
+      if (__any_sync(0xffffffffu, cnt + __popc(pmask) > A)) {
+        flush();
+        mask = 0;
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        if ((mask >> (8 * g)) & 0xffu) {
+        for (int j = 0; j < 32; ++j) mask |= (vals[j] > thr) ? (1u << j) : 0u;
+        mask &= valid_mask;
+      }
+      const uint32_t m = mask & (A == 32 ? 0xffffffffu : (0xffffu << (16 * part)));
+      if (m) {
 #pragma unroll
-          for (int jj = 0; jj < 8; ++jj) {
-            const int j = 8 * g + jj;
-            if (mask & (1u << j)) {
-              __stcg(reinterpret_cast<unsigned long long*>(app + cnt * kRows + r),
-                     (unsigned long long)make_key(vals[j], f0 + uint32_t(j)));
-              ++cnt;
+        for (int g = (A == 32 ? 0 : 2 * part); g < (A == 32 ? 4 : 2 * part + 2); ++g) {
+          if ((m >> (8 * g)) & 0xffu) {
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+              const int j = 8 * g + jj;
+              if (m & (1u << j)) push(make_key(vals[j], f0 + uint32_t(j)));
             }
           }
         }

@@ -167,11 +167,11 @@ __device__ __forceinline__ void load_bias_tile(const float* __restrict__ bias, i
 //   warp 0: TMA producer        warp 1: TMEM owner + MMA issuer
 //   warps 2..5: epilogue, warp w reads TMEM lanes 32*(w%4)..+31 (= batch rows)
 // ---------------------------------------------------------------------------
-template <int L, int NT, int STAGES>
+template <int L, int NT, int STAGES, int A, bool APP_SMEM>
 __global__ void __launch_bounds__(kFusedThreads, 1)
     fused_topk_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                       const __grid_constant__ CUtensorMap tmap_w32, const FusedParams p) {
-  using Cfg = FusedCfg<L, NT, STAGES>;
+  using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM>;
   uint8_t* smem = stk_smem + ((1024u - (smem_u32(stk_smem) & 1023u)) & 1023u);
   uint64_t* top = reinterpret_cast<uint64_t*>(smem + Cfg::kTopOff);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOff);
@@ -313,8 +313,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     const int r = q * 32 + lane;
     const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
     const uint32_t top_s = (uint32_t)(reinterpret_cast<uint8_t*>(top) - stk_smem);
-    uint64_t* app_cta = p.app + (size_t)blockIdx.x * (kAppend * kRows);
-    RowTopK<L> acc;
+    const uint32_t app_s = (uint32_t)(reinterpret_cast<uint8_t*>(smem + Cfg::kAppOff) - stk_smem);
+    uint64_t* app_cta = p.app + (size_t)blockIdx.x * (kAppendMax * kRows);
+    RowTopK<L, A, APP_SMEM> acc;
     uint32_t tile = 0;
     bool ok = true;
     TileWalk<NT> cur;
@@ -325,7 +326,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       TileWalk<NT> nxt = cur;
       nxt.next(g);
       if (nxt.valid(g)) load_bias_tile<NT>(p.bias, nxt.ft, nxt.width(), p.F, lane, bnext);
-      if (cur.first_of_unit()) acc.init(top_s, app_cta, r, p.k);
+      if (cur.first_of_unit()) acc.init(top_s, app_s, app_cta, r, p.k);
       const bool row_ok = (int64_t)cur.m * kRows + r < p.B;
       const int w = cur.width();
       const int a = tile & 1;
@@ -347,6 +348,54 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       tc_fence_after();
       const int nchunk = w / 32;
       const uint32_t tcol = t_lane + (uint32_t)(a * NT);
+      if (p.pilot_hist != nullptr && cur.first_of_unit()) {
+        // Sample: histogram the first chunks of this tile (they stay in TMEM
+        // and are offered below), meet the other CTAs, read back a floor.
+        uint32_t* h = p.pilot_hist + ((size_t)cur.m * kRows + r) * kPilotBins;
+        uint32_t bmax = 0;
+        bool any = false;
+#pragma unroll 1
+        for (int c = 0; c < kPilotChunks && c < nchunk; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tcol + (uint32_t)(c * 32), v);
+          tmem_wait_ld(v);
+          const int64_t f = cur.ft + 32 * c;
+          const float bl = pick<NT / 32>(bcur, c);
+          const uint32_t valid = row_ok ? feature_mask(f, p.F) : 0u;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float vj = __uint_as_float(v[j]) + __shfl_sync(0xffffffffu, bl, j);
+            if (valid & (1u << j)) {
+              const uint32_t bin = float_order(vj) >> (32 - kPilotBits);
+              atomicAdd(h + bin, 1u);
+              bmax = max(bmax, bin);
+            }
+          }
+          any |= valid != 0u;
+        }
+        if (any) atomicMax(p.pilot_rowmax + (size_t)cur.m * kRows + r, bmax);
+        __threadfence();
+        epilogue_bar();
+        if (warp == 2 && lane == 0) {
+          atomicAdd(p.pilot_count, 1u);
+          const unsigned long long t0 = global_timer_ns();
+          int ok_all = 1;
+          while (ld_acquire_u32(p.pilot_count) < gridDim.x) {
+            if (global_timer_ns() - t0 > kPilotWaitNs) {
+              ok_all = 0;
+              break;
+            }
+            __nanosleep(256);
+          }
+          *pilot_flag = ok_all;
+        }
+        epilogue_bar();
+        if (*pilot_flag && row_ok) {
+          const uint32_t tb = __ldcg(p.pilot_rowmax + (size_t)cur.m * kRows + r);
+          float lb;
+          if (pilot_bound(h, tb, p.k, lb)) acc.set_floor(lb);
+        }
+      }
 #pragma unroll 1
       for (int c = 0; c < nchunk; ++c) {
         uint32_t v[32];
@@ -363,41 +412,6 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j) vals[j] = __uint_as_float(v[j]) + __shfl_sync(0xffffffffu, bl, j);
         const uint32_t valid = row_ok ? feature_mask(f, p.F) : 0u;
-        if (p.pilot_hist != nullptr && c == 0 && cur.first_of_unit()) {
-          // Sample: histogram this chunk, meet the other CTAs, read back a floor.
-          uint32_t* h = p.pilot_hist + ((size_t)cur.m * kRows + r) * kPilotBins;
-          uint32_t bmax = 0;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (valid & (1u << j)) {
-              const uint32_t bin = float_order(vals[j]) >> (32 - kPilotBits);
-              atomicAdd(h + bin, 1u);
-              bmax = max(bmax, bin);
-            }
-          }
-          if (valid) atomicMax(p.pilot_rowmax + (size_t)cur.m * kRows + r, bmax);
-          __threadfence();
-          epilogue_bar();
-          if (warp == 2 && lane == 0) {
-            atomicAdd(p.pilot_count, 1u);
-            const unsigned long long t0 = global_timer_ns();
-            int ok_all = 1;
-            while (ld_acquire_u32(p.pilot_count) < gridDim.x) {
-              if (global_timer_ns() - t0 > kPilotWaitNs) {
-                ok_all = 0;
-                break;
-              }
-              __nanosleep(256);
-            }
-            *pilot_flag = ok_all;
-          }
-          epilogue_bar();
-          if (*pilot_flag && row_ok) {
-            const uint32_t tb = __ldcg(p.pilot_rowmax + (size_t)cur.m * kRows + r);
-            float lb;
-            if (pilot_bound(h, tb, p.k, lb)) acc.set_floor(lb);
-          }
-        }
         acc.offer(vals, p.index_offset + (uint32_t)f, valid);
       }
       if (cur.last_of_unit()) {
@@ -446,13 +460,13 @@ __global__ void __launch_bounds__(kSimtThreads, 1) simt_topk_kernel(const T* __r
   float* ws = reinterpret_cast<float*>(smem + Cfg::kWsOff);        // [kKc][129] features
   float* sc = reinterpret_cast<float*>(smem + Cfg::kScOff);        // [128 rows][129]
   const uint32_t top_s = (uint32_t)Cfg::kTopOff;
-  uint64_t* app_cta = p.app + (size_t)blockIdx.x * (kAppend * kRows);
+  uint64_t* app_cta = p.app + (size_t)blockIdx.x * (kAppendMax * kRows);
 
   const int tid = threadIdx.x;
   const int tx = tid & 15, ty = tid >> 4;
   const int lane = tid & 31;
   const UnitGrid& g = p.grid;
-  RowTopK<L> acc;
+  RowTopK<L, 32, false> acc;
   const bool vec_bias = (reinterpret_cast<uintptr_t>(p.bias) & 15) == 0;
 
   for (int u = blockIdx.x; u < g.units; u += gridDim.x) {
@@ -460,7 +474,7 @@ __global__ void __launch_bounds__(kSimtThreads, 1) simt_topk_kernel(const T* __r
     int64_t fb, fe;
     unit_range(g, u, m, fb, fe);
     const int64_t row0 = (int64_t)m * kRows;
-    if (tid < kRows) acc.init(top_s, app_cta, tid, p.k);
+    if (tid < kRows) acc.init(top_s, 0u, app_cta, tid, p.k);
     for (int64_t ft = fb; ft < fe; ft += Cfg::kNT) {
       const int w = (int)min((int64_t)Cfg::kNT, fe - ft);
       float c[8][8];
@@ -529,6 +543,7 @@ __global__ void __launch_bounds__(kSimtThreads, 1) simt_topk_kernel(const T* __r
 // that grid has completed and its writes are visible (a no-op otherwise).
 // ---------------------------------------------------------------------------
 constexpr int kMergeWarps = 16;
+constexpr int kMergeBatch = 8;
 
 template <int L>
 __global__ void __launch_bounds__(kMergeWarps * 32) merge_lists_kernel(const uint64_t* __restrict__ lists, int nlists,
@@ -544,27 +559,25 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_lists_kernel(const uin
   uint64_t acc[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) acc[e] = kEmptyKey;
-  if (warp < nlists) {
-    const uint64_t* p0 = lists + ((int64_t)warp * list_stride + b) * L;
+  // Warp w folds lists w, w+16, ...; kMergeBatch lists are loaded at once so
+  // each batch costs one memory round trip, and a list whose best key does not
+  // beat the current L-th best is skipped.
+  for (int s0 = warp; s0 < nlists; s0 += kMergeWarps * kMergeBatch) {
+    uint64_t buf[kMergeBatch][E];
 #pragma unroll
-    for (int e = 0; e < E; ++e) acc[e] = __ldcg(reinterpret_cast<const unsigned long long*>(p0 + e * 32 + lane));
-    uint64_t nxt[E];
-    int s = warp + kMergeWarps;
-    if (s < nlists) {
-      const uint64_t* p1 = lists + ((int64_t)s * list_stride + b) * L;
+    for (int q = 0; q < kMergeBatch; ++q) {
+      const int s = s0 + q * kMergeWarps;
+      const uint64_t* ps = lists + ((int64_t)s * list_stride + b) * L;
 #pragma unroll
-      for (int e = 0; e < E; ++e) nxt[e] = __ldcg(reinterpret_cast<const unsigned long long*>(p1 + e * 32 + lane));
+      for (int e = 0; e < E; ++e)
+        buf[q][e] = s < nlists ? (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(ps + e * 32 + lane))
+                               : kEmptyKey;
     }
-    for (; s < nlists; s += kMergeWarps) {
-      uint64_t cur[E];
 #pragma unroll
-      for (int e = 0; e < E; ++e) cur[e] = nxt[e];
-      if (s + kMergeWarps < nlists) {
-        const uint64_t* p1 = lists + ((int64_t)(s + kMergeWarps) * list_stride + b) * L;
-#pragma unroll
-        for (int e = 0; e < E; ++e) nxt[e] = __ldcg(reinterpret_cast<const unsigned long long*>(p1 + e * 32 + lane));
-      }
-      warp_merge_lists<E>(acc, cur, lane);
+    for (int q = 0; q < kMergeBatch; ++q) {
+      const uint64_t best = __shfl_sync(0xffffffffu, buf[q][0], 0);
+      const uint64_t worst = __shfl_sync(0xffffffffu, acc[E - 1], 31);
+      if (best > worst) warp_merge_lists<E>(acc, buf[q], lane);
     }
   }
 #pragma unroll
@@ -599,11 +612,11 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_lists_kernel(const uin
 // ---------------------------------------------------------------------------
 // Explicit instantiations and launch helpers (host side of this TU).
 // ---------------------------------------------------------------------------
-template <int L, int NT, int STAGES>
+template <int L, int NT, int STAGES, int A, bool APP_SMEM>
 cudaError_t launch_fused(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tw32, const FusedParams& p,
                          int grid, cudaStream_t stream) {
-  using Cfg = FusedCfg<L, NT, STAGES>;
-  auto kern = fused_topk_kernel<L, NT, STAGES>;
+  using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM>;
+  auto kern = fused_topk_kernel<L, NT, STAGES, A, APP_SMEM>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   if (e != cudaSuccess) return e;
   kern<<<grid, kFusedThreads, Cfg::kSmemBytes, stream>>>(tx, tw, tw32, p);
@@ -637,9 +650,9 @@ cudaError_t launch_merge(const uint64_t* lists, int nlists, int64_t list_stride,
   return cudaLaunchKernelEx(&cfg, merge_lists_kernel<L>, lists, nlists, list_stride, rows, k, V, I, keys_out);
 }
 
-#define STK_INST_FUSED(L, NT, S)                                                                                  \
-  template cudaError_t launch_fused<L, NT, S>(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, \
-                                              const FusedParams&, int, cudaStream_t);
+#define STK_INST_FUSED(L, NT, S, A, SM)                                                                           \
+  template cudaError_t launch_fused<L, NT, S, A, SM>(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, \
+                                                     const FusedParams&, int, cudaStream_t);
 STK_FUSED_CONFIGS(STK_INST_FUSED)
 
 #define STK_INST_SIMT(L)                                                                                         \

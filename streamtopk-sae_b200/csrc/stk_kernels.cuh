@@ -21,14 +21,16 @@ struct UnitGrid {
   int64_t nchunks;  // ceil(F / 32)
 };
 
-// Per-CTA append buffers live in the workspace: [gridDim.x][kAppend][kRows] keys.
-constexpr size_t kAppendBytesPerCta = (size_t)kAppend * kRows * 8;
+// Per-CTA global append buffers (configurations whose append slots do not fit
+// in shared memory): [gridDim.x][kAppendMax][kRows] keys in the workspace.
+constexpr size_t kAppendBytesPerCta = (size_t)kAppendMax * kRows * 8;
 
 // Pilot threshold: every CTA histograms the scores of its first 32 features
 // per row (bins = top kPilotBits of the order-preserving key), the CTAs meet
 // at a bounded grid barrier, and each row starts with the lower edge of the
 // bin that holds its k-th largest sampled score as filter floor.
 constexpr int kPilotBits = 12;
+constexpr int kPilotChunks = 2;  // sampled 32-feature chunks per CTA
 constexpr int kPilotBins = 1 << kPilotBits;
 constexpr unsigned long long kPilotWaitNs = 200000;  // give up (no floor) after 200 us
 
@@ -36,7 +38,7 @@ struct FusedParams {
   UnitGrid grid;
   const float* bias;
   uint64_t* partials;  // [units][128][L] keys
-  uint64_t* app;       // [gridDim.x][kAppend][128] keys
+  uint64_t* app;       // [gridDim.x][kAppendMax][128] keys (global append slots)
   uint32_t* pilot_hist;    // [m_tiles][128][kPilotBins] counts, zeroed by the host; null = no pilot
   uint32_t* pilot_rowmax;  // [m_tiles][128] highest bin seen per row
   uint32_t* pilot_count;   // CTAs that finished their sample
@@ -59,15 +61,16 @@ struct SimtParams {
 };
 
 // Shared-memory plan of the fused kernel: STAGES x (X tile 128x64, W tile
-// NTx64, both K-major 128-byte swizzled), the per-row top lists, then the
-// mbarriers.
-template <int L, int NT, int STAGES>
+// NTx64, both K-major 128-byte swizzled), the per-row top lists, the per-row
+// append slots when they live in shared memory (APP_SMEM), then the mbarriers.
+template <int L, int NT, int STAGES, int A, bool APP_SMEM>
 struct FusedCfg {
   static constexpr int kXBytes = kRows * 64 * 2;
   static constexpr int kWBytes = NT * 64 * 2;
   static constexpr int kStageBytes = kXBytes + kWBytes;
   static constexpr int kTopOff = STAGES * kStageBytes;
-  static constexpr int kBarOff = kTopOff + L * kRows * 8;
+  static constexpr int kAppOff = kTopOff + L * kRows * 8;
+  static constexpr int kBarOff = kAppOff + (APP_SMEM ? A * kRows * 8 : 0);
   static constexpr int kSmemBytes = 1024 + kBarOff + 256;
   static constexpr int kTmemCols = (2 * NT <= 32) ? 32 : (2 * NT <= 64) ? 64 : (2 * NT <= 128) ? 128 : (2 * NT <= 256) ? 256 : 512;
   static_assert(NT % 32 == 0 && NT >= 32 && NT <= 256, "tile width");
@@ -91,16 +94,17 @@ struct SimtCfg {
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
-// (L, NT, STAGES) instantiated for the fused kernel.
+// (L, NT, STAGES, A, APP_SMEM) instantiated for the fused kernel; the first
+// entry per L is the default (stk_capi.cu).
 #define STK_FUSED_CONFIGS(X) \
-  X(32, 256, 4)              \
-  X(32, 256, 3)              \
-  X(64, 256, 3)              \
-  X(64, 128, 5)              \
-  X(128, 256, 2)             \
-  X(128, 128, 3)
+  X(32, 256, 3, 32, true)    \
+  X(32, 256, 4, 32, false)   \
+  X(64, 256, 3, 16, true)    \
+  X(64, 256, 3, 32, false)   \
+  X(128, 256, 2, 32, false)  \
+  X(128, 128, 3, 32, false)
 
-template <int L, int NT, int STAGES>
+template <int L, int NT, int STAGES, int A, bool APP_SMEM>
 cudaError_t launch_fused(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tw32, const FusedParams& p,
                          int grid, cudaStream_t stream);
 
