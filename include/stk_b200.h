@@ -98,10 +98,14 @@ STK_API int stk_approx_forward(const void* X, const void* W, const float* b, flo
  * 128-feature tile t, the tile's best c scores, descending, padded with
  * (-FLT_MAX, -1) where the tile holds fewer than c features.
  * cand_vals / cand_idxs: (B, ceil(F/128), c).  Replaces the candidate buffer
- * written by streamtopk_approx_kernel (streamtopk_approx.cu:42-167).
+ * written by streamtopk_approx_kernel (streamtopk_approx.cu:42-167, returned
+ * by streamtopk_cuda_approx_forward at :286-290).  c in {16,32,64,128}.
+ * Workspace sized by stk_candidates_workspace_bytes.
  */
 STK_API int stk_approx_candidates(const void* X, const void* W, const float* b, float* cand_vals, int32_t* cand_idxs,
-                          int64_t B, int64_t d, int64_t F, int64_t c, int dtype, void* stream);
+                                  int64_t B, int64_t d, int64_t F, int64_t c, int dtype, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+STK_API int stk_candidates_workspace_bytes(int64_t B, int64_t d, int64_t F, int64_t c, int dtype, size_t* bytes);
 
 /*
  * One F-shard of a multi-GPU encode: the best L = stk_list_len(k) keys per row

@@ -148,6 +148,18 @@ stk::UnitGrid make_grid(int64_t B, int64_t F, int sms) {
   if ((int64_t)segs > g.nchunks) segs = (int)g.nchunks;
   g.segs = segs;
   g.units = g.m_tiles * segs;
+  g.fixed_chunks = 0;
+  return g;
+}
+
+// One unit per 128-feature tile (the approximate path's candidate tiles).
+stk::UnitGrid make_tile_grid(int64_t B, int64_t F) {
+  stk::UnitGrid g;
+  g.m_tiles = (int)((B + stk::kRows - 1) / stk::kRows);
+  g.nchunks = (F + 31) / 32;
+  g.fixed_chunks = 4;
+  g.segs = (int)((F + 127) / 128);
+  g.units = g.m_tiles * g.segs;
   return g;
 }
 
@@ -404,11 +416,62 @@ int stk_merge_keys(const uint64_t* lists, int64_t nlists, int64_t B, int64_t k, 
   return run_merge(list_len(k), lists, (int)nlists, B, B, k, V, I, nullptr, static_cast<cudaStream_t>(stream));
 }
 
+// Plan of the candidates path: one unit per 128-feature tile, list length L >= c.
+int candidates_plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t c, int dtype, Plan* pl) {
+  int sms = 0;
+  int rc = device_sms(&sms);
+  if (rc) return rc;
+  pl->L = list_len(c);
+  pl->tc = (dtype == STK_BF16 || dtype == STK_F16) && (d % 8 == 0) && (X == nullptr || aligned16(X)) &&
+           (W == nullptr || aligned16(W));
+  pl->grid = make_tile_grid(B, F);
+  if (pl->grid.units > 0x7fffffff / 2) return fail(STK_EINVAL, "too many candidate tiles");
+  pl->ctas = pl->grid.units < sms ? pl->grid.units : sms;
+  pl->pilot = false;
+  pl->ws_partials = (partial_bytes(pl->grid, pl->L) + 255) & ~size_t(255);
+  pl->ws_app = ((size_t)pl->ctas * stk::kAppendBytesPerCta + 255) & ~size_t(255);
+  pl->ws_pilot = 0;
+  pl->ws = pl->ws_partials + pl->ws_app;
+  return STK_OK;
+}
+
+int stk_candidates_workspace_bytes(int64_t B, int64_t d, int64_t F, int64_t c, int dtype, size_t* bytes) {
+  if (!bytes) return fail(STK_EINVAL, "bytes is NULL");
+  int rc = check_common("stk_candidates_workspace_bytes", B, d, F, dtype);
+  if (rc) return rc;
+  if (!(c == 16 || c == 32 || c == 64 || c == 128))
+    return fail(STK_EINVAL, "streamtopk_cuda_approx: unsupported c=" + std::to_string(c) + ". Supported: 16,32,64,128.");
+  Plan pl;
+  rc = candidates_plan(nullptr, nullptr, B, d, F, c, dtype, &pl);
+  if (rc) return rc;
+  *bytes = pl.ws;
+  return STK_OK;
+}
+
 int stk_approx_candidates(const void* X, const void* W, const float* b, float* cand_vals, int32_t* cand_idxs,
-                          int64_t B, int64_t d, int64_t F, int64_t c, int dtype, void* stream) {
-  (void)X; (void)W; (void)b; (void)cand_vals; (void)cand_idxs; (void)B; (void)d; (void)F; (void)c; (void)dtype;
-  (void)stream;
-  return fail(STK_EINVAL, "stk_approx_candidates: not built yet");
+                          int64_t B, int64_t d, int64_t F, int64_t c, int dtype, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  int rc = check_common("streamtopk_cuda_approx", B, d, F, dtype);
+  if (rc) return rc;
+  if (!(c == 16 || c == 32 || c == 64 || c == 128))
+    return fail(STK_EINVAL, "streamtopk_cuda_approx: unsupported c=" + std::to_string(c) + ". Supported: 16,32,64,128.");
+  Plan pl;
+  rc = candidates_plan(X, W, B, d, F, c, dtype, &pl);
+  if (rc) return rc;
+  if (B == 0) return STK_OK;
+  if (workspace_bytes < pl.ws || workspace == nullptr)
+    return fail(STK_ENOSPACE, "workspace too small (need " + std::to_string(pl.ws) + " bytes)");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint64_t* partials = static_cast<uint64_t*>(workspace);
+  uint64_t* app = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + pl.ws_partials);
+  // Every tile keeps its best L >= c scores per row (k = c); no threshold floor.
+  rc = pl.tc ? run_fused(pl, X, W, b, partials, app, B, d, F, c, dtype, 0u, s)
+             : run_simt(pl, X, W, b, partials, app, B, d, F, c, dtype, 0u, s);
+  if (rc) return rc;
+  cudaError_t e = stk::launch_candidates_out(partials, pl.L, pl.grid.m_tiles, pl.grid.segs, B, (int)c, cand_vals,
+                                             cand_idxs, s);
+  if (e != cudaSuccess) return cuda_fail(e, "candidates_out_kernel launch");
+  return STK_OK;
 }
 
 int stk_profile_begin(int64_t max_launches) {

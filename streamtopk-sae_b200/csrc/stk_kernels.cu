@@ -31,8 +31,9 @@ __device__ __forceinline__ void raise_device_error(unsigned code) { atomicCAS(&g
 __device__ __forceinline__ void unit_range(const UnitGrid& g, int u, int& m, int64_t& f_begin, int64_t& f_end) {
   const int seg = u / g.m_tiles;
   m = u - seg * g.m_tiles;
-  const int64_t c0 = (int64_t)seg * g.nchunks / g.segs;
-  const int64_t c1 = (int64_t)(seg + 1) * g.nchunks / g.segs;
+  const int64_t c0 = g.fixed_chunks > 0 ? (int64_t)seg * g.fixed_chunks : (int64_t)seg * g.nchunks / g.segs;
+  const int64_t c1 = g.fixed_chunks > 0 ? min(c0 + g.fixed_chunks, g.nchunks)
+                                        : (int64_t)(seg + 1) * g.nchunks / g.segs;
   f_begin = c0 * 32;
   f_end = c1 * 32;  // may pass F by < 32 on the last range; masked in the epilogue
 }
@@ -665,6 +666,29 @@ STK_FUSED_CONFIGS(STK_INST_FUSED)
 STK_INST_SIMT(32)
 STK_INST_SIMT(64)
 STK_INST_SIMT(128)
+
+__global__ void candidates_out_kernel(const uint64_t* __restrict__ partials, int L, int m_tiles, int64_t tiles,
+                                      int64_t rows, int c, float* __restrict__ vals, int32_t* __restrict__ idxs) {
+  const int64_t total = rows * tiles * c;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int s = (int)(i % c);
+    const int64_t t = (i / c) % tiles;
+    const int64_t b = i / ((int64_t)c * tiles);
+    const int64_t m = b / kRows, r = b % kRows;
+    const uint64_t key = partials[((t * m_tiles + m) * kRows + r) * L + s];
+    vals[i] = key ? key_value(key) : -3.402823466e+38f;
+    idxs[i] = key ? key_index(key) : -1;
+  }
+}
+
+cudaError_t launch_candidates_out(const uint64_t* partials, int L, int m_tiles, int64_t tiles, int64_t rows, int c,
+                                  float* vals, int32_t* idxs, cudaStream_t stream) {
+  const int64_t total = rows * tiles * c;
+  if (total <= 0) return cudaSuccess;
+  const int64_t blocks = min((total + 255) / 256, (int64_t)148 * 16);
+  candidates_out_kernel<<<(unsigned)blocks, 256, 0, stream>>>(partials, L, m_tiles, tiles, rows, c, vals, idxs);
+  return cudaGetLastError();
+}
 
 cudaError_t read_and_clear_device_error(unsigned* out, cudaStream_t stream) {
   unsigned zero = 0;

@@ -19,6 +19,7 @@ struct UnitGrid {
   int segs;         // feature ranges
   int units;        // m_tiles * segs
   int64_t nchunks;  // ceil(F / 32)
+  int fixed_chunks; // > 0: range s is chunks [s*fixed_chunks, (s+1)*fixed_chunks); 0: balanced split
 };
 
 // Per-CTA global append buffers (configurations whose append slots do not fit
@@ -114,6 +115,12 @@ cudaError_t launch_simt(const void* X, const void* W, const SimtParams& p, int g
 template <int L>
 cudaError_t launch_merge(const uint64_t* lists, int nlists, int64_t list_stride, int64_t rows, int k, float* V,
                          int32_t* I, uint64_t* keys_out, cudaStream_t stream);
+
+// Per-tile candidates of the approximate path: partials[(tile * m_tiles + m) *
+// 128 + r][0..L) -> cand_vals / cand_idxs [(row) * tiles + tile][0..c),
+// empty keys as (-FLT_MAX, -1).
+cudaError_t launch_candidates_out(const uint64_t* partials, int L, int m_tiles, int64_t tiles, int64_t rows, int c,
+                                  float* vals, int32_t* idxs, cudaStream_t stream);
 
 cudaError_t read_and_clear_device_error(unsigned* out, cudaStream_t stream);
 

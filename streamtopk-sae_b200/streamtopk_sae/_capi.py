@@ -20,7 +20,7 @@ EXPORTS = (
     "stk_version", "stk_last_error", "stk_list_len", "stk_workspace_bytes",
     "stk_exact_forward", "stk_approx_forward", "stk_approx_candidates",
     "stk_shard_forward", "stk_merge_keys", "stk_device_error",
-    "stk_profile_begin", "stk_profile_end", "stk_exact_forward_noalloc",
+    "stk_profile_begin", "stk_profile_end", "stk_exact_forward_noalloc", "stk_candidates_workspace_bytes",
 )
 
 _lib = None
@@ -58,7 +58,9 @@ def load():
         L.stk_approx_forward.restype = i32
         L.stk_approx_forward.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32, vp, sz, vp]
         L.stk_approx_candidates.restype = i32
-        L.stk_approx_candidates.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, i64, i32, vp]
+        L.stk_approx_candidates.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, i64, i32, vp, sz, vp]
+        L.stk_candidates_workspace_bytes.restype = i32
+        L.stk_candidates_workspace_bytes.argtypes = [i64, i64, i64, i64, i32, ctypes.POINTER(sz)]
         L.stk_shard_forward.restype = i32
         L.stk_shard_forward.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32, vp, sz, vp]
         L.stk_merge_keys.restype = i32
@@ -85,6 +87,12 @@ def check(rc: int) -> None:
 def workspace_bytes(B: int, d: int, F: int, k: int, dtype_code: int) -> int:
     out = ctypes.c_size_t(0)
     check(load().stk_workspace_bytes(B, d, F, k, dtype_code, ctypes.byref(out)))
+    return int(out.value)
+
+
+def candidates_workspace_bytes(B: int, d: int, F: int, c: int, dtype_code: int) -> int:
+    out = ctypes.c_size_t(0)
+    check(load().stk_candidates_workspace_bytes(B, d, F, c, dtype_code, ctypes.byref(out)))
     return int(out.value)
 
 

@@ -111,10 +111,12 @@ def streamtopk_cuda_approx_forward(X, W_enc, b_enc, k, c, candidate_buffer=None)
     _require(c in (16, 32, 64, 128), f"streamtopk_cuda_approx: unsupported c={c}. Supported: 16,32,64,128.")
     lib = _capi.load()
     with torch.cuda.device(X.device):
+        nbytes = _capi.candidates_workspace_bytes(B, d, F, c, _DTYPE_CODE[X.dtype])
+        ws = torch.empty(max(nbytes, 8), dtype=torch.uint8, device=X.device)
         stream = torch.cuda.current_stream(X.device).cuda_stream
         _capi.check(lib.stk_approx_candidates(X.data_ptr(), W_enc.data_ptr(), b_enc.data_ptr(),
                                               cand_vals.data_ptr(), cand_idxs.data_ptr(), B, d, F, c,
-                                              _DTYPE_CODE[X.dtype], stream))
+                                              _DTYPE_CODE[X.dtype], ws.data_ptr(), nbytes, stream))
     return cand_vals.view(B, tiles * c), cand_idxs.view(B, tiles * c), cand_vals, cand_idxs
 
 
