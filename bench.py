@@ -260,6 +260,8 @@ def config_dict(args, cfg):
                       (f", W_enc F-sharded over {args.gpus} GPUs" if args.gpus > 1 else "")),
          "B": cfg["B"], "d": cfg["d"], "F": cfg["F"], "k": cfg["k"], "global_batch": cfg["B"],
          "parallelism": f"F-shard{args.gpus}" if args.gpus > 1 else "single-gpu",
+         "exchange": (("direct peer stores over NVLink (stk_exchange_*)" if args.transport == "p2p" else
+                       "NCCL all_gather_into_tensor + merge kernel") if args.gpus > 1 else None),
          "l2": "inputs larger than L2: each rank streams >= 128 MiB of W_enc per step"}
     return d
 
@@ -294,7 +296,8 @@ def run_b200(args, cfg):
         W = W[f0:f1].clone()
         b = b[f0:f1].clone()
         torch.cuda.empty_cache()
-        enc = stk_shard.ShardedEncoder(W, b, F, f0, k, mode=cfg["mode"], c=cfg.get("c"))
+        enc = stk_shard.ShardedEncoder(W, b, F, f0, k, mode=cfg["mode"], c=cfg.get("c"),
+                                       transport=args.transport, max_rows=B)
         step = enc.encode
     elif cfg["mode"] == "approx":
         step = lambda x: stk.topk_sae_cuda_approx(x, W, b, k, cfg["c"])  # noqa: E731
@@ -341,8 +344,9 @@ def run_b200(args, cfg):
     else:
         # N GPUs: per-rank GPU time per step is small enough that host launch
         # work (checks, ctypes, NCCL enqueue) would dominate, so each timed
-        # iteration replays a CUDA graph of G encode steps (memset, kernels,
-        # NCCL all-gather), as a serving loop would.
+        # iteration replays a CUDA graph of G encode steps (memset, kernels and
+        # the peer-store exchange, or the NCCL all-gather), as a serving loop
+        # would.
         G = next(g for g in (8, 4, 2, 1) if args.steps % g == 0)
         with _capi.KernelTimer(max_launches=G * 4 + 16) as kt:
             timed = CapturedEncode(step, X, steps=G, warmup=0)   # event nodes around each library kernel
@@ -443,9 +447,11 @@ def run_b200(args, cfg):
                     "path": ("streamtopk_sae.topk_sae_cuda_exact" if world == 1 else
                              "streamtopk_sae.shard.ShardedEncoder.encode in a CUDA graph (graph.CapturedEncode)")},
             "gpu_launches": launches, "graph_steps": G, "clocks": clk.summary(),
+            "kernel_ms_per_step": {kk: v / (args.steps if world == 1 else G) for kk, v in kt.ms.items()},
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        enc.close()      # collective: unmaps the peers' exchange buffers
         barrier()
         torch.cuda.synchronize(dev)
         sys.stdout.flush()
@@ -466,6 +472,8 @@ def main():
     ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS))
     ap.add_argument("--dtype", default=None, choices=["bf16", "fp16", "fp32"],
                     help="input dtype override (config 2 is a dtype sweep)")
+    ap.add_argument("--transport", default="p2p", choices=["p2p", "nccl"],
+                    help="N>1: cross-GPU exchange of the per-rank key lists")
     ap.add_argument("--shape", default=None,
                     help="B,d,F,k override of the config's shape (small cases for ncu captures)")
     args = ap.parse_args()

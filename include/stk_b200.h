@@ -149,12 +149,52 @@ STK_API int stk_exact_forward_noalloc(const void* X, const void* W, const float*
                                       int64_t d, int64_t F, int64_t k, int dtype, int flags, void* stream);
 
 /*
+ * Direct GPU-to-GPU exchange for the F-sharded encode (no counterpart in the
+ * reference, which is single-GPU; the F-sharding follows the multi-GPU scheme
+ * of the hot path: shard W_enc / b_enc along F, exchange each rank's per-row
+ * top-L key lists, merge).  One process per GPU, all GPUs on one node with
+ * peer access (NVLink); at most 8 ranks.  Replaces the all-gather + merge of
+ * stk_shard_forward / stk_merge_keys with peer stores: each rank writes its
+ * lists straight into every rank's receive buffer and bumps that rank's
+ * arrival counter; each rank's final merge waits for all ranks' rows (bounded
+ * by wait_seconds, after which it reports device error 3 through
+ * stk_device_error and the exchange must be destroyed and re-created).
+ *
+ * Setup (collective: every rank, same world / max_rows / k):
+ *   stk_exchange_bytes -> allocate a 256-byte aligned device buffer of that size
+ *     (plain cudaMalloc-backed memory: cudaIpcGetMemHandle must accept it)
+ *   stk_exchange_create (clears its counters, synchronously)
+ *   stk_exchange_ipc_handle -> share the STK_IPC_HANDLE_BYTES handle + offset
+ *     with every rank (any host transport)
+ *   stk_exchange_connect with all ranks' handles / offsets (rank order)
+ * Each encode (collective, same B on every rank, calls in the same order):
+ *   stk_exchange_forward -> V (B, k) fp32, I (B, k) int32 over the global F.
+ * The step counter lives on the device, so forwards can be captured in a CUDA
+ * graph and replayed.  Teardown: make sure no rank has a forward in flight
+ * (synchronise + a host barrier), stk_exchange_destroy on every rank, a host
+ * barrier, then free the buffers.  The handle object is a small host struct.
+ */
+#define STK_IPC_HANDLE_BYTES 64
+typedef struct stk_exchange stk_exchange;
+STK_API int stk_exchange_bytes(int world, int64_t max_rows, int64_t k, size_t* bytes);
+STK_API int stk_exchange_create(int rank, int world, int64_t max_rows, int64_t k, void* buffer, size_t bytes,
+                                double wait_seconds, stk_exchange** out);
+STK_API int stk_exchange_ipc_handle(const stk_exchange* ex, void* handle /* STK_IPC_HANDLE_BYTES */,
+                                    int64_t* offset);
+STK_API int stk_exchange_connect(stk_exchange* ex, const void* handles /* world x STK_IPC_HANDLE_BYTES */,
+                                 const int64_t* offsets /* world */);
+STK_API int stk_exchange_forward(stk_exchange* ex, const void* X, const void* W_shard, const float* b_shard, float* V,
+                                 int32_t* I, int64_t B, int64_t d, int64_t F_shard, int64_t k, int64_t index_offset,
+                                 int dtype, int flags, void* workspace, size_t workspace_bytes, void* stream);
+STK_API int stk_exchange_destroy(stk_exchange* ex);
+
+/*
  * Profiling hook (no reference counterpart).  stk_profile_begin arms CUDA
  * events around each kernel launched by the calls that follow (up to
  * max_launches launches, any thread); stk_profile_end synchronises them and
  * returns, per kernel kind (0 fused tcgen05 score kernel, 1 SIMT score
- * kernel, 2 merge kernel, 3 unused), the summed device time in ms and the
- * number of launches.  No work is skipped or reordered.
+ * kernel, 2 merge kernel, 3 exchange publish + final merge), the summed
+ * device time in ms and the number of launches.  No work is skipped or reordered.
  */
 STK_API int stk_profile_begin(int64_t max_launches);
 STK_API int stk_profile_end(double* ms_by_kind /* [4] */, int64_t* launches_by_kind /* [4] */);

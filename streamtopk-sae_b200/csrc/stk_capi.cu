@@ -56,7 +56,7 @@ int device_sms(int* sms) {
 
 // Optional per-launch CUDA-event timing (stk_profile_begin/end): events are
 // recorded on the launching stream around each kernel, nothing is skipped.
-enum ProfKind { kProfFused = 0, kProfSimt = 1, kProfMerge = 2, kProfKinds = 4 };
+enum ProfKind { kProfFused = 0, kProfSimt = 1, kProfMerge = 2, kProfExchange = 3, kProfKinds = 4 };
 struct ProfState {
   std::mutex mu;
   std::atomic<bool> on{false};
@@ -107,6 +107,21 @@ EncodeTiledFn encode_tiled() {
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
       fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+using AddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+AddressRangeFn address_range() {
+  static AddressRangeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<AddressRangeFn>(p);
   });
   return fn;
 }
@@ -528,6 +543,195 @@ int stk_device_error(void* stream, unsigned* code) {
     return STK_EDEVICE;
   }
   return STK_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Direct GPU-to-GPU exchange for the F-sharded encode.
+// ---------------------------------------------------------------------------
+struct stk_exchange {
+  stk::ExchangeDev dev;
+  int device;
+  int L;
+  void* mapped[stk::kMaxWorld];  // IPC mapping bases of the peers' allocations
+};
+
+namespace {
+
+struct ExchangeLayout {
+  size_t recv, arrive, state, total;
+};
+
+ExchangeLayout exchange_layout(int world, int64_t max_rows, int L) {
+  ExchangeLayout x;
+  x.recv = 0;
+  x.arrive = (size_t(2) * world * max_rows * L * 8 + 255) & ~size_t(255);
+  x.state = x.arrive + ((size_t(2) * world * 8 + 255) & ~size_t(255));
+  x.total = x.state + 256;
+  return x;
+}
+
+int exchange_check(int world, int64_t max_rows, int64_t k) {
+  if (world < 1 || world > stk::kMaxWorld)
+    return fail(STK_EINVAL, "world must be in [1, " + std::to_string(stk::kMaxWorld) + "]");
+  if (max_rows < 1 || max_rows > (int64_t(1) << 24)) return fail(STK_EINVAL, "max_rows out of range");
+  if (k < 1 || k > 128) return fail(STK_EINVAL, "k out of range");
+  return STK_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int stk_exchange_bytes(int world, int64_t max_rows, int64_t k, size_t* bytes) {
+  if (!bytes) return fail(STK_EINVAL, "bytes is NULL");
+  int rc = exchange_check(world, max_rows, k);
+  if (rc) return rc;
+  *bytes = exchange_layout(world, max_rows, list_len(k)).total;
+  return STK_OK;
+}
+
+int stk_exchange_create(int rank, int world, int64_t max_rows, int64_t k, void* buffer, size_t bytes,
+                        double wait_seconds, stk_exchange** out) {
+  if (!out) return fail(STK_EINVAL, "out is NULL");
+  *out = nullptr;
+  int rc = exchange_check(world, max_rows, k);
+  if (rc) return rc;
+  if (rank < 0 || rank >= world) return fail(STK_EINVAL, "rank out of range");
+  if (!(wait_seconds > 0.0 && wait_seconds <= 600.0)) return fail(STK_EINVAL, "wait_seconds must be in (0, 600]");
+  const int L = list_len(k);
+  const ExchangeLayout lay = exchange_layout(world, max_rows, L);
+  if (!buffer || bytes < lay.total)
+    return fail(STK_ENOSPACE, "exchange buffer too small (need " + std::to_string(lay.total) + " bytes)");
+  if (reinterpret_cast<uintptr_t>(buffer) % 256) return fail(STK_EINVAL, "exchange buffer must be 256-byte aligned");
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  char* base = static_cast<char*>(buffer);
+  // Counters and the step start at zero; synchronous, so that no peer can
+  // store into the buffer before it is cleared.
+  e = cudaMemset(base + lay.arrive, 0, lay.total - lay.arrive);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "exchange buffer clear");
+  stk_exchange* x = new stk_exchange();
+  x->device = device;
+  x->L = L;
+  x->dev.recv = reinterpret_cast<uint64_t*>(base + lay.recv);
+  x->dev.arrive = reinterpret_cast<unsigned long long*>(base + lay.arrive);
+  x->dev.state = reinterpret_cast<unsigned long long*>(base + lay.state);
+  x->dev.rank = rank;
+  x->dev.world = world;
+  x->dev.max_rows = max_rows;
+  x->dev.wait_ns = (unsigned long long)(wait_seconds * 1e9);
+  x->dev.peer_recv[rank] = x->dev.recv;
+  x->dev.peer_arrive[rank] = x->dev.arrive;
+  *out = x;
+  return STK_OK;
+}
+
+int stk_exchange_ipc_handle(const stk_exchange* x, void* handle, int64_t* offset) {
+  if (!x || !handle || !offset) return fail(STK_EINVAL, "null argument");
+  AddressRangeFn range = address_range();
+  if (!range) return fail(STK_ECUDA, "cuMemGetAddressRange unavailable");
+  CUdeviceptr alloc_base = 0;
+  size_t alloc_size = 0;
+  CUresult r = range(&alloc_base, &alloc_size, reinterpret_cast<CUdeviceptr>(x->dev.recv));
+  if (r != CUDA_SUCCESS) return fail(STK_ECUDA, "cuMemGetAddressRange failed (CUresult " + std::to_string(r) + ")");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(alloc_base));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  std::memcpy(handle, &h, sizeof h);
+  *offset = (int64_t)(reinterpret_cast<CUdeviceptr>(x->dev.recv) - alloc_base);
+  return STK_OK;
+}
+
+int stk_exchange_connect(stk_exchange* x, const void* handles, const int64_t* offsets) {
+  if (!x || !handles || !offsets) return fail(STK_EINVAL, "null argument");
+  const ExchangeLayout lay = exchange_layout(x->dev.world, x->dev.max_rows, x->L);
+  for (int p = 0; p < x->dev.world; ++p) {
+    if (p == x->dev.rank || x->mapped[p]) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, static_cast<const char*>(handles) + (size_t)p * STK_IPC_HANDLE_BYTES, sizeof h);
+    void* m = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&m, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e, ("cudaIpcOpenMemHandle (rank " + std::to_string(p) + ")").c_str());
+    x->mapped[p] = m;
+    char* peer = static_cast<char*>(m) + offsets[p];
+    x->dev.peer_recv[p] = reinterpret_cast<uint64_t*>(peer + lay.recv);
+    x->dev.peer_arrive[p] = reinterpret_cast<unsigned long long*>(peer + lay.arrive);
+  }
+  return STK_OK;
+}
+
+int stk_exchange_forward(stk_exchange* x, const void* X, const void* W_shard, const float* b_shard, float* V,
+                         int32_t* I, int64_t B, int64_t d, int64_t F_shard, int64_t k, int64_t index_offset,
+                         int dtype, int flags, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!x) return fail(STK_EINVAL, "exchange is NULL");
+  for (int p = 0; p < x->dev.world; ++p)
+    if (!x->dev.peer_recv[p]) return fail(STK_EINVAL, "exchange is not connected");
+  // An empty shard (F_shard == 0) still publishes (empty lists): every rank's
+  // final merge waits for the rows of all ranks.
+  int rc = check_common("stk_exchange_forward", B, d, F_shard > 0 ? F_shard : 1, dtype);
+  if (rc) return rc;
+  if (k < 1 || k > 128 || list_len(k) != x->L) return fail(STK_EINVAL, "k does not match the exchange");
+  if (B > x->dev.max_rows) return fail(STK_EINVAL, "B exceeds the exchange's max_rows");
+  if (index_offset < 0 || index_offset + F_shard > 0x7fffffffLL)
+    return fail(STK_EINVAL, "index_offset + F_shard must fit int32 indices");
+  Plan pl;
+  if (F_shard > 0) {
+    rc = plan(X, W_shard, B, d, F_shard, k, dtype, flags, &pl);
+    if (rc) return rc;
+  }
+  if (B == 0) return STK_OK;
+  if (F_shard > 0 && (workspace_bytes < pl.ws || (pl.ws && workspace == nullptr)))
+    return fail(STK_ENOSPACE, "workspace too small (need " + std::to_string(pl.ws) + " bytes)");
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (device != x->device) return fail(STK_EINVAL, "current device is not the exchange's device");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint64_t* partials = static_cast<uint64_t*>(workspace);
+  int nlists = 0;
+  int64_t stride = 0;
+  if (F_shard > 0) {
+    uint64_t* app = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + pl.ws_partials);
+    rc = pl.tc ? run_fused(pl, X, W_shard, b_shard, partials, app, B, d, F_shard, k, dtype, (uint32_t)index_offset, s)
+               : run_simt(pl, X, W_shard, b_shard, partials, app, B, d, F_shard, k, dtype, (uint32_t)index_offset,
+                          s);
+    if (rc) return rc;
+    nlists = pl.grid.segs;
+    stride = (int64_t)pl.grid.m_tiles * stk::kRows;
+  }
+  {
+    ProfScope prof(kProfExchange, s);
+    e = cudaErrorInvalidValue;
+    if (x->L == 32) e = stk::launch_publish<32>(partials, nlists, stride, B, x->dev, s);
+    if (x->L == 64) e = stk::launch_publish<64>(partials, nlists, stride, B, x->dev, s);
+    if (x->L == 128) e = stk::launch_publish<128>(partials, nlists, stride, B, x->dev, s);
+    if (e != cudaSuccess) return cuda_fail(e, "publish_kernel launch");
+    if (x->L == 32) e = stk::launch_exchange_merge<32>(x->dev, B, (int)k, V, I, s);
+    if (x->L == 64) e = stk::launch_exchange_merge<64>(x->dev, B, (int)k, V, I, s);
+    if (x->L == 128) e = stk::launch_exchange_merge<128>(x->dev, B, (int)k, V, I, s);
+    if (e != cudaSuccess) return cuda_fail(e, "exchange_merge_kernel launch");
+  }
+  return STK_OK;
+}
+
+int stk_exchange_destroy(stk_exchange* x) {
+  if (!x) return STK_OK;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(x->device);
+  int rc = STK_OK;
+  for (int p = 0; p < stk::kMaxWorld; ++p) {
+    if (!x->mapped[p]) continue;
+    cudaError_t e = cudaIpcCloseMemHandle(x->mapped[p]);
+    if (e != cudaSuccess && rc == STK_OK) rc = cuda_fail(e, "cudaIpcCloseMemHandle");
+  }
+  cudaSetDevice(prev);
+  delete x;
+  return rc;
 }
 
 }  // extern "C"

@@ -546,23 +546,18 @@ __global__ void __launch_bounds__(kSimtThreads, 1) simt_topk_kernel(const T* __r
 constexpr int kMergeWarps = 16;
 constexpr int kMergeBatch = 8;
 
+// Folds the nlists sorted lists of row b (list s at lists[(s*list_stride + b)*L])
+// into the best L keys, left in warp 0's acc.  Warp w folds lists w, w+16, ...;
+// kMergeBatch lists are loaded at once (one memory round trip per batch) and a
+// list whose best key does not beat the current L-th best is skipped; a 4-level
+// tree in shared memory folds the 16 warp results.  All threads must call it.
 template <int L>
-__global__ void __launch_bounds__(kMergeWarps * 32) merge_lists_kernel(const uint64_t* __restrict__ lists, int nlists,
-                                                                        int64_t list_stride, int64_t rows, int k,
-                                                                        float* __restrict__ V, int32_t* __restrict__ I,
-                                                                        uint64_t* __restrict__ keys_out) {
+__device__ __forceinline__ void fold_row(const uint64_t* __restrict__ lists, int nlists, int64_t list_stride,
+                                         int64_t b, uint64_t (&acc)[L / 32], uint64_t (*red)[L], int warp,
+                                         int lane) {
   constexpr int E = L / 32;
-  __shared__ uint64_t red[kMergeWarps][L];
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int64_t b = blockIdx.x;
-  if (b >= rows) return;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint64_t acc[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) acc[e] = kEmptyKey;
-  // Warp w folds lists w, w+16, ...; kMergeBatch lists are loaded at once so
-  // each batch costs one memory round trip, and a list whose best key does not
-  // beat the current L-th best is skipped.
   for (int s0 = warp; s0 < nlists; s0 += kMergeWarps * kMergeBatch) {
     uint64_t buf[kMergeBatch][E];
 #pragma unroll
@@ -596,16 +591,126 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_lists_kernel(const uin
     }
     __syncthreads();
   }
-  if (warp == 0) {
+}
+
+template <int L>
+__device__ __forceinline__ void write_row(const uint64_t (&acc)[L / 32], int64_t b, int k, float* __restrict__ V,
+                                          int32_t* __restrict__ I, uint64_t* __restrict__ keys_out, int lane) {
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-      const int i = e * 32 + lane;
-      const uint64_t key = acc[e];
-      if (i < k) {
-        V[b * k + i] = key ? key_value(key) : -3.402823466e+38f;
-        I[b * k + i] = key ? key_index(key) : -1;
+  for (int e = 0; e < L / 32; ++e) {
+    const int i = e * 32 + lane;
+    const uint64_t key = acc[e];
+    if (i < k) {
+      V[b * k + i] = key ? key_value(key) : -3.402823466e+38f;
+      I[b * k + i] = key ? key_index(key) : -1;
+    }
+    if (keys_out) keys_out[b * L + i] = key;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Merge kernel: one CTA (16 warps) per row.  Launched with programmatic
+// dependent launch after the score kernel: griddepcontrol.wait blocks until
+// that grid has completed and its writes are visible (a no-op otherwise).
+// ---------------------------------------------------------------------------
+template <int L>
+__global__ void __launch_bounds__(kMergeWarps * 32) merge_lists_kernel(const uint64_t* __restrict__ lists, int nlists,
+                                                                        int64_t list_stride, int64_t rows, int k,
+                                                                        float* __restrict__ V, int32_t* __restrict__ I,
+                                                                        uint64_t* __restrict__ keys_out) {
+  __shared__ uint64_t red[kMergeWarps][L];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int64_t b = blockIdx.x;
+  if (b >= rows) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t acc[L / 32];
+  fold_row<L>(lists, nlists, list_stride, b, acc, red, warp, lane);
+  if (warp == 0) write_row<L>(acc, b, k, V, I, keys_out, lane);
+}
+
+// ---------------------------------------------------------------------------
+// Publish kernel (F-sharded encode): folds this rank's CTA lists of row b like
+// the merge kernel; then warp p stores the row's best L keys into slot
+// [step & 1][rank] of rank p's receive buffer (a peer store over NVLink for
+// p != rank) and, after a system-scope fence, adds 1 to rank p's arrival
+// counter for this rank.
+// ---------------------------------------------------------------------------
+template <int L>
+__global__ void __launch_bounds__(kMergeWarps * 32) publish_kernel(const uint64_t* __restrict__ lists, int nlists,
+                                                                    int64_t list_stride, int64_t rows,
+                                                                    const ExchangeDev ex) {
+  __shared__ uint64_t red[kMergeWarps][L];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int64_t b = blockIdx.x;
+  if (b >= rows) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned long long step = *reinterpret_cast<volatile unsigned long long*>(ex.state);
+  const int slot = (int)(step & 1ull);
+  uint64_t acc[L / 32];
+  fold_row<L>(lists, nlists, list_stride, b, acc, red, warp, lane);  // ends with red[0] = the row's list
+  if (warp < ex.world) {
+    uint64_t* dst = ex.peer_recv[warp] + (((int64_t)slot * ex.world + ex.rank) * ex.max_rows + b) * L;
+#pragma unroll
+    for (int e = 0; e < L / 32; ++e)
+      __stcg(reinterpret_cast<unsigned long long*>(dst + e * 32 + lane), (unsigned long long)red[0][e * 32 + lane]);
+    __threadfence_system();
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence_system();  // cumulative: the whole warp's stores precede the count
+      atomicAdd_system(ex.peer_arrive[warp] + slot * ex.world + ex.rank, 1ull);
+    }
+  }
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// Final merge of the exchange: one CTA per row waits (bounded) until every
+// rank's rows of this step have arrived, folds the world lists, writes V/I;
+// the last CTA clears the slot's counters and advances the step counter.
+// ---------------------------------------------------------------------------
+template <int L>
+__global__ void __launch_bounds__(kMergeWarps * 32) exchange_merge_kernel(const ExchangeDev ex, int64_t rows, int k,
+                                                                           float* __restrict__ V,
+                                                                           int32_t* __restrict__ I) {
+  __shared__ uint64_t red[kMergeWarps][L];
+  __shared__ int timed_out;
+  const int64_t b = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned long long step = *reinterpret_cast<volatile unsigned long long*>(ex.state);
+  const int slot = (int)(step & 1ull);
+  if (threadIdx.x == 0) {
+    timed_out = 0;
+    const unsigned long long t0 = global_timer_ns();
+    for (int p = 0; p < ex.world; ++p) {
+      while (ld_acquire_sys_u64(ex.arrive + slot * ex.world + p) < (unsigned long long)rows) {
+        if (global_timer_ns() - t0 > ex.wait_ns) {
+          timed_out = 1;
+          break;
+        }
+        __nanosleep(128);
       }
-      if (keys_out) keys_out[b * L + i] = key;
+      if (timed_out) break;
+    }
+    if (timed_out) raise_device_error(kErrExchangeTimeout);
+  }
+  __syncthreads();
+  uint64_t acc[L / 32];
+  fold_row<L>(ex.recv + (int64_t)slot * ex.world * ex.max_rows * L, ex.world, ex.max_rows, b, acc, red, warp, lane);
+  if (warp == 0) write_row<L>(acc, b, k, V, I, nullptr, lane);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned long long done = atomicAdd(ex.state + 1, 1ull);
+    if (done == (unsigned long long)gridDim.x - 1) {
+      // Every CTA of this step has passed its wait: reset for step + 2.
+      for (int p = 0; p < ex.world; ++p) ex.arrive[slot * ex.world + p] = 0ull;
+      ex.state[1] = 0ull;
+      __threadfence();
+      ex.state[0] = step + 1ull;
     }
   }
 }
@@ -631,6 +736,30 @@ cudaError_t launch_simt(const void* X, const void* W, const SimtParams& p, int g
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   if (e != cudaSuccess) return e;
   kern<<<grid, kSimtThreads, Cfg::kSmemBytes, stream>>>(static_cast<const T*>(X), static_cast<const T*>(W), p);
+  return cudaGetLastError();
+}
+
+template <int L>
+cudaError_t launch_publish(const uint64_t* lists, int nlists, int64_t list_stride, int64_t rows,
+                           const ExchangeDev& ex, cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)rows);
+  cfg.blockDim = dim3(kMergeWarps * 32);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, publish_kernel<L>, lists, nlists, list_stride, rows, ex);
+}
+
+template <int L>
+cudaError_t launch_exchange_merge(const ExchangeDev& ex, int64_t rows, int k, float* V, int32_t* I,
+                                  cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  exchange_merge_kernel<L><<<(unsigned)rows, kMergeWarps * 32, 0, stream>>>(ex, rows, k, V, I);
   return cudaGetLastError();
 }
 
@@ -662,7 +791,10 @@ STK_FUSED_CONFIGS(STK_INST_FUSED)
   template cudaError_t launch_simt<__nv_bfloat16, L>(const void*, const void*, const SimtParams&, int,          \
                                                      cudaStream_t);                                             \
   template cudaError_t launch_merge<L>(const uint64_t*, int, int64_t, int64_t, int, float*, int32_t*, uint64_t*, \
-                                       cudaStream_t);
+                                       cudaStream_t);                                                           \
+  template cudaError_t launch_publish<L>(const uint64_t*, int, int64_t, int64_t, const ExchangeDev&,            \
+                                         cudaStream_t);                                                         \
+  template cudaError_t launch_exchange_merge<L>(const ExchangeDev&, int64_t, int, float*, int32_t*, cudaStream_t);
 STK_INST_SIMT(32)
 STK_INST_SIMT(64)
 STK_INST_SIMT(128)

@@ -116,6 +116,33 @@ template <int L>
 cudaError_t launch_merge(const uint64_t* lists, int nlists, int64_t list_stride, int64_t rows, int k, float* V,
                          int32_t* I, uint64_t* keys_out, cudaStream_t stream);
 
+// Direct GPU-to-GPU exchange of per-rank key lists (F-sharded encode, one
+// process per GPU on one node).  Each rank owns one exchange buffer:
+//   recv   [2][world][max_rows][L] keys   (slot = step & 1)
+//   arrive [2][world] u64 row counters     (rows received from each rank)
+//   state  [2] u64: step counter, CTAs done in the current final merge
+// peer_recv / peer_arrive[p] are rank p's recv / arrive mapped into this
+// process (CUDA IPC); entry `rank` is the local buffer.
+constexpr int kMaxWorld = 8;
+struct ExchangeDev {
+  uint64_t* peer_recv[kMaxWorld];
+  unsigned long long* peer_arrive[kMaxWorld];
+  uint64_t* recv;
+  unsigned long long* arrive;
+  unsigned long long* state;
+  int rank, world;
+  int64_t max_rows;
+  unsigned long long wait_ns;
+};
+constexpr unsigned kErrExchangeTimeout = 3;
+
+template <int L>
+cudaError_t launch_publish(const uint64_t* lists, int nlists, int64_t list_stride, int64_t rows,
+                           const ExchangeDev& ex, cudaStream_t stream);
+template <int L>
+cudaError_t launch_exchange_merge(const ExchangeDev& ex, int64_t rows, int k, float* V, int32_t* I,
+                                  cudaStream_t stream);
+
 // Per-tile candidates of the approximate path: partials[(tile * m_tiles + m) *
 // 128 + r][0..L) -> cand_vals / cand_idxs [(row) * tiles + tile][0..c),
 // empty keys as (-FLT_MAX, -1).

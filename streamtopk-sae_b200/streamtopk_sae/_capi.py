@@ -21,7 +21,10 @@ EXPORTS = (
     "stk_exact_forward", "stk_approx_forward", "stk_approx_candidates",
     "stk_shard_forward", "stk_merge_keys", "stk_device_error",
     "stk_profile_begin", "stk_profile_end", "stk_exact_forward_noalloc", "stk_candidates_workspace_bytes",
+    "stk_exchange_bytes", "stk_exchange_create", "stk_exchange_ipc_handle", "stk_exchange_connect",
+    "stk_exchange_forward", "stk_exchange_destroy",
 )
+IPC_HANDLE_BYTES = 64
 
 _lib = None
 _lock = threading.Lock()
@@ -73,6 +76,18 @@ def load():
         L.stk_profile_end.argtypes = [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]
         L.stk_device_error.restype = i32
         L.stk_device_error.argtypes = [vp, ctypes.POINTER(ctypes.c_uint)]
+        L.stk_exchange_bytes.restype = i32
+        L.stk_exchange_bytes.argtypes = [i32, i64, i64, ctypes.POINTER(sz)]
+        L.stk_exchange_create.restype = i32
+        L.stk_exchange_create.argtypes = [i32, i32, i64, i64, vp, sz, ctypes.c_double, ctypes.POINTER(vp)]
+        L.stk_exchange_ipc_handle.restype = i32
+        L.stk_exchange_ipc_handle.argtypes = [vp, vp, ctypes.POINTER(i64)]
+        L.stk_exchange_connect.restype = i32
+        L.stk_exchange_connect.argtypes = [vp, vp, vp]
+        L.stk_exchange_forward.restype = i32
+        L.stk_exchange_forward.argtypes = [vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32, vp, sz, vp]
+        L.stk_exchange_destroy.restype = i32
+        L.stk_exchange_destroy.argtypes = [vp]
         _lib = L
     return _lib
 
@@ -107,7 +122,7 @@ def device_error(stream_handle: int) -> int:
     return int(code.value)
 
 
-PROFILE_KINDS = ("fused_topk_kernel", "simt_topk_kernel", "merge_lists_kernel", "unused")
+PROFILE_KINDS = ("fused_topk_kernel", "simt_topk_kernel", "merge_lists_kernel", "exchange_kernels")
 
 
 class KernelTimer:

@@ -11,6 +11,13 @@ Each rank holds the contiguous feature range [f0, f1) of W_enc / b_enc
      group (NCCL over NVLink on B200; gloo works for host-side tests).
   3. ``stk_merge_keys`` on every rank: top-k of world * L keys per row.
 
+With ``transport="p2p"`` steps 2-3 run as two library kernels instead
+(``PeerExchange``, C ABI stk_exchange_*): a publish kernel merges the local
+lists and stores each row's keys straight into every rank's receive buffer
+(CUDA IPC mappings, peer stores over NVLink) and bumps that rank's arrival
+counter; the final merge waits (bounded) for all ranks' rows and merges.  No
+NCCL call and no host involvement per step.
+
 Keys order by (score desc, feature index asc), so the result is identical to
 the single-GPU encode for any world size.  The reference has no multi-GPU
 path; the shard / all-gather / merge scheme follows BASELINE.json's north
@@ -18,6 +25,8 @@ star.  The kernels are pluggable (``shard_fn`` / ``merge_fn``) so that the
 collective plumbing can be tested on CPU ranks with gloo.
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -62,6 +71,65 @@ def _cuda_merge_fn(gathered, k):
     return V, I
 
 
+class PeerExchange:
+    """One rank's receive buffer of the direct GPU-to-GPU exchange.
+
+    Collective: every rank of `group` constructs it with the same max_rows and
+    k (the IPC handles are all-gathered over the group).  ``forward`` runs the
+    shard's scores + top-k, the publish kernel and the final merge on the
+    current stream.  ``close()`` (collective) unmaps the peers' buffers.
+    """
+
+    def __init__(self, max_rows, k, device, group=None, wait_seconds=10.0):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.max_rows, self.k, self.device = int(max_rows), int(k), torch.device(device)
+        lib = _capi.load()
+        nbytes = ctypes.c_size_t(0)
+        _capi.check(lib.stk_exchange_bytes(self.world, self.max_rows, self.k, ctypes.byref(nbytes)))
+        self.handle = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            self.buf = torch.empty(int(nbytes.value), dtype=torch.uint8, device=self.device)
+            _capi.check(lib.stk_exchange_create(self.rank, self.world, self.max_rows, self.k, self.buf.data_ptr(),
+                                                int(nbytes.value), float(wait_seconds), ctypes.byref(self.handle)))
+            ipc = (ctypes.c_char * _capi.IPC_HANDLE_BYTES)()
+            off = ctypes.c_int64(0)
+            _capi.check(lib.stk_exchange_ipc_handle(self.handle, ipc, ctypes.byref(off)))
+        mine = (bytes(ipc), int(off.value))
+        every = [None] * self.world
+        dist.all_gather_object(every, mine, group=group)
+        handles = b"".join(h for h, _ in every)
+        offsets = (ctypes.c_int64 * self.world)(*[o for _, o in every])
+        with torch.cuda.device(self.device):
+            _capi.check(lib.stk_exchange_connect(self.handle, handles, offsets))
+
+    def forward(self, X, W_shard, b_shard, f_offset, V, I):
+        B, d = X.shape
+        Fs = W_shard.shape[0]
+        lib = _capi.load()
+        with torch.cuda.device(self.device):
+            nbytes = _capi.workspace_bytes(B, d, Fs, self.k, _DTYPE_CODE[X.dtype]) if Fs > 0 else 0
+            ws = torch.empty(max(nbytes, 8), dtype=torch.uint8, device=self.device)
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+            _capi.check(lib.stk_exchange_forward(self.handle, X.data_ptr(), W_shard.data_ptr(), b_shard.data_ptr(),
+                                                 V.data_ptr(), I.data_ptr(), B, d, Fs, self.k, f_offset,
+                                                 _DTYPE_CODE[X.dtype], _capi.STK_FLAG_ANY_K | _capi.STK_FLAG_ANY_D,
+                                                 ws.data_ptr(), nbytes, stream))
+        return V, I
+
+    def close(self):
+        if self.handle is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        rc = _capi.load().stk_exchange_destroy(self.handle)
+        self.handle = None
+        dist.barrier(group=self.group)
+        self.buf = None
+        _capi.check(rc)
+
+
 class ShardedEncoder:
     """F-sharded exact (or approx, c >= k) top-k encoder for one rank.
 
@@ -72,8 +140,11 @@ class ShardedEncoder:
     """
 
     def __init__(self, W_shard, b_shard, F_total, f_offset, k, group=None, mode="exact", c=None,
-                 shard_fn=None, merge_fn=None):
+                 shard_fn=None, merge_fn=None, transport="nccl", max_rows=128):
         k = int(k)
+        _require(transport in ("nccl", "p2p"), "transport must be 'nccl' or 'p2p'")
+        _require(transport == "nccl" or (shard_fn is None and merge_fn is None),
+                 "transport 'p2p' runs the library kernels only")
         _require(1 <= k <= 128, "k out of range")
         _require(mode in ("exact", "approx"), "mode must be 'exact' or 'approx'")
         if mode == "approx":
@@ -92,12 +163,35 @@ class ShardedEncoder:
         self.L = _capi.list_len(k) if shard_fn is None else (32 if k <= 32 else 64 if k <= 64 else 128)
         self.shard_fn = shard_fn or _cuda_shard_fn
         self.merge_fn = merge_fn or _cuda_merge_fn
+        self.transport = transport if self.world > 1 else "nccl"
+        self.max_rows = int(max_rows)
+        self.exchange = None
+
+    def _peer_exchange(self, B, device):
+        if self.exchange is not None and self.exchange.max_rows < B:
+            self.exchange.close()
+            self.exchange = None
+        if self.exchange is None:
+            self.exchange = PeerExchange(max(B, self.max_rows), self.k, device, group=self.group)
+        return self.exchange
+
+    def close(self):
+        """Release the p2p exchange (collective); a no-op for the NCCL transport."""
+        if self.exchange is not None:
+            self.exchange.close()
+            self.exchange = None
 
     def encode(self, X):
         X = X.contiguous()
         _require(X.dim() == 2 and X.shape[1] == self.W.shape[1], "W_enc d-dim mismatch")
         _require(X.dtype == self.W.dtype, "W_enc dtype must match X")
         B = X.shape[0]
+        if self.transport == "p2p":
+            V = torch.empty((B, self.k), dtype=torch.float32, device=X.device)
+            I = torch.empty((B, self.k), dtype=torch.int32, device=X.device)
+            if B == 0:
+                return V, I
+            return self._peer_exchange(B, X.device).forward(X, self.W, self.b, self.f_offset, V, I)
         keys = torch.empty((B, self.L), dtype=torch.int64, device=X.device)
         if self.W.shape[0] > 0:
             self.shard_fn(X, self.W, self.b, self.k, self.f_offset, keys)
@@ -113,5 +207,5 @@ class ShardedEncoder:
 
 
 def topk_sae_cuda_exact_sharded(X, W_shard, b_shard, k, F_total, f_offset, group=None):
-    """One-shot sharded exact encode (see ShardedEncoder)."""
+    """One-shot sharded exact encode over NCCL (see ShardedEncoder)."""
     return ShardedEncoder(W_shard, b_shard, F_total, f_offset, k, group=group).encode(X)

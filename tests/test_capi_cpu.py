@@ -66,3 +66,39 @@ def test_ops_fail_loudly_without_library(monkeypatch, tmp_path):
     monkeypatch.setattr(_capi, "LIB_PATH", str(tmp_path / "missing.so"))
     with pytest.raises(_capi.NativeLibraryMissing):
         _capi.load()
+
+
+def test_exchange_sizes_and_argument_checks():
+    """stk_exchange_*: sizes and argument errors that need no GPU."""
+    import ctypes
+    lib = _capi.load()
+    n = ctypes.c_size_t(0)
+    assert lib.stk_exchange_bytes(2, 128, 64, ctypes.byref(n)) == _capi.STK_OK
+    # receive slots [2][world][rows][L] of int64 keys, counters, step state
+    assert n.value >= 2 * 2 * 128 * 64 * 8 + 2 * 2 * 8 + 16
+    m = ctypes.c_size_t(0)
+    assert lib.stk_exchange_bytes(8, 128, 128, ctypes.byref(m)) == _capi.STK_OK and m.value > n.value
+    assert lib.stk_exchange_bytes(9, 128, 64, ctypes.byref(n)) == _capi.STK_EINVAL
+    assert "world must be in [1, 8]" in lib.stk_last_error().decode()
+    assert lib.stk_exchange_bytes(2, 128, 129, ctypes.byref(n)) == _capi.STK_EINVAL
+    h = ctypes.c_void_p()
+    assert lib.stk_exchange_create(2, 2, 128, 64, None, 0, 1.0, ctypes.byref(h)) == _capi.STK_EINVAL
+    assert "rank out of range" in lib.stk_last_error().decode()
+    assert lib.stk_exchange_create(0, 2, 128, 64, None, 0, 0.0, ctypes.byref(h)) == _capi.STK_EINVAL
+    assert lib.stk_exchange_create(0, 2, 128, 64, None, 0, 1.0, ctypes.byref(h)) == _capi.STK_ENOSPACE
+    assert "exchange buffer too small" in lib.stk_last_error().decode()
+    assert not h.value
+    assert lib.stk_exchange_forward(None, None, None, None, None, None, 4, 64, 128, 8, 0, _capi.STK_BF16, 0,
+                                    None, 0, None) == _capi.STK_EINVAL
+    assert lib.stk_exchange_destroy(None) == _capi.STK_OK
+
+
+def test_p2p_transport_rejects_custom_kernels():
+    import torch
+    from streamtopk_sae import shard
+    W = torch.zeros(128, 16)
+    b = torch.zeros(128)
+    with pytest.raises(RuntimeError, match="transport 'p2p' runs the library kernels only"):
+        shard.ShardedEncoder(W, b, 128, 0, 8, transport="p2p", shard_fn=lambda *a: None)
+    with pytest.raises(RuntimeError, match="transport must be"):
+        shard.ShardedEncoder(W, b, 128, 0, 8, transport="mpi")
