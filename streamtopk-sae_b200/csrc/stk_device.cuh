@@ -114,8 +114,11 @@ __device__ __forceinline__ void merge_desc(uint64_t (&a)[N]) {
 //
 // Layout (slot-major, row-minor, so the 32 threads of a warp touch 32
 // consecutive 8-byte words):
-//   top[s * kRows + r], s < L : row r's best L keys, descending (0 = empty),
-//                               shared memory
+//   top[s * kRows + (r ^ (s & 31))], s < L : row r's best L keys, descending
+//                               (0 = empty), shared memory.  The XOR swizzle
+//                               keeps per-thread access conflict-free and lets
+//                               a warp read one row's 32 consecutive slots in
+//                               2 wavefronts instead of 32 (store_partials).
 //   app[s * kRows + r], s < A : row r's unsorted survivors since the last
 //                               merge, in shared memory or (when shared
 //                               memory is short) in an L2-resident workspace
@@ -129,6 +132,11 @@ extern __shared__ __align__(16) uint8_t stk_smem[];
 
 __device__ __forceinline__ uint64_t* smem_keys(uint32_t off) { return reinterpret_cast<uint64_t*>(stk_smem + off); }
 
+// Slot s of row r in a swizzled top list at byte offset `top`.
+__device__ __forceinline__ uint64_t& top_slot(uint32_t top, int s, int r) {
+  return smem_keys(top)[s * kRows + (r ^ (s & 31))];
+}
+
 // Merge row r's n waiting survivors (A append slots, unsorted) into its sorted
 // top list and return the new threshold: the value of the (kth+1)-th best key,
 // never below floor_thr (a lower bound known from elsewhere, -inf if none).
@@ -139,7 +147,7 @@ template <int L, int A, bool APP_SMEM>
 __device__ __noinline__ float merge_survivors(uint32_t top_off, uint32_t app_off, const uint64_t* __restrict__ app_g,
                                               int r, int n, int kth, float floor_thr) {
   static_assert(A == 16 || A == 32, "append slots");
-  uint64_t* top = smem_keys(top_off) + r;  // top[s * kRows] is slot s of row r
+#define TOP(s) top_slot(top_off, (s), r)
   uint64_t a[A];
 #pragma unroll
   for (int s = 0; s < A; ++s) {
@@ -155,26 +163,26 @@ __device__ __noinline__ float merge_survivors(uint32_t top_off, uint32_t app_off
     // (a' = a padded with empty keys; only the last A positions change).
     uint64_t c[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) c[i] = top[i * kRows];
+    for (int i = 0; i < 32; ++i) c[i] = TOP(i);
 #pragma unroll
     for (int q = 0; q < A; ++q) c[32 - A + q] = kmax(c[32 - A + q], a[A - 1 - q]);
     merge_desc<32>(c);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) top[i * kRows] = c[i];
+    for (int i = 0; i < 32; ++i) TOP(i) = c[i];
   } else {
     // Only the last A positions can change in c[i] = max(top[i], a'[L-1-i]).
 #pragma unroll
-    for (int q = 0; q < A; ++q) top[(L - A + q) * kRows] = kmax(top[(L - A + q) * kRows], a[A - 1 - q]);
+    for (int q = 0; q < A; ++q) TOP(L - A + q) = kmax(TOP(L - A + q), a[A - 1 - q]);
     // Bitonic merge: strides >= 32 in shared memory, then 32-blocks in registers.
 #pragma unroll
     for (int stride = L >> 1; stride >= 32; stride >>= 1) {
 #pragma unroll 16
       for (int i = 0; i < L; ++i) {
         if ((i & stride) == 0) {
-          uint64_t x = top[i * kRows], y = top[(i + stride) * kRows];
+          uint64_t x = TOP(i), y = TOP(i + stride);
           cx(x, y);
-          top[i * kRows] = x;
-          top[(i + stride) * kRows] = y;
+          TOP(i) = x;
+          TOP(i + stride) = y;
         }
       }
     }
@@ -182,13 +190,14 @@ __device__ __noinline__ float merge_survivors(uint32_t top_off, uint32_t app_off
     for (int blk = 0; blk < L / 32; ++blk) {
       uint64_t c[32];
 #pragma unroll
-      for (int q = 0; q < 32; ++q) c[q] = top[(blk * 32 + q) * kRows];
+      for (int q = 0; q < 32; ++q) c[q] = TOP(blk * 32 + q);
       merge_desc<32>(c);
 #pragma unroll
-      for (int q = 0; q < 32; ++q) top[(blk * 32 + q) * kRows] = c[q];
+      for (int q = 0; q < 32; ++q) TOP(blk * 32 + q) = c[q];
     }
   }
-  const uint64_t kk = top[kth * kRows];
+  const uint64_t kk = TOP(kth);
+#undef TOP
   return kk ? fmaxf(key_value(kk), floor_thr) : floor_thr;
 }
 
@@ -213,7 +222,7 @@ struct RowTopK {
     floor_thr = thr;
     kth = k - 1;
 #pragma unroll 4
-    for (int s = 0; s < L; ++s) smem_keys(top)[s * kRows + r] = kEmptyKey;
+    for (int s = 0; s < L; ++s) top_slot(top, s, r) = kEmptyKey;
   }
 
   __device__ __forceinline__ void flush() {

@@ -72,7 +72,7 @@ __device__ __forceinline__ void store_partials(uint32_t top, uint64_t* __restric
     const int r = warp_row0 + rr;
 #pragma unroll
     for (int e = 0; e < L / 32; ++e)
-      out_unit[(int64_t)r * L + e * 32 + lane] = smem_keys(top)[(e * 32 + lane) * kRows + r];
+      out_unit[(int64_t)r * L + e * 32 + lane] = top_slot(top, e * 32 + lane, r);
   }
   __syncwarp();
 }
@@ -363,11 +363,20 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           const int64_t f = cur.ft + 32 * c;
           const float bl = pick<NT / 32>(bcur, c);
           const uint32_t valid = row_ok ? feature_mask(f, p.F) : 0u;
+          // Histogram the maximum of each group of kPilotGroup scores: they
+          // are real scores of distinct features, so the k-th largest of them
+          // still bounds the row's k-th score from below, at 1/kPilotGroup of
+          // the global atomics of histogramming every sample.
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float vj = __uint_as_float(v[j]) + __shfl_sync(0xffffffffu, bl, j);
-            if (valid & (1u << j)) {
-              const uint32_t bin = float_order(vj) >> (32 - kPilotBits);
+          for (int g0 = 0; g0 < 32; g0 += kPilotGroup) {
+            float gm = -__int_as_float(0x7f800000);
+#pragma unroll
+            for (int j = g0; j < g0 + kPilotGroup; ++j) {
+              const float vj = __uint_as_float(v[j]) + __shfl_sync(0xffffffffu, bl, j);
+              if (valid & (1u << j)) gm = fmaxf(gm, vj);
+            }
+            if ((valid >> g0) & ((1u << kPilotGroup) - 1u)) {
+              const uint32_t bin = float_order(gm) >> (32 - kPilotBits);
               atomicAdd(h + bin, 1u);
               bmax = max(bmax, bin);
             }

@@ -26,12 +26,14 @@ struct UnitGrid {
 // in shared memory): [gridDim.x][kAppendMax][kRows] keys in the workspace.
 constexpr size_t kAppendBytesPerCta = (size_t)kAppendMax * kRows * 8;
 
-// Pilot threshold: every CTA histograms the scores of its first 32 features
-// per row (bins = top kPilotBits of the order-preserving key), the CTAs meet
-// at a bounded grid barrier, and each row starts with the lower edge of the
-// bin that holds its k-th largest sampled score as filter floor.
+// Pilot threshold: every CTA takes the scores of its first kPilotChunks * 32
+// features per row, histograms the maximum of each group of kPilotGroup of
+// them (bins = top kPilotBits of the order-preserving key), the CTAs meet at
+// a bounded grid barrier, and each row starts with the lower edge of the bin
+// that holds its k-th largest histogrammed score as filter floor.
 constexpr int kPilotBits = 12;
 constexpr int kPilotChunks = 2;  // sampled 32-feature chunks per CTA
+constexpr int kPilotGroup = 8;   // scores per histogrammed group maximum
 constexpr int kPilotBins = 1 << kPilotBits;
 constexpr unsigned long long kPilotWaitNs = 200000;  // give up (no floor) after 200 us
 
@@ -102,6 +104,9 @@ struct SimtCfg {
   X(32, 256, 4, 32, false)   \
   X(64, 256, 3, 16, true)    \
   X(64, 256, 3, 32, false)   \
+  X(64, 128, 4, 16, true)    \
+  X(64, 64, 6, 16, true)     \
+  X(32, 128, 5, 32, true)    \
   X(128, 256, 2, 32, false)  \
   X(128, 128, 3, 32, false)
 
