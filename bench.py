@@ -260,8 +260,6 @@ def config_dict(args, cfg):
                       (f", W_enc F-sharded over {args.gpus} GPUs" if args.gpus > 1 else "")),
          "B": cfg["B"], "d": cfg["d"], "F": cfg["F"], "k": cfg["k"], "global_batch": cfg["B"],
          "parallelism": f"F-shard{args.gpus}" if args.gpus > 1 else "single-gpu",
-         "exchange": (("direct peer stores over NVLink (stk_exchange_*)" if args.transport == "p2p" else
-                       "NCCL all_gather_into_tensor + merge kernel") if args.gpus > 1 else None),
          "l2": "inputs larger than L2: each rank streams >= 128 MiB of W_enc per step"}
     return d
 
@@ -447,6 +445,10 @@ def run_b200(args, cfg):
                     "path": ("streamtopk_sae.topk_sae_cuda_exact" if world == 1 else
                              "streamtopk_sae.shard.ShardedEncoder.encode in a CUDA graph (graph.CapturedEncode)")},
             "gpu_launches": launches, "graph_steps": G, "clocks": clk.summary(),
+            "exchange": (None if world == 1 else
+                         "direct peer stores over NVLink (stk_exchange_*)" if enc.transport in ("p2p", "auto") else
+                         "NCCL all_gather_into_tensor + merge kernel" +
+                         (f" (p2p unavailable: {enc.fallback_reason})" if enc.fallback_reason else "")),
             "kernel_ms_per_step": {kk: v / (args.steps if world == 1 else G) for kk, v in kt.ms.items()},
         }
         print(json.dumps(line), flush=True)
@@ -472,8 +474,9 @@ def main():
     ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS))
     ap.add_argument("--dtype", default=None, choices=["bf16", "fp16", "fp32"],
                     help="input dtype override (config 2 is a dtype sweep)")
-    ap.add_argument("--transport", default="p2p", choices=["p2p", "nccl"],
-                    help="N>1: cross-GPU exchange of the per-rank key lists")
+    ap.add_argument("--transport", default="auto", choices=["auto", "p2p", "nccl"],
+                    help="N>1: cross-GPU exchange of the per-rank key lists (auto: p2p, NCCL if the "
+                         "peer mappings cannot be set up)")
     ap.add_argument("--shape", default=None,
                     help="B,d,F,k override of the config's shape (small cases for ncu captures)")
     args = ap.parse_args()

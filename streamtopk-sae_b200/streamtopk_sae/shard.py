@@ -71,6 +71,10 @@ def _cuda_merge_fn(gathered, k):
     return V, I
 
 
+class PeerExchangeUnavailable(RuntimeError):
+    """Raised on every rank when some rank could not map its peers' buffers."""
+
+
 class PeerExchange:
     """One rank's receive buffer of the direct GPU-to-GPU exchange.
 
@@ -85,24 +89,53 @@ class PeerExchange:
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.max_rows, self.k, self.device = int(max_rows), int(k), torch.device(device)
-        lib = _capi.load()
-        nbytes = ctypes.c_size_t(0)
-        _capi.check(lib.stk_exchange_bytes(self.world, self.max_rows, self.k, ctypes.byref(nbytes)))
-        self.handle = ctypes.c_void_p()
-        with torch.cuda.device(self.device):
-            self.buf = torch.empty(int(nbytes.value), dtype=torch.uint8, device=self.device)
-            _capi.check(lib.stk_exchange_create(self.rank, self.world, self.max_rows, self.k, self.buf.data_ptr(),
-                                                int(nbytes.value), float(wait_seconds), ctypes.byref(self.handle)))
-            ipc = (ctypes.c_char * _capi.IPC_HANDLE_BYTES)()
-            off = ctypes.c_int64(0)
-            _capi.check(lib.stk_exchange_ipc_handle(self.handle, ipc, ctypes.byref(off)))
-        mine = (bytes(ipc), int(off.value))
+        self.handle = None
+        self.buf = None
+        # Each step may fail on some ranks only; the ranks always run the same
+        # collectives and decide together, so either every rank is connected
+        # or every rank raises PeerExchangeUnavailable.
+        mine, why = None, ""
+        try:
+            lib = _capi.load()
+            nbytes = ctypes.c_size_t(0)
+            _capi.check(lib.stk_exchange_bytes(self.world, self.max_rows, self.k, ctypes.byref(nbytes)))
+            handle = ctypes.c_void_p()
+            with torch.cuda.device(self.device):
+                self.buf = torch.empty(int(nbytes.value), dtype=torch.uint8, device=self.device)
+                _capi.check(lib.stk_exchange_create(self.rank, self.world, self.max_rows, self.k,
+                                                    self.buf.data_ptr(), int(nbytes.value), float(wait_seconds),
+                                                    ctypes.byref(handle)))
+                self.handle = handle
+                ipc = (ctypes.c_char * _capi.IPC_HANDLE_BYTES)()
+                off = ctypes.c_int64(0)
+                _capi.check(lib.stk_exchange_ipc_handle(self.handle, ipc, ctypes.byref(off)))
+            mine = (bytes(ipc), int(off.value))
+        except Exception as e:  # noqa: BLE001 - reported to every rank below
+            why = f"rank {self.rank}: {e}"
         every = [None] * self.world
-        dist.all_gather_object(every, mine, group=group)
-        handles = b"".join(h for h, _ in every)
-        offsets = (ctypes.c_int64 * self.world)(*[o for _, o in every])
-        with torch.cuda.device(self.device):
-            _capi.check(lib.stk_exchange_connect(self.handle, handles, offsets))
+        dist.all_gather_object(every, (mine, why), group=group)
+        if any(m is None for m, _ in every):
+            self._release()
+            raise PeerExchangeUnavailable(next(w for m, w in every if m is None))
+        ok = 1
+        try:
+            handles = b"".join(m[0] for m, _ in every)
+            offsets = (ctypes.c_int64 * self.world)(*[m[1] for m, _ in every])
+            with torch.cuda.device(self.device):
+                _capi.check(lib.stk_exchange_connect(self.handle, handles, offsets))
+        except Exception as e:  # noqa: BLE001
+            ok, why = 0, f"rank {self.rank}: {e}"
+        verdict = [None] * self.world
+        dist.all_gather_object(verdict, (ok, why), group=group)
+        if not all(v for v, _ in verdict):
+            self._release()
+            raise PeerExchangeUnavailable(next(w for v, w in verdict if not v))
+
+    def _release(self):
+        if self.handle is not None:
+            _capi.load().stk_exchange_destroy(self.handle)
+            self.handle = None
+        self.buf = None
 
     def forward(self, X, W_shard, b_shard, f_offset, V, I):
         B, d = X.shape
@@ -125,7 +158,7 @@ class PeerExchange:
         dist.barrier(group=self.group)
         rc = _capi.load().stk_exchange_destroy(self.handle)
         self.handle = None
-        dist.barrier(group=self.group)
+        dist.barrier(group=self.group)   # no rank frees its buffer while a peer still maps it
         self.buf = None
         _capi.check(rc)
 
@@ -142,8 +175,8 @@ class ShardedEncoder:
     def __init__(self, W_shard, b_shard, F_total, f_offset, k, group=None, mode="exact", c=None,
                  shard_fn=None, merge_fn=None, transport="nccl", max_rows=128):
         k = int(k)
-        _require(transport in ("nccl", "p2p"), "transport must be 'nccl' or 'p2p'")
-        _require(transport == "nccl" or (shard_fn is None and merge_fn is None),
+        _require(transport in ("nccl", "p2p", "auto"), "transport must be 'nccl', 'p2p' or 'auto'")
+        _require(transport != "p2p" or (shard_fn is None and merge_fn is None),
                  "transport 'p2p' runs the library kernels only")
         _require(1 <= k <= 128, "k out of range")
         _require(mode in ("exact", "approx"), "mode must be 'exact' or 'approx'")
@@ -166,13 +199,21 @@ class ShardedEncoder:
         self.transport = transport if self.world > 1 else "nccl"
         self.max_rows = int(max_rows)
         self.exchange = None
+        self.fallback_reason = None
 
     def _peer_exchange(self, B, device):
         if self.exchange is not None and self.exchange.max_rows < B:
             self.exchange.close()
             self.exchange = None
         if self.exchange is None:
-            self.exchange = PeerExchange(max(B, self.max_rows), self.k, device, group=self.group)
+            try:
+                self.exchange = PeerExchange(max(B, self.max_rows), self.k, device, group=self.group)
+            except PeerExchangeUnavailable as e:
+                if self.transport != "auto":
+                    raise
+                self.transport = "nccl"        # same decision on every rank (collective check)
+                self.fallback_reason = str(e)
+                return None
         return self.exchange
 
     def close(self):
@@ -186,12 +227,14 @@ class ShardedEncoder:
         _require(X.dim() == 2 and X.shape[1] == self.W.shape[1], "W_enc d-dim mismatch")
         _require(X.dtype == self.W.dtype, "W_enc dtype must match X")
         B = X.shape[0]
-        if self.transport == "p2p":
+        if self.transport in ("p2p", "auto"):
             V = torch.empty((B, self.k), dtype=torch.float32, device=X.device)
             I = torch.empty((B, self.k), dtype=torch.int32, device=X.device)
             if B == 0:
                 return V, I
-            return self._peer_exchange(B, X.device).forward(X, self.W, self.b, self.f_offset, V, I)
+            ex = self._peer_exchange(B, X.device)
+            if ex is not None:
+                return ex.forward(X, self.W, self.b, self.f_offset, V, I)
         keys = torch.empty((B, self.L), dtype=torch.int64, device=X.device)
         if self.W.shape[0] > 0:
             self.shard_fn(X, self.W, self.b, self.k, self.f_offset, keys)

@@ -64,7 +64,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, F, k, out_q):
+def _worker(rank, world, port, F, k, out_q, transport="nccl"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -74,8 +74,19 @@ def _worker(rank, world, port, F, k, out_q):
         W = torch.from_numpy(rng.standard_normal((F, 32)).astype(np.float32))
         b = torch.from_numpy(rng.standard_normal(F).astype(np.float32) * 0.1)
         f0, f1 = shard.shard_bounds(F, world, rank)
-        enc = shard.ShardedEncoder(W[f0:f1], b[f0:f1], F, f0, k, shard_fn=cpu_shard_fn, merge_fn=cpu_merge_fn)
+        if transport == "auto":
+            # The peer exchange cannot be set up without GPUs: every rank must
+            # reach the same verdict and fall back to the process-group path
+            # (here with the CPU stand-ins).
+            enc = shard.ShardedEncoder(W[f0:f1], b[f0:f1], F, f0, k, transport="auto")
+            enc.shard_fn, enc.merge_fn = cpu_shard_fn, cpu_merge_fn
+        else:
+            enc = shard.ShardedEncoder(W[f0:f1], b[f0:f1], F, f0, k, shard_fn=cpu_shard_fn, merge_fn=cpu_merge_fn)
         V, I = enc.encode(X)
+        if transport == "auto":
+            assert enc.transport == "nccl" and enc.fallback_reason, (enc.transport, enc.fallback_reason)
+            V2, I2 = enc.encode(X)     # later steps stay on the fallback path
+            assert torch.equal(V, V2) and torch.equal(I, I2)
         out_q.put((rank, V.numpy(), I.numpy()))
     except Exception as e:  # report instead of leaving the parent waiting
         out_q.put((rank, repr(e), None))
@@ -84,12 +95,13 @@ def _worker(rank, world, port, F, k, out_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,F,k", [(2, 1000, 16), (3, 700, 64), (2, 200, 128)])
-def test_sharded_matches_unsharded(world, F, k):
+@pytest.mark.parametrize("world,F,k,transport", [(2, 1000, 16, "nccl"), (3, 700, 64, "nccl"), (2, 200, 128, "nccl"),
+                                                 (2, 1000, 16, "auto"), (3, 700, 64, "auto")])
+def test_sharded_matches_unsharded(world, F, k, transport):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, F, k, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, F, k, q, transport)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=60) for _ in range(world)]
