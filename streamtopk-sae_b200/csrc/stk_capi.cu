@@ -232,9 +232,17 @@ bool fused_override(int L, int* nt, int* stages, int* app, int* app_smem) {
 
 int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint64_t* partials, uint64_t* app,
               int64_t B, int64_t d, int64_t F, int64_t k, int dtype, uint32_t index_offset, cudaStream_t stream) {
-  // Defaults: append slots in shared memory where 3 pipeline stages still fit.
-  int nt = 256;
-  int stages = pl.L == 128 ? 2 : 3;
+  // Defaults: 256-feature tiles, append slots in shared memory where 3
+  // pipeline stages still fit.  When a CTA's unit fits in one such tile (F
+  // small per CTA, e.g. one shard of a multi-GPU encode) 128-feature tiles
+  // are used instead: the epilogue of the first tile then overlaps the loads
+  // of the second, and the pilot barrier comes after half the loads.
+  const int64_t unit_feats =
+      32 * (pl.grid.fixed_chunks > 0 ? (int64_t)pl.grid.fixed_chunks
+                                     : (pl.grid.nchunks + pl.grid.segs - 1) / pl.grid.segs);
+  const bool narrow = unit_feats <= 256;
+  int nt = narrow ? 128 : 256;
+  int stages = narrow ? (pl.L == 128 ? 3 : pl.L == 64 ? 4 : 5) : (pl.L == 128 ? 2 : 3);
   int nslots = pl.L == 64 ? 16 : 32;
   int app_smem = pl.L == 128 ? 0 : 1;
   fused_override(pl.L, &nt, &stages, &nslots, &app_smem);

@@ -201,6 +201,20 @@ __device__ __noinline__ float merge_survivors(uint32_t top_off, uint32_t app_off
   return kk ? fmaxf(key_value(kk), floor_thr) : floor_thr;
 }
 
+// vals[j & 31] for a per-lane (divergent) j, by a 5-level select tree.
+__device__ __forceinline__ float pick32(const float (&vals)[32], int j) {
+  float t16[16], t8[8], t4[4], t2[2];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) t16[i] = (j & 16) ? vals[i + 16] : vals[i];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) t8[i] = (j & 8) ? t16[i + 8] : t16[i];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) t4[i] = (j & 4) ? t8[i + 4] : t8[i];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) t2[i] = (j & 2) ? t4[i + 2] : t4[i];
+  return (j & 1) ? t2[1] : t2[0];
+}
+
 template <int L, int A, bool APP_SMEM>
 struct RowTopK {
   uint32_t top;     // byte offset of top[0] from stk_smem
@@ -243,6 +257,9 @@ struct RowTopK {
   // must call this together: a merge runs for every lane as soon as one lane
   // would overflow its append slots.  A chunk may bring more survivors than
   // A, so the chunk is taken in (at most 32 / A) passes of A candidates.
+  // Survivors are rare once a threshold is known, so the warp loops once per
+  // survivor of its busiest lane; each lane takes its lowest pending survivor
+  // (value picked from registers by a select tree, no divergent branches).
   __device__ __forceinline__ void offer(const float (&vals)[32], uint32_t f0, uint32_t valid_mask) {
     uint32_t mask = 0;
 #pragma unroll
@@ -250,26 +267,21 @@ struct RowTopK {
     mask &= valid_mask;
 #pragma unroll
     for (int part = 0; part < 32 / A; ++part) {
-      const uint32_t pmask = mask & (A == 32 ? 0xffffffffu : (0xffffu << (16 * part)));
-      if (__any_sync(0xffffffffu, cnt + __popc(pmask) > A)) {
+      const uint32_t pm = A == 32 ? 0xffffffffu : (0xffffu << (16 * part));
+      if (__any_sync(0xffffffffu, cnt + __popc(mask & pm) > A)) {
         flush();
         mask = 0;
 #pragma unroll
         for (int j = 0; j < 32; ++j) mask |= (vals[j] > thr) ? (1u << j) : 0u;
         mask &= valid_mask;
       }
-      const uint32_t m = mask & (A == 32 ? 0xffffffffu : (0xffffu << (16 * part)));
-      if (m) {
-#pragma unroll
-        for (int g = (A == 32 ? 0 : 2 * part); g < (A == 32 ? 4 : 2 * part + 2); ++g) {
-          if ((m >> (8 * g)) & 0xffu) {
-#pragma unroll
-            for (int jj = 0; jj < 8; ++jj) {
-              const int j = 8 * g + jj;
-              if (m & (1u << j)) push(make_key(vals[j], f0 + uint32_t(j)));
-            }
-          }
-        }
+      uint32_t m = mask & pm;
+      while (__any_sync(0xffffffffu, m != 0u)) {
+        const bool has = m != 0u;
+        const int j = __ffs(m) - 1;  // -1 (ignored) when this lane has none
+        m &= m - 1u;
+        const float v = pick32(vals, j);
+        if (has) push(make_key(v, f0 + uint32_t(j)));
       }
     }
   }

@@ -120,25 +120,47 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
 // the lower edge of the highest bin at which the count from the top reaches
 // k.  Returns false when fewer than k samples lie within 256 bins of the top.
 __device__ __forceinline__ bool pilot_bound(const uint32_t* __restrict__ hist, uint32_t top_bin, int k, float& lb) {
-  uint32_t total = 0;
-#pragma unroll 1
-  for (int round = 0; round < 8; ++round) {
-    uint32_t c[32];
+  // First look: the 64 bins ending at the 4-aligned group that holds top_bin,
+  // fetched as 16 independent 16-byte loads (one memory round trip), scanned
+  // from top_bin down with predicated adds.
+  const int hi = (int)(top_bin | 3u);
+  const int base = hi - 63;
+  uint32_t c[64];
 #pragma unroll
-    for (int q = 0; q < 32; ++q) {
-      const int bin = (int)top_bin - 32 * round - q;
-      c[q] = bin >= 0 ? __ldcg(hist + bin) : 0u;
-    }
+  for (int q = 0; q < 16; ++q) {
+    uint4 t = make_uint4(0u, 0u, 0u, 0u);
+    if (base + 4 * q >= 0) t = __ldcg(reinterpret_cast<const uint4*>(hist + base + 4 * q));
+    c[4 * q + 0] = t.x;
+    c[4 * q + 1] = t.y;
+    c[4 * q + 2] = t.z;
+    c[4 * q + 3] = t.w;
+  }
+  uint32_t total = 0;
+  int found = -1;
+#pragma unroll
+  for (int q = 63; q >= 0; --q) {
+    const bool in = base + q <= (int)top_bin;
+    total += in ? c[q] : 0u;
+    if (found < 0 && total >= (uint32_t)k) found = base + q;
+  }
+  if (found >= 0) {
+    lb = order_float((uint32_t)found << (32 - kPilotBits));
+    return true;
+  }
+  // Rare: the k-th sampled score lies deeper; continue 32 bins at a time.
+#pragma unroll 1
+  for (int round = 0; round < 6 && base - 32 * round > 0; ++round) {
+    const int b0 = base - 1 - 32 * round;  // scan b0, b0 - 1, ...
+#pragma unroll
+    for (int q = 0; q < 32; ++q) c[q] = b0 - q >= 0 ? __ldcg(hist + b0 - q) : 0u;
 #pragma unroll
     for (int q = 0; q < 32; ++q) {
       total += c[q];
       if (total >= (uint32_t)k) {
-        const uint32_t bin = top_bin - 32 * round - q;
-        lb = order_float(bin << (32 - kPilotBits));
+        lb = order_float((uint32_t)(b0 - q) << (32 - kPilotBits));
         return true;
       }
     }
-    if ((int)top_bin - 32 * round - 31 <= 0) break;
   }
   return false;
 }
