@@ -418,7 +418,7 @@ def run_b200(args, cfg):
         per_launch = alg_bytes(B, d, Fs, k, cfg["dtype"])
         achieved = per_launch / (fused_avg_ms / 1e3) / 1e9
         roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                "traffic": profiled_traffic(args.config, world),
+                "traffic": (None if args.shape else profiled_traffic(args.config, world)),
                 "kernel": "fused_topk_kernel", "kernel_ms": fused_avg_ms,
                 "algorithmic_bytes_per_launch": per_launch,
                 "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else "fallback"}
@@ -427,13 +427,13 @@ def run_b200(args, cfg):
         achieved = flops / (fused_avg_ms / 1e3) / 1e12
         peak = tf_sus
         roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                "traffic": profiled_traffic(args.config, world), "kernel": "fused_topk_kernel",
+                "traffic": (None if args.shape else profiled_traffic(args.config, world)), "kernel": "fused_topk_kernel",
                 "kernel_ms": fused_avg_ms, "algorithmic_flops_per_launch": flops,
                 "peak_source": f"{src} bf16_tflops_sustained (fp16 assumed equal)"}
 
     line = None
     if rank == 0:
-        cpu = time_reference_single(cfg) if world == 1 else None
+        cpu = time_reference_single(cfg) if world == 1 and not args.no_cpu_baseline else None
         line = {
             "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": el_ms / args.steps, "higher_is_better": True,
@@ -474,6 +474,8 @@ def main():
     ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS))
     ap.add_argument("--dtype", default=None, choices=["bf16", "fp16", "fp32"],
                     help="input dtype override (config 2 is a dtype sweep)")
+    ap.add_argument("--no-cpu-baseline", action="store_true",
+                    help="omit the timed CPU sample (profiling runs)")
     ap.add_argument("--transport", default="auto", choices=["auto", "p2p", "nccl"],
                     help="N>1: cross-GPU exchange of the per-rank key lists (auto: p2p, NCCL if the "
                          "peer mappings cannot be set up)")
