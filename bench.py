@@ -345,21 +345,32 @@ def run_b200(args, cfg):
         # iteration replays a CUDA graph of G encode steps (memset, kernels and
         # the peer-store exchange, or the NCCL all-gather), as a serving loop
         # would.
+        # The timed graph holds no profiling events (they would sit between
+        # programmatically dependent kernels); a second, instrumented graph of
+        # the same G steps gives the per-kernel durations afterwards.
         G = next(g for g in (8, 4, 2, 1) if args.steps % g == 0)
-        with _capi.KernelTimer(max_launches=G * 4 + 16) as kt:
-            timed = CapturedEncode(step, X, steps=G, warmup=0)   # event nodes around each library kernel
-            barrier()
+        timed = CapturedEncode(step, X, steps=G, warmup=0)
+        barrier()
+        torch.cuda.synchronize(dev)
+        with ClockSampler(local) as clk:
+            e0.record(stream)
+            for _ in range(args.steps // G):
+                timed.replay()
+            e1.record(stream)
             torch.cuda.synchronize(dev)
-            with ClockSampler(local) as clk:
-                e0.record(stream)
-                for _ in range(args.steps // G):
-                    timed.replay()
-                e1.record(stream)
-                torch.cuda.synchronize(dev)
+        barrier()
+        el_ms = e0.elapsed_time(e1)
+        timed.close()
+        del timed
+        with _capi.KernelTimer(max_launches=G * 4 + 16) as kt:
+            inst = CapturedEncode(step, X, steps=G, warmup=0)   # event nodes around each library kernel
             barrier()
-            el_ms = e0.elapsed_time(e1)
-            timed.close()
-            del timed
+            for _ in range(4):
+                inst.replay()
+            torch.cuda.synchronize(dev)
+            barrier()
+            inst.close()
+            del inst
         # kt holds the G steps of the last replay (event nodes re-record per replay)
         launches = sum(kt.launches.values()) // G * args.steps
     assert _capi.device_error(stream.cuda_stream) == 0

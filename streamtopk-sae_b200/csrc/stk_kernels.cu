@@ -672,6 +672,9 @@ __global__ void __launch_bounds__(kMergeWarps * 32) publish_kernel(const uint64_
                                                                     const ExchangeDev ex) {
   __shared__ uint64_t red[kMergeWarps][L];
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // The final merge (launched as this grid's programmatic dependent) may now
+  // be scheduled: it synchronises on the arrival counters, not on this grid.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int64_t b = blockIdx.x;
   if (b >= rows) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -790,8 +793,18 @@ template <int L>
 cudaError_t launch_exchange_merge(const ExchangeDev& ex, int64_t rows, int k, float* V, int32_t* I,
                                   cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
-  exchange_merge_kernel<L><<<(unsigned)rows, kMergeWarps * 32, 0, stream>>>(ex, rows, k, V, I);
-  return cudaGetLastError();
+  // Programmatic dependent of the publish kernel: all publish CTAs are
+  // resident (or done) before any of these CTAs starts spinning.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)rows);
+  cfg.blockDim = dim3(kMergeWarps * 32);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, exchange_merge_kernel<L>, ex, rows, k, V, I);
 }
 
 template <int L>
