@@ -714,9 +714,9 @@ int stk_exchange_forward(stk_exchange* x, const void* X, const void* W_shard, co
   {
     ProfScope prof(kProfExchange, s);
     e = cudaErrorInvalidValue;
-    if (x->L == 32) e = stk::launch_publish<32>(partials, nlists, stride, B, x->dev, s);
-    if (x->L == 64) e = stk::launch_publish<64>(partials, nlists, stride, B, x->dev, s);
-    if (x->L == 128) e = stk::launch_publish<128>(partials, nlists, stride, B, x->dev, s);
+    if (x->L == 32) e = stk::launch_publish<32>(partials, nlists, stride, B, (int)k, x->dev, s);
+    if (x->L == 64) e = stk::launch_publish<64>(partials, nlists, stride, B, (int)k, x->dev, s);
+    if (x->L == 128) e = stk::launch_publish<128>(partials, nlists, stride, B, (int)k, x->dev, s);
     if (e != cudaSuccess) return cuda_fail(e, "publish_kernel launch");
     if (x->L == 32) e = stk::launch_exchange_merge<32>(x->dev, B, (int)k, V, I, s);
     if (x->L == 64) e = stk::launch_exchange_merge<64>(x->dev, B, (int)k, V, I, s);

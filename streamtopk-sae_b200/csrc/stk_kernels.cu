@@ -640,23 +640,135 @@ __device__ __forceinline__ void write_row(const uint64_t (&acc)[L / 32], int64_t
 }
 
 // ---------------------------------------------------------------------------
+// Select merge of one row.  The lists of the score kernel's units are sparse
+// (every key passed the row's threshold floor, most lists hold a few keys), so
+// instead of folding all of them:
+//  1. tau = the k-th largest list head: the k largest heads are k distinct
+//     keys, so the row's k-th key is >= tau (tau = 1, every key, when fewer
+//     than k lists are non-empty);
+//  2. every key >= tau is gathered into shared memory (a list whose head is
+//     below tau is skipped; a list is read until its first 32-key chunk that
+//     is not all >= tau) -- ~1.3 k candidates per row on Gaussian data;
+//  3. each candidate's rank is the number of larger candidates (keys are
+//     distinct), which is also its position in the row's sorted result.
+// More than kSelectCap candidates or lists: the caller folds instead.
+// ---------------------------------------------------------------------------
+constexpr int kSelectCap = kMergeWarps * 32;
+
+template <int L>
+struct MergeSmem {
+  uint64_t red[kMergeWarps][L];  // fold_row (fallback)
+  uint64_t heads[kSelectCap];
+  uint64_t cand[kSelectCap];
+  uint64_t tau;
+  int cnt;
+};
+
+// Returns the number of candidates (in sm.cand, unsorted), or -1 when the row
+// must be folded instead.  All threads of the CTA must call it.
+template <int L>
+__device__ __forceinline__ int select_candidates(const uint64_t* __restrict__ lists, int nlists, int64_t list_stride,
+                                                 int64_t b, int k, MergeSmem<L>& sm, int tid, int warp, int lane) {
+  if (nlists > kSelectCap) return -1;
+  if (tid == 0) {
+    sm.tau = 1ull;
+    sm.cnt = 0;
+  }
+  if (tid < nlists)
+    sm.heads[tid] = (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(lists + ((int64_t)tid * list_stride + b) * L));
+  __syncthreads();
+  if (tid < nlists) {
+    const uint64_t h = sm.heads[tid];
+    if (h != 0ull) {
+      int r = 0;
+      for (int j = 0; j < nlists; ++j) r += sm.heads[j] > h ? 1 : 0;
+      if (r == k - 1) sm.tau = h;
+    }
+  }
+  __syncthreads();
+  const uint64_t tau = sm.tau;
+  for (int s0 = warp; s0 < nlists; s0 += kMergeWarps * kMergeBatch) {
+    uint64_t buf[kMergeBatch];
+#pragma unroll
+    for (int q = 0; q < kMergeBatch; ++q) {
+      const int s = s0 + q * kMergeWarps;
+      buf[q] = (s < nlists && sm.heads[s] >= tau)
+                   ? (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(
+                         lists + ((int64_t)s * list_stride + b) * L + lane))
+                   : 0ull;
+    }
+#pragma unroll
+    for (int q = 0; q < kMergeBatch; ++q) {
+      const int s = s0 + q * kMergeWarps;
+      if (s >= nlists || sm.heads[s] < tau) continue;  // warp-uniform
+      const uint64_t* ps = lists + ((int64_t)s * list_stride + b) * L;
+      uint64_t key = buf[q];
+      for (int e = 0;;) {
+        const bool take = key >= tau;
+        const unsigned m = __ballot_sync(0xffffffffu, take);
+        int base = 0;
+        if (lane == 0 && m != 0u) base = atomicAdd(&sm.cnt, __popc(m));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if (take) {
+          const int pos = base + __popc(m & ((1u << lane) - 1u));
+          if (pos < kSelectCap) sm.cand[pos] = key;
+        }
+        if (m != 0xffffffffu || ++e == L / 32) break;  // sorted: the next chunk holds smaller keys
+        key = (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(ps + e * 32 + lane));
+      }
+    }
+  }
+  __syncthreads();
+  const int C = sm.cnt;
+  return C > kSelectCap ? -1 : C;
+}
+
+// Position of `key` in the descending order of the C distinct candidates.
+__device__ __forceinline__ int candidate_rank(const uint64_t* cand, int C, uint64_t key) {
+  int r = 0;
+  for (int j = 0; j < C; ++j) r += cand[j] > key ? 1 : 0;
+  return r;
+}
+
+// ---------------------------------------------------------------------------
 // Merge kernel: one CTA (16 warps) per row.  Launched with programmatic
 // dependent launch after the score kernel: griddepcontrol.wait blocks until
 // that grid has completed and its writes are visible (a no-op otherwise).
+// Writes the row's top k (V, I) and, if keys_out, its best keys in slots
+// [0, L) (the top min(L, #candidates), then empty keys: at least the top k).
 // ---------------------------------------------------------------------------
 template <int L>
 __global__ void __launch_bounds__(kMergeWarps * 32) merge_lists_kernel(const uint64_t* __restrict__ lists, int nlists,
                                                                         int64_t list_stride, int64_t rows, int k,
                                                                         float* __restrict__ V, int32_t* __restrict__ I,
                                                                         uint64_t* __restrict__ keys_out) {
-  __shared__ uint64_t red[kMergeWarps][L];
+  __shared__ MergeSmem<L> sm;
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int64_t b = blockIdx.x;
   if (b >= rows) return;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint64_t acc[L / 32];
-  fold_row<L>(lists, nlists, list_stride, b, acc, red, warp, lane);
-  if (warp == 0) write_row<L>(acc, b, k, V, I, keys_out, lane);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int C = select_candidates<L>(lists, nlists, list_stride, b, k, sm, tid, warp, lane);
+  if (C < 0) {
+    uint64_t acc[L / 32];
+    fold_row<L>(lists, nlists, list_stride, b, acc, sm.red, warp, lane);
+    if (warp == 0) write_row<L>(acc, b, k, V, I, keys_out, lane);
+    return;
+  }
+  if (tid < C) {
+    const uint64_t key = sm.cand[tid];
+    const int r = candidate_rank(sm.cand, C, key);
+    if (r < k) {
+      V[b * k + r] = key_value(key);
+      I[b * k + r] = key_index(key);
+    }
+    if (keys_out && r < L) keys_out[b * L + r] = key;
+  } else {
+    if (tid < k) {
+      V[b * k + tid] = -3.402823466e+38f;
+      I[b * k + tid] = -1;
+    }
+    if (keys_out && tid < L) keys_out[b * L + tid] = 0ull;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -668,9 +780,9 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_lists_kernel(const uin
 // ---------------------------------------------------------------------------
 template <int L>
 __global__ void __launch_bounds__(kMergeWarps * 32) publish_kernel(const uint64_t* __restrict__ lists, int nlists,
-                                                                    int64_t list_stride, int64_t rows,
+                                                                    int64_t list_stride, int64_t rows, int k,
                                                                     const ExchangeDev ex) {
-  __shared__ uint64_t red[kMergeWarps][L];
+  __shared__ MergeSmem<L> sm;
   asm volatile("griddepcontrol.wait;" ::: "memory");
   // The final merge (launched as this grid's programmatic dependent) may now
   // be scheduled: it synchronises on the arrival counters, not on this grid.
@@ -680,8 +792,24 @@ __global__ void __launch_bounds__(kMergeWarps * 32) publish_kernel(const uint64_
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const unsigned long long step = *reinterpret_cast<volatile unsigned long long*>(ex.state);
   const int slot = (int)(step & 1ull);
-  uint64_t acc[L / 32];
-  fold_row<L>(lists, nlists, list_stride, b, acc, red, warp, lane);  // ends with red[0] = the row's list
+  // The row's list into sm.red[0]: its top min(L, #candidates) keys, then empty
+  // keys (at least the top k, which is all the final merge needs).
+  const int tid = threadIdx.x;
+  const int C = select_candidates<L>(lists, nlists, list_stride, b, k, sm, tid, warp, lane);
+  if (C < 0) {
+    uint64_t acc[L / 32];
+    fold_row<L>(lists, nlists, list_stride, b, acc, sm.red, warp, lane);  // ends with red[0] = the row's list
+  } else {
+    if (tid < C) {
+      const uint64_t key = sm.cand[tid];
+      const int r = candidate_rank(sm.cand, C, key);
+      if (r < L) sm.red[0][r] = key;
+    } else if (tid < L) {
+      sm.red[0][tid] = 0ull;
+    }
+    __syncthreads();
+  }
+  uint64_t (&red)[kMergeWarps][L] = sm.red;
   if (warp < ex.world) {
     uint64_t* dst = ex.peer_recv[warp] + (((int64_t)slot * ex.world + ex.rank) * ex.max_rows + b) * L;
 #pragma unroll
@@ -774,7 +902,7 @@ cudaError_t launch_simt(const void* X, const void* W, const SimtParams& p, int g
 }
 
 template <int L>
-cudaError_t launch_publish(const uint64_t* lists, int nlists, int64_t list_stride, int64_t rows,
+cudaError_t launch_publish(const uint64_t* lists, int nlists, int64_t list_stride, int64_t rows, int k,
                            const ExchangeDev& ex, cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
   cudaLaunchConfig_t cfg = {};
@@ -786,7 +914,7 @@ cudaError_t launch_publish(const uint64_t* lists, int nlists, int64_t list_strid
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, publish_kernel<L>, lists, nlists, list_stride, rows, ex);
+  return cudaLaunchKernelEx(&cfg, publish_kernel<L>, lists, nlists, list_stride, rows, k, ex);
 }
 
 template <int L>
@@ -836,7 +964,7 @@ STK_FUSED_CONFIGS(STK_INST_FUSED)
                                                      cudaStream_t);                                             \
   template cudaError_t launch_merge<L>(const uint64_t*, int, int64_t, int64_t, int, float*, int32_t*, uint64_t*, \
                                        cudaStream_t);                                                           \
-  template cudaError_t launch_publish<L>(const uint64_t*, int, int64_t, int64_t, const ExchangeDev&,            \
+  template cudaError_t launch_publish<L>(const uint64_t*, int, int64_t, int64_t, int, const ExchangeDev&,       \
                                          cudaStream_t);                                                         \
   template cudaError_t launch_exchange_merge<L>(const ExchangeDev&, int64_t, int, float*, int32_t*, cudaStream_t);
 STK_INST_SIMT(32)

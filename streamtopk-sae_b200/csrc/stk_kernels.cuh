@@ -142,7 +142,7 @@ struct ExchangeDev {
 constexpr unsigned kErrExchangeTimeout = 3;
 
 template <int L>
-cudaError_t launch_publish(const uint64_t* lists, int nlists, int64_t list_stride, int64_t rows,
+cudaError_t launch_publish(const uint64_t* lists, int nlists, int64_t list_stride, int64_t rows, int k,
                            const ExchangeDev& ex, cudaStream_t stream);
 template <int L>
 cudaError_t launch_exchange_merge(const ExchangeDev& ex, int64_t rows, int k, float* V, int32_t* I,

@@ -216,3 +216,37 @@ def test_sampled_floor_changes_nothing(B, d, F, k):
     assert torch.equal(V1, V2) and torch.equal(I1, I2)
     if F <= 70000:
         check(V1, I1, Xr, Wr, br, k, RTOL["bf16"])
+
+
+@pytest.mark.parametrize("k", [16, 64, 128])
+def test_exchange_single_rank_equals_exact(k):
+    """A one-rank peer exchange (publish kernel into its own receive buffer, arrival
+    counters, final merge) over several steps equals the exact encode."""
+    import ctypes
+    import streamtopk_sae as stk
+    from streamtopk_sae import _capi
+    lib = _capi.load()
+    B, d, F = 128, 1024, 50000
+    X, W, b = stk.make_inputs(B, d, F, dtype=torch.bfloat16, seed=5, device="cuda", w_init="unit_rows")
+    nbytes = ctypes.c_size_t(0)
+    _capi.check(lib.stk_exchange_bytes(1, B, k, ctypes.byref(nbytes)))
+    buf = torch.empty(nbytes.value, dtype=torch.uint8, device="cuda")
+    h = ctypes.c_void_p()
+    _capi.check(lib.stk_exchange_create(0, 1, B, k, buf.data_ptr(), nbytes.value, 5.0, ctypes.byref(h)))
+    try:
+        _capi.check(lib.stk_exchange_connect(h, b"\0" * _capi.IPC_HANDLE_BYTES, (ctypes.c_int64 * 1)(0)))
+        wsb = _capi.workspace_bytes(B, d, F, k, _capi.STK_BF16)
+        ws = torch.empty(max(wsb, 8), dtype=torch.uint8, device="cuda")
+        stream = torch.cuda.current_stream().cuda_stream
+        Ve, Ie = stk.topk_sae_cuda_exact(X, W, b, k)
+        for _ in range(3):   # both receive slots and the step counter
+            V = torch.empty((B, k), dtype=torch.float32, device="cuda")
+            I = torch.empty((B, k), dtype=torch.int32, device="cuda")
+            _capi.check(lib.stk_exchange_forward(h, X.data_ptr(), W.data_ptr(), b.data_ptr(), V.data_ptr(),
+                                                 I.data_ptr(), B, d, F, k, 0, _capi.STK_BF16, 0, ws.data_ptr(),
+                                                 wsb, stream))
+            torch.cuda.synchronize()
+            assert torch.equal(V, Ve) and torch.equal(I, Ie)
+        assert _capi.device_error(stream) == 0
+    finally:
+        lib.stk_exchange_destroy(h)
