@@ -10,6 +10,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <new>
 #include <numeric>
 #include <string>
 #include <vector>
@@ -622,7 +623,8 @@ int stk_exchange_create(int rank, int world, int64_t max_rows, int64_t k, void* 
   e = cudaMemset(base + lay.arrive, 0, lay.total - lay.arrive);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return cuda_fail(e, "exchange buffer clear");
-  stk_exchange* x = new stk_exchange();
+  stk_exchange* x = new (std::nothrow) stk_exchange();
+  if (!x) return fail(STK_ENOSPACE, "out of host memory");
   x->device = device;
   x->L = L;
   x->dev.recv = reinterpret_cast<uint64_t*>(base + lay.recv);
