@@ -5,7 +5,8 @@ ayushimehrotra/streamtopk-sae): ``topk_sae_cuda_exact`` and
 ``topk_sae_cuda_approx`` compute top_k(X @ W_enc.T + b_enc, k) without
 materialising the (B, F) score matrix, on tcgen05 tensor cores with the top-k
 selection fused into the GEMM epilogue.  ``shard`` adds the multi-GPU
-F-sharded encoder (one process per GPU, NCCL all-gather + merge).
+F-sharded encoder (one process per GPU; the per-rank key lists are exchanged
+by direct peer stores between the GPUs, or by an NCCL all-gather, then merged).
 """
 from streamtopk_sae.ops import topk_sae_cpu, topk_sae_cuda_approx, topk_sae_cuda_exact
 from streamtopk_sae.utils import make_inputs, recall_at_k
