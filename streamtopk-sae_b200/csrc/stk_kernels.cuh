@@ -110,9 +110,25 @@ struct SimtCfg {
   X(128, 256, 2, 32, false)  \
   X(128, 128, 3, 32, false)
 
-template <int L, int NT, int STAGES, int A, bool APP_SMEM>
-cudaError_t launch_fused(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tw32, const FusedParams& p,
-                         int grid, cudaStream_t stream);
+// Configurations of the fp32 (3-pass TF32) variant: same shared-memory plan
+// (X hi + lo tiles take the bytes of the 16-bit X tile, W + its residual those
+// of the 16-bit W tile, K = 16 per stage with 64-byte swizzle).
+#define STK_FUSED_TF32_CONFIGS(X) \
+  X(32, 256, 3, 32, true)         \
+  X(64, 256, 3, 16, true)         \
+  X(128, 256, 2, 32, false)       \
+  X(32, 128, 5, 32, true)         \
+  X(64, 128, 4, 16, true)         \
+  X(128, 128, 3, 32, false)
+
+// TF32: X is read through two maps (txl: the residual X - round_tf32(X));
+// otherwise txl is unused.
+template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TF32>
+cudaError_t launch_fused(const CUtensorMap& tx, const CUtensorMap& txl, const CUtensorMap& tw, const CUtensorMap& tw32,
+                         const FusedParams& p, int grid, cudaStream_t stream);
+
+// Xh = round_tf32(X), Xl = round_tf32(X - Xh), n elements.
+cudaError_t launch_split_tf32(const float* X, float* Xh, float* Xl, int64_t n, cudaStream_t stream);
 
 template <typename T, int L>
 cudaError_t launch_simt(const void* X, const void* W, const SimtParams& p, int grid, cudaStream_t stream);

@@ -250,3 +250,29 @@ def test_exchange_single_rank_equals_exact(k):
         assert _capi.device_error(stream) == 0
     finally:
         lib.stk_exchange_destroy(h)
+
+
+@pytest.mark.parametrize("B,d,F,k", [(128, 768, 65536, 32), (64, 256, 30001, 64), (130, 100, 5000, 16),
+                                     (1, 64, 300, 8), (32, 2048, 20000, 128), (128, 2048, 262144, 64)])
+def test_tf32_path_matches_oracle(B, d, F, k):
+    """fp32 inputs on tensor cores (STK_FLAG_TF32: round_tf32 split, 3 passes) within the fp32 tolerance."""
+    from streamtopk_sae import _capi, native
+    X, W, b = oracle.gaussian_inputs(B, d, F, seed=B + d + k)
+    Xt, Wt, bt, Xr, Wr, br = device_inputs(X, W, b, "fp32")
+    V, I = native.streamtopk_cuda_exact_forward(Xt, Wt, bt, k, flags=_capi.STK_FLAG_TF32)
+    torch.cuda.synchronize()
+    no_device_error()
+    check(V, I, Xr, Wr, br, k, RTOL["fp32"])
+
+
+def test_tf32_path_ties_and_zero_x():
+    """All-equal scores rank by feature index on the TF32 path too."""
+    from streamtopk_sae import _capi, native
+    B, d, F, k = 16, 128, 3000, 32
+    X = torch.zeros(B, d, device="cuda")
+    W = torch.randn(F, d, device="cuda")
+    b = torch.zeros(F, device="cuda")
+    V, I = native.streamtopk_cuda_exact_forward(X, W, b, k, flags=_capi.STK_FLAG_TF32)
+    torch.cuda.synchronize()
+    assert torch.equal(I.cpu(), torch.arange(k, dtype=torch.int32).expand(B, k))
+    assert torch.all(V == 0)
