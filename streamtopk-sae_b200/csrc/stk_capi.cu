@@ -414,8 +414,10 @@ int stk_workspace_bytes(int64_t B, int64_t d, int64_t F, int64_t k, int dtype, s
   int rc = check_common("stk_workspace_bytes", B, d, F, dtype);
   if (rc) return rc;
   if (k < 1 || list_len(k) == 0) return fail(STK_EINVAL, "k out of range");
+  // Sized for every path a call with these shapes may take: fp32 inputs
+  // include the split X of the TF32 path (STK_FLAG_TF32 is a call flag).
   Plan pl;
-  rc = plan(nullptr, nullptr, B, d, F, k, dtype, 0, &pl);
+  rc = plan(nullptr, nullptr, B, d, F, k, dtype, dtype == STK_F32 ? STK_FLAG_TF32 : 0, &pl);
   if (rc) return rc;
   *bytes = pl.ws;
   return STK_OK;
