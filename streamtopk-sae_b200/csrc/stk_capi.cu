@@ -306,6 +306,11 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   p.ab_format = bf16 ? 1 : 0;
   p.w_evict_first = pl.grid.m_tiles == 1 ? 1 : 0;
   p.index_offset = index_offset;
+  p.pilot_chunks = stk::kPilotChunks;
+  if (const char* e = std::getenv("STK_PILOT_CHUNKS")) {  // tuning sweeps
+    const int v = std::atoi(e);
+    if (v >= 1 && v <= 8) p.pilot_chunks = v;
+  }
   p.pilot_hist = nullptr;
   p.pilot_rowmax = nullptr;
   p.pilot_count = nullptr;

@@ -458,7 +458,7 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
         uint32_t bmax = 0;
         bool any = false;
 #pragma unroll 1
-        for (int c = 0; c < kPilotChunks && c < nchunk; ++c) {
+        for (int c = 0; c < p.pilot_chunks && c < nchunk; ++c) {
           uint32_t v[32];
           tmem_ld32(tcol + (uint32_t)(c * 32), v);
           tmem_wait_ld(v);

@@ -32,7 +32,7 @@ constexpr size_t kAppendBytesPerCta = (size_t)kAppendMax * kRows * 8;
 // a bounded grid barrier, and each row starts with the lower edge of the bin
 // that holds its k-th largest histogrammed score as filter floor.
 constexpr int kPilotBits = 12;
-constexpr int kPilotChunks = 2;  // sampled 32-feature chunks per CTA
+constexpr int kPilotChunks = 2;  // default sampled 32-feature chunks per CTA
 constexpr int kPilotGroup = 8;   // scores per histogrammed group maximum
 constexpr int kPilotBins = 1 << kPilotBits;
 constexpr unsigned long long kPilotWaitNs = 200000;  // give up (no floor) after 200 us
@@ -51,6 +51,7 @@ struct FusedParams {
   int ab_format;       // 0 fp16, 1 bf16
   int w_evict_first;   // W is read once (single M tile): stream it past L2
   uint32_t index_offset;
+  int pilot_chunks;    // sampled 32-feature chunks per CTA (<= the first tile's chunks)
 };
 
 struct SimtParams {
