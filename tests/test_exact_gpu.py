@@ -276,3 +276,22 @@ def test_tf32_path_ties_and_zero_x():
     torch.cuda.synchronize()
     assert torch.equal(I.cpu(), torch.arange(k, dtype=torch.int32).expand(B, k))
     assert torch.all(V == 0)
+
+
+@pytest.mark.parametrize("B,d,F,k", [(128, 2048, 262144, 64), (128, 768, 65536, 32), (300, 256, 50000, 128)])
+def test_working_memory_is_the_workspace(B, d, F, k):
+    """Peak device memory of a call = inputs + V/I + the workspace the C ABI reports
+    (the reference's run_memory.py 'working memory'); no F-sized scratch."""
+    import streamtopk_sae as stk
+    from streamtopk_sae import _capi
+    X, W, b = stk.make_inputs(B, d, F, dtype=torch.bfloat16, seed=1, device="cuda")
+    stk.topk_sae_cuda_exact(X, W, b, k)          # first call: library and module setup
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats()
+    base = torch.cuda.memory_allocated()
+    stk.topk_sae_cuda_exact(X, W, b, k)
+    torch.cuda.synchronize()
+    working = torch.cuda.max_memory_allocated() - base - B * k * 8
+    ws = _capi.workspace_bytes(B, d, F, k, _capi.STK_BF16)
+    assert ws - 4096 <= working <= ws + 4096, (working, ws)
+    assert ws < 64 << 20 or B > 256
