@@ -49,7 +49,8 @@ enum stk_flags {
   STK_FLAG_ANY_K = 1, /* accept any 1 <= k <= 128, not only {1,2,4,8,16,32,64,128} */
   STK_FLAG_ANY_D = 2, /* lift the reference's d <= 4096 limit */
   STK_FLAG_SIMT = 4,    /* force the fp32 SIMT kernel (testing / comparison) */
-  STK_FLAG_NO_PILOT = 8 /* skip the sampled threshold floor (testing / comparison) */
+  STK_FLAG_NO_PILOT = 8, /* skip the sampled threshold floor (testing / comparison) */
+  STK_FLAG_TF32 = 16     /* fp32 inputs on tensor cores: 3-pass TF32 (hi*hi + hi*lo + lo*hi), d % 4 == 0 */
 };
 
 /* Library version (major * 10000 + minor * 100 + patch). */

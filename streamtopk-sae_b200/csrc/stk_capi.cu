@@ -147,6 +147,26 @@ int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t d, int bo
   return STK_OK;
 }
 
+// 2-D K-major tensor map over a (rows, d) row-major fp32 matrix with a
+// (16 x box_rows) box (64 bytes of K per row) and 64-byte swizzle.
+int make_map_f32(CUtensorMap* map, const void* base, int64_t rows, int64_t d, int box_rows) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return fail(STK_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {(cuuint64_t)d, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)d * 4};
+  const cuuint32_t box[2] = {16, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[96];
+    std::snprintf(buf, sizeof buf, "cuTensorMapEncodeTiled (fp32) failed (CUresult %d)", (int)r);
+    return fail(STK_ECUDA, buf);
+  }
+  return STK_OK;
+}
+
 int list_len(int64_t k) { return k <= 32 ? 32 : k <= 64 ? 64 : k <= 128 ? 128 : 0; }
 
 bool ref_k(int64_t k) {
@@ -182,7 +202,8 @@ stk::UnitGrid make_tile_grid(int64_t B, int64_t F) {
 size_t partial_bytes(const stk::UnitGrid& g, int L) { return (size_t)g.units * stk::kRows * L * sizeof(uint64_t); }
 
 struct Plan {
-  bool tc;  // tcgen05 path
+  bool tc;    // tcgen05 path
+  bool tf32;  // tcgen05 path for fp32 inputs (3-pass TF32), opt-in
   int L;
   stk::UnitGrid grid;
   int ctas;
@@ -190,6 +211,7 @@ struct Plan {
   size_t ws_partials;
   size_t ws_app;
   size_t ws_pilot;
+  size_t ws_split;  // TF32: round_tf32(X) and its residual, each 256-byte aligned
   size_t ws;
 };
 
@@ -200,8 +222,10 @@ int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t 
   int rc = device_sms(&sms);
   if (rc) return rc;
   pl->L = list_len(k);
-  pl->tc = (dtype == STK_BF16 || dtype == STK_F16) && (d % 8 == 0) && !(flags & STK_FLAG_SIMT) &&
-           (X == nullptr || aligned16(X)) && (W == nullptr || aligned16(W));
+  const bool aligned = (X == nullptr || aligned16(X)) && (W == nullptr || aligned16(W));
+  pl->tf32 = dtype == STK_F32 && (flags & STK_FLAG_TF32) && (d % 4 == 0) && !(flags & STK_FLAG_SIMT) && aligned;
+  pl->tc = ((dtype == STK_BF16 || dtype == STK_F16) && (d % 8 == 0) && !(flags & STK_FLAG_SIMT) && aligned) ||
+           pl->tf32;
   pl->grid = make_grid(B, F, sms);
   pl->ctas = pl->grid.units < sms ? pl->grid.units : sms;
   // partial lists, then one append buffer per CTA, then (optionally) the
@@ -213,7 +237,8 @@ int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t 
   pl->pilot = pl->tc && pl->grid.units <= pl->ctas && pl->grid.m_tiles <= 2 &&
               pl->grid.nchunks >= 4 * (int64_t)pl->grid.segs && !(flags & STK_FLAG_NO_PILOT);
   pl->ws_pilot = pl->pilot ? (size_t)pl->grid.m_tiles * stk::kRows * (stk::kPilotBins + 1) * 4 + 256 : 0;
-  pl->ws = pl->ws_partials + pl->ws_app + pl->ws_pilot;
+  pl->ws_split = pl->tf32 ? 2 * (((size_t)B * d * 4 + 255) & ~size_t(255)) : 0;
+  pl->ws = pl->ws_partials + pl->ws_app + pl->ws_pilot + pl->ws_split;
   return STK_OK;
 }
 
@@ -247,11 +272,27 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   int nslots = pl.L == 64 ? 16 : 32;
   int app_smem = pl.L == 128 ? 0 : 1;
   fused_override(pl.L, &nt, &stages, &nslots, &app_smem);
-  CUtensorMap tx, tw, tw32;
+  CUtensorMap tx, txl, tw, tw32;
   const bool bf16 = dtype == STK_BF16;
-  int rc = make_map(&tx, X, B, d, stk::kRows, bf16);
-  if (!rc) rc = make_map(&tw, W, F, d, nt, bf16);
-  if (!rc) rc = make_map(&tw32, W, F, d, 32, bf16);
+  int rc = STK_OK;
+  if (pl.tf32) {
+    // X is split once per call into round_tf32(X) and its residual (L2-resident,
+    // re-read by every tile); W is split tile by tile inside the kernel.
+    uint8_t* split = reinterpret_cast<uint8_t*>(partials) + pl.ws_partials + pl.ws_app + pl.ws_pilot;
+    float* xh = reinterpret_cast<float*>(split);
+    float* xl = reinterpret_cast<float*>(split + pl.ws_split / 2);
+    cudaError_t se = stk::launch_split_tf32(static_cast<const float*>(X), xh, xl, B * d, stream);
+    if (se != cudaSuccess) return cuda_fail(se, "split_tf32_kernel launch");
+    rc = make_map_f32(&tx, xh, B, d, stk::kRows);
+    if (!rc) rc = make_map_f32(&txl, xl, B, d, stk::kRows);
+    if (!rc) rc = make_map_f32(&tw, W, F, d, nt);
+    if (!rc) rc = make_map_f32(&tw32, W, F, d, 32);
+  } else {
+    rc = make_map(&tx, X, B, d, stk::kRows, bf16);
+    if (!rc) rc = make_map(&tw, W, F, d, nt, bf16);
+    if (!rc) rc = make_map(&tw32, W, F, d, 32, bf16);
+    txl = tx;
+  }
   if (rc) return rc;
   stk::FusedParams p;
   p.grid = pl.grid;
@@ -261,10 +302,15 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   p.B = B;
   p.F = F;
   p.k = (int)k;
-  p.num_kb = (int)((d + 63) / 64);
+  p.num_kb = pl.tf32 ? (int)((d + 15) / 16) : (int)((d + 63) / 64);
   p.ab_format = bf16 ? 1 : 0;
   p.w_evict_first = pl.grid.m_tiles == 1 ? 1 : 0;
   p.index_offset = index_offset;
+  p.pilot_chunks = stk::kPilotChunks;
+  if (const char* e = std::getenv("STK_PILOT_CHUNKS")) {  // tuning sweeps
+    const int v = std::atoi(e);
+    if (v >= 1 && v <= 8) p.pilot_chunks = v;
+  }
   p.pilot_hist = nullptr;
   p.pilot_rowmax = nullptr;
   p.pilot_count = nullptr;
@@ -278,11 +324,16 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   }
   cudaError_t e = cudaErrorInvalidValue;
   ProfScope prof(kProfFused, stream);
-#define STK_TRY_FUSED(Lc, NTc, Sc, Ac, SMc)                                                  \
-  if (pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc)       \
-    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc>(tx, tw, tw32, p, pl.ctas, stream);
+#define STK_TRY_FUSED(Lc, NTc, Sc, Ac, SMc)                                                           \
+  if (!pl.tf32 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc)    \
+    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, false>(tx, txl, tw, tw32, p, pl.ctas, stream);
   STK_FUSED_CONFIGS(STK_TRY_FUSED)
 #undef STK_TRY_FUSED
+#define STK_TRY_FUSED_TF32(Lc, NTc, Sc, Ac, SMc)                                                      \
+  if (pl.tf32 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc)     \
+    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, true>(tx, txl, tw, tw32, p, pl.ctas, stream);
+  STK_FUSED_TF32_CONFIGS(STK_TRY_FUSED_TF32)
+#undef STK_TRY_FUSED_TF32
   if (e != cudaSuccess) return cuda_fail(e, "fused_topk_kernel launch");
   return STK_OK;
 }
@@ -368,8 +419,10 @@ int stk_workspace_bytes(int64_t B, int64_t d, int64_t F, int64_t k, int dtype, s
   int rc = check_common("stk_workspace_bytes", B, d, F, dtype);
   if (rc) return rc;
   if (k < 1 || list_len(k) == 0) return fail(STK_EINVAL, "k out of range");
+  // Sized for every path a call with these shapes may take: fp32 inputs
+  // include the split X of the TF32 path (STK_FLAG_TF32 is a call flag).
   Plan pl;
-  rc = plan(nullptr, nullptr, B, d, F, k, dtype, 0, &pl);
+  rc = plan(nullptr, nullptr, B, d, F, k, dtype, dtype == STK_F32 ? STK_FLAG_TF32 : 0, &pl);
   if (rc) return rc;
   *bytes = pl.ws;
   return STK_OK;
@@ -455,6 +508,8 @@ int candidates_plan(const void* X, const void* W, int64_t B, int64_t d, int64_t 
   pl->ws_partials = (partial_bytes(pl->grid, pl->L) + 255) & ~size_t(255);
   pl->ws_app = ((size_t)pl->ctas * stk::kAppendBytesPerCta + 255) & ~size_t(255);
   pl->ws_pilot = 0;
+  pl->tf32 = false;
+  pl->ws_split = 0;
   pl->ws = pl->ws_partials + pl->ws_app;
   return STK_OK;
 }

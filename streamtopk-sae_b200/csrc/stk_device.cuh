@@ -459,6 +459,32 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64
 }
 
 // Arrive on the mbarrier once all previously issued tcgen05.mma of this thread complete.
+// Same with operands in TF32 (fp32 bit patterns; the tensor core reads the top
+// 19 bits), K = 8 per instruction.
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Makes this thread's generic-proxy writes to shared memory visible to the
+// async proxy (tensor-core operand reads) after the next synchronisation.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// fp32 -> the nearest TF32 value (10 explicit mantissa bits, ties to even),
+// returned as fp32 with the low 13 bits clear; inf / NaN pass through.
+__device__ __forceinline__ float round_tf32(float x) {
+  uint32_t u = __float_as_uint(x);
+  if ((u & 0x7f800000u) != 0x7f800000u) u += 0xfffu + ((u >> 13) & 1u);
+  return __uint_as_float(u & 0xffffe000u);
+}
+
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
@@ -507,10 +533,25 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
   return d;
 }
 
+// Shared-memory matrix descriptor, K-major, 64-byte swizzle (8-row groups
+// 512 bytes apart); K advances by 32 bytes = +2 in the address field.
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= uint64_t((saddr & 0x3ffffu) >> 4);         // start address
+  d |= uint64_t(1) << 16;                          // leading byte offset (ignored for swizzled K-major)
+  d |= uint64_t(512 >> 4) << 32;                   // stride byte offset
+  d |= uint64_t(1) << 46;                          // descriptor version
+  d |= uint64_t(4) << 61;                          // SWIZZLE_64B
+  return d;
+}
+
 // Instruction descriptor, kind::f16, fp32 accumulate, A and B K-major.
 // ab_format: 0 = fp16, 1 = bf16.
 __host__ __device__ constexpr uint32_t make_idesc_f16(uint32_t ab_format, uint32_t m, uint32_t n) {
   return (1u << 4) | (ab_format << 7) | (ab_format << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
+
+// Instruction descriptor, kind::tf32 (A and B format 2), fp32 accumulate, K-major.
+__host__ __device__ constexpr uint32_t make_idesc_tf32(uint32_t m, uint32_t n) { return make_idesc_f16(2u, m, n); }
 
 }  // namespace stk

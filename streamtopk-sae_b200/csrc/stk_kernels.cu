@@ -190,11 +190,22 @@ __device__ __forceinline__ void load_bias_tile(const float* __restrict__ bias, i
 //   warp 0: TMA producer        warp 1: TMEM owner + MMA issuer
 //   warps 2..5: epilogue, warp w reads TMEM lanes 32*(w%4)..+31 (= batch rows)
 // ---------------------------------------------------------------------------
-template <int L, int NT, int STAGES, int A, bool APP_SMEM>
-__global__ void __launch_bounds__(kFusedThreads, 1)
-    fused_topk_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
-                      const __grid_constant__ CUtensorMap tmap_w32, const FusedParams p) {
+// TF32 = false: 16-bit X / W, K = 64 per stage, 128-byte swizzle, warps 0 TMA,
+// 1 MMA, 2-5 epilogue.  TF32 = true (fp32 inputs): K = 16 per stage, 64-byte
+// swizzle; a stage holds round_tf32(X) and its residual (both precomputed,
+// two maps) and a W tile that warps 2-3 split in place into round_tf32(W) and
+// its residual; the MMA issuer accumulates Xh*Wh + Xh*Wl + Xl*Wh (the dropped
+// Xl*Wl term is ~2^-22 of |x||w|); warps 4-7 are the epilogue.
+template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TF32>
+__global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
+    fused_topk_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_xl,
+                      const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_w32,
+                      const FusedParams p) {
   using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM>;
+  constexpr int kSplitThreads = 64;                 // warps 2-3 (TF32)
+  constexpr int kFirstEpiWarp = TF32 ? 4 : 2;
+  constexpr uint32_t kWRowBytes = TF32 ? 64u : 128u;  // bytes of one W row in a stage
+  constexpr int kKPerStage = TF32 ? 16 : 64;        // elements of K per stage
   uint8_t* smem = stk_smem + ((1024u - (smem_u32(stk_smem) & 1023u)) & 1023u);
   uint64_t* top = reinterpret_cast<uint64_t*>(smem + Cfg::kTopOff);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOff);
@@ -203,7 +214,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   uint64_t* acc_full = bars + 2 * STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* mma_done = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* split_done = mma_done + 1;  // [STAGES], TF32 only
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(split_done + (TF32 ? STAGES : 0));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* pilot_flag = abort_flag + 1;
 
@@ -223,9 +235,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       mbar_init(&acc_empty[a], kEpilogueWarps);
     }
     mbar_init(mma_done, 1);
+    if constexpr (TF32)
+      for (int s = 0; s < STAGES; ++s) mbar_init(&split_done[s], kSplitThreads);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmap_x);
+    if constexpr (TF32) tma_prefetch_desc(&tmap_xl);
     tma_prefetch_desc(&tmap_w);
     tma_prefetch_desc(&tmap_w32);
   }
@@ -252,7 +267,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         unit_range(g, u, m, fb, fe);
         for (int64_t ft = fb; ft < fe && ok; ft += NT) {
           const int w = (int)min((int64_t)NT, fe - ft);
-          const uint32_t bytes = Cfg::kXBytes + (uint32_t)w * 128u;
+          const uint32_t bytes = Cfg::kXBytes + (uint32_t)w * kWRowBytes;
           for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
             const int s = it % STAGES;
             if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag)) {
@@ -262,12 +277,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
             uint8_t* sx = smem + s * Cfg::kStageBytes;
             uint8_t* sw = sx + Cfg::kXBytes;
             mbar_arrive_expect_tx(&full[s], bytes);
-            tma_load_2d(&tmap_x, &full[s], sx, kb * 64, m * kRows, pol_x);
+            const int kx = kb * kKPerStage;
+            tma_load_2d(&tmap_x, &full[s], sx, kx, m * kRows, pol_x);
+            if constexpr (TF32) tma_load_2d(&tmap_xl, &full[s], sx + Cfg::kXBytes / 2, kx, m * kRows, pol_x);
             if (w == NT) {
-              tma_load_2d(&tmap_w, &full[s], sw, kb * 64, (int)ft, pol_w);
+              tma_load_2d(&tmap_w, &full[s], sw, kx, (int)ft, pol_w);
             } else {
               for (int q = 0; q < w / 32; ++q)
-                tma_load_2d(&tmap_w32, &full[s], sw + q * 32 * 128, kb * 64, (int)ft + 32 * q, pol_w);
+                tma_load_2d(&tmap_w32, &full[s], sw + q * 32 * kWRowBytes, kx, (int)ft + 32 * q, pol_w);
             }
           }
         }
@@ -302,20 +319,35 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           }
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + (uint32_t)(a * NT);
-          const uint32_t idesc = make_idesc_f16((uint32_t)p.ab_format, 128u, (uint32_t)w);
+          const uint32_t idesc = TF32 ? make_idesc_tf32(128u, (uint32_t)w)
+                                      : make_idesc_f16((uint32_t)p.ab_format, 128u, (uint32_t)w);
           for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
             const int s = it % STAGES;
-            if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag)) {
+            // TF32: the W tile must also have been split by warps 2-3.
+            if (!mbar_wait(TF32 ? &split_done[s] : &full[s], (it / STAGES) & 1, abort_flag)) {
               ok = false;
               break;
             }
             tc_fence_after();
             const uint32_t sx = smem_u32(smem + s * Cfg::kStageBytes);
-            const uint64_t dx = smem_desc_sw128(sx);
-            const uint64_t dw = smem_desc_sw128(sx + Cfg::kXBytes);
+            if constexpr (TF32) {
+              const uint64_t dxh = smem_desc_sw64(sx);
+              const uint64_t dxl = smem_desc_sw64(sx + Cfg::kXBytes / 2);
+              const uint64_t dwh = smem_desc_sw64(sx + Cfg::kXBytes);
+              const uint64_t dwl = smem_desc_sw64(sx + Cfg::kXBytes + NT * kWRowBytes);
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_f16(d_tmem, dx + 2 * kk, dw + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+              for (int kk = 0; kk < 2; ++kk) {
+                umma_tf32(d_tmem, dxh + 2 * kk, dwh + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+                umma_tf32(d_tmem, dxh + 2 * kk, dwl + 2 * kk, idesc, 1u);
+                umma_tf32(d_tmem, dxl + 2 * kk, dwh + 2 * kk, idesc, 1u);
+              }
+            } else {
+              const uint64_t dx = smem_desc_sw128(sx);
+              const uint64_t dw = smem_desc_sw128(sx + Cfg::kXBytes);
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                umma_f16(d_tmem, dx + 2 * kk, dw + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+            }
             umma_commit(&empty[s]);
           }
           if (ok) umma_commit(&acc_full[a]);
@@ -330,6 +362,54 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       mbar_wait(mma_done, 0, nullptr);
     }
     __syncwarp();
+  } else if (TF32 && warp < kFirstEpiWarp) {
+    // ------------------------------------------------------------ W splitter (TF32)
+    // Walks the producer's stage sequence; every thread waits for the stage's
+    // TMA itself (so that the loaded bytes are visible to its own reads),
+    // rewrites its share of the W tile as round_tf32(W) and writes the
+    // residual round_tf32(W - that) to the tile's second half, then makes the
+    // writes visible to the tensor core and arrives on split_done.
+    const int st = (warp - 2) * 32 + lane;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < g.units && ok; u += gridDim.x) {
+      int m;
+      int64_t fb, fe;
+      unit_range(g, u, m, fb, fe);
+      for (int64_t ft = fb; ft < fe && ok; ft += NT) {
+        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const bool got = mbar_wait(&full[s], (it / STAGES) & 1, abort_flag);
+          if (!__all_sync(0xffffffffu, got)) {
+            ok = false;
+            break;
+          }
+          float4* wh = reinterpret_cast<float4*>(smem + s * Cfg::kStageBytes + Cfg::kXBytes);
+          float4* wl = wh + NT * (kWRowBytes / 16);
+#pragma unroll 4
+          for (int i = st; i < NT * (int)(kWRowBytes / 16); i += kSplitThreads) {
+            const float4 v = wh[i];
+            float4 h, l;
+            h.x = round_tf32(v.x);
+            h.y = round_tf32(v.y);
+            h.z = round_tf32(v.z);
+            h.w = round_tf32(v.w);
+            l.x = round_tf32(v.x - h.x);
+            l.y = round_tf32(v.y - h.y);
+            l.z = round_tf32(v.z - h.z);
+            l.w = round_tf32(v.w - h.w);
+            wh[i] = h;
+            wl[i] = l;
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(&split_done[s]);
+        }
+      }
+    }
+    if (!ok && lane == 0) {
+      raise_device_error(kErrWaitTimeout);
+      *abort_flag = 1;
+    }
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
@@ -362,7 +442,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           // Match the two epilogue barriers of the sample step so the other
           // epilogue warps cannot wait on this one forever.
           epilogue_bar();
-          if (warp == 2 && lane == 0) *pilot_flag = 0;
+          if (warp == kFirstEpiWarp && lane == 0) *pilot_flag = 0;
           epilogue_bar();
         }
         ok = false;
@@ -378,7 +458,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         uint32_t bmax = 0;
         bool any = false;
 #pragma unroll 1
-        for (int c = 0; c < kPilotChunks && c < nchunk; ++c) {
+        for (int c = 0; c < p.pilot_chunks && c < nchunk; ++c) {
           uint32_t v[32];
           tmem_ld32(tcol + (uint32_t)(c * 32), v);
           tmem_wait_ld(v);
@@ -408,7 +488,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         if (any) atomicMax(p.pilot_rowmax + (size_t)cur.m * kRows + r, bmax);
         __threadfence();
         epilogue_bar();
-        if (warp == 2 && lane == 0) {
+        if (warp == kFirstEpiWarp && lane == 0) {
           atomicAdd(p.pilot_count, 1u);
           const unsigned long long t0 = global_timer_ns();
           int ok_all = 1;
@@ -880,14 +960,31 @@ __global__ void __launch_bounds__(kMergeWarps * 32) exchange_merge_kernel(const 
 // ---------------------------------------------------------------------------
 // Explicit instantiations and launch helpers (host side of this TU).
 // ---------------------------------------------------------------------------
-template <int L, int NT, int STAGES, int A, bool APP_SMEM>
-cudaError_t launch_fused(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tw32, const FusedParams& p,
-                         int grid, cudaStream_t stream) {
+template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TF32>
+cudaError_t launch_fused(const CUtensorMap& tx, const CUtensorMap& txl, const CUtensorMap& tw, const CUtensorMap& tw32,
+                         const FusedParams& p, int grid, cudaStream_t stream) {
   using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM>;
-  auto kern = fused_topk_kernel<L, NT, STAGES, A, APP_SMEM>;
+  auto kern = fused_topk_kernel<L, NT, STAGES, A, APP_SMEM, TF32>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   if (e != cudaSuccess) return e;
-  kern<<<grid, kFusedThreads, Cfg::kSmemBytes, stream>>>(tx, tw, tw32, p);
+  kern<<<grid, TF32 ? kFusedThreads + 64 : kFusedThreads, Cfg::kSmemBytes, stream>>>(tx, txl, tw, tw32, p);
+  return cudaGetLastError();
+}
+
+__global__ void split_tf32_kernel(const float* __restrict__ X, float* __restrict__ Xh, float* __restrict__ Xl,
+                                  int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float x = X[i];
+    const float h = round_tf32(x);
+    Xh[i] = h;
+    Xl[i] = round_tf32(x - h);
+  }
+}
+
+cudaError_t launch_split_tf32(const float* X, float* Xh, float* Xl, int64_t n, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  const int64_t blocks = (n + 255) / 256;
+  split_tf32_kernel<<<(unsigned)(blocks < 1184 ? blocks : 1184), 256, 0, stream>>>(X, Xh, Xl, n);
   return cudaGetLastError();
 }
 
@@ -952,10 +1049,16 @@ cudaError_t launch_merge(const uint64_t* lists, int nlists, int64_t list_stride,
   return cudaLaunchKernelEx(&cfg, merge_lists_kernel<L>, lists, nlists, list_stride, rows, k, V, I, keys_out);
 }
 
-#define STK_INST_FUSED(L, NT, S, A, SM)                                                                           \
-  template cudaError_t launch_fused<L, NT, S, A, SM>(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, \
-                                                     const FusedParams&, int, cudaStream_t);
+#define STK_INST_FUSED(L, NT, S, A, SM)                                                                            \
+  template cudaError_t launch_fused<L, NT, S, A, SM, false>(const CUtensorMap&, const CUtensorMap&,              \
+                                                            const CUtensorMap&, const CUtensorMap&,              \
+                                                            const FusedParams&, int, cudaStream_t);
 STK_FUSED_CONFIGS(STK_INST_FUSED)
+#define STK_INST_FUSED_TF32(L, NT, S, A, SM)                                                                       \
+  template cudaError_t launch_fused<L, NT, S, A, SM, true>(const CUtensorMap&, const CUtensorMap&,               \
+                                                           const CUtensorMap&, const CUtensorMap&,               \
+                                                           const FusedParams&, int, cudaStream_t);
+STK_FUSED_TF32_CONFIGS(STK_INST_FUSED_TF32)
 
 #define STK_INST_SIMT(L)                                                                                         \
   template cudaError_t launch_simt<float, L>(const void*, const void*, const SimtParams&, int, cudaStream_t);   \

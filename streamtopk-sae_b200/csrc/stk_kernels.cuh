@@ -32,7 +32,7 @@ constexpr size_t kAppendBytesPerCta = (size_t)kAppendMax * kRows * 8;
 // a bounded grid barrier, and each row starts with the lower edge of the bin
 // that holds its k-th largest histogrammed score as filter floor.
 constexpr int kPilotBits = 12;
-constexpr int kPilotChunks = 2;  // sampled 32-feature chunks per CTA
+constexpr int kPilotChunks = 2;  // default sampled 32-feature chunks per CTA
 constexpr int kPilotGroup = 8;   // scores per histogrammed group maximum
 constexpr int kPilotBins = 1 << kPilotBits;
 constexpr unsigned long long kPilotWaitNs = 200000;  // give up (no floor) after 200 us
@@ -51,6 +51,7 @@ struct FusedParams {
   int ab_format;       // 0 fp16, 1 bf16
   int w_evict_first;   // W is read once (single M tile): stream it past L2
   uint32_t index_offset;
+  int pilot_chunks;    // sampled 32-feature chunks per CTA (<= the first tile's chunks)
 };
 
 struct SimtParams {
@@ -110,9 +111,25 @@ struct SimtCfg {
   X(128, 256, 2, 32, false)  \
   X(128, 128, 3, 32, false)
 
-template <int L, int NT, int STAGES, int A, bool APP_SMEM>
-cudaError_t launch_fused(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tw32, const FusedParams& p,
-                         int grid, cudaStream_t stream);
+// Configurations of the fp32 (3-pass TF32) variant: same shared-memory plan
+// (X hi + lo tiles take the bytes of the 16-bit X tile, W + its residual those
+// of the 16-bit W tile, K = 16 per stage with 64-byte swizzle).
+#define STK_FUSED_TF32_CONFIGS(X) \
+  X(32, 256, 3, 32, true)         \
+  X(64, 256, 3, 16, true)         \
+  X(128, 256, 2, 32, false)       \
+  X(32, 128, 5, 32, true)         \
+  X(64, 128, 4, 16, true)         \
+  X(128, 128, 3, 32, false)
+
+// TF32: X is read through two maps (txl: the residual X - round_tf32(X));
+// otherwise txl is unused.
+template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TF32>
+cudaError_t launch_fused(const CUtensorMap& tx, const CUtensorMap& txl, const CUtensorMap& tw, const CUtensorMap& tw32,
+                         const FusedParams& p, int grid, cudaStream_t stream);
+
+// Xh = round_tf32(X), Xl = round_tf32(X - Xh), n elements.
+cudaError_t launch_split_tf32(const float* X, float* Xh, float* Xl, int64_t n, cudaStream_t stream);
 
 template <typename T, int L>
 cudaError_t launch_simt(const void* X, const void* W, const SimtParams& p, int grid, cudaStream_t stream);

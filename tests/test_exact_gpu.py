@@ -250,3 +250,48 @@ def test_exchange_single_rank_equals_exact(k):
         assert _capi.device_error(stream) == 0
     finally:
         lib.stk_exchange_destroy(h)
+
+
+@pytest.mark.parametrize("B,d,F,k", [(128, 768, 65536, 32), (64, 256, 30001, 64), (130, 100, 5000, 16),
+                                     (1, 64, 300, 8), (32, 2048, 20000, 128), (128, 2048, 262144, 64)])
+def test_tf32_path_matches_oracle(B, d, F, k):
+    """fp32 inputs on tensor cores (STK_FLAG_TF32: round_tf32 split, 3 passes) within the fp32 tolerance."""
+    from streamtopk_sae import _capi, native
+    X, W, b = oracle.gaussian_inputs(B, d, F, seed=B + d + k)
+    Xt, Wt, bt, Xr, Wr, br = device_inputs(X, W, b, "fp32")
+    V, I = native.streamtopk_cuda_exact_forward(Xt, Wt, bt, k, flags=_capi.STK_FLAG_TF32)
+    torch.cuda.synchronize()
+    no_device_error()
+    check(V, I, Xr, Wr, br, k, RTOL["fp32"])
+
+
+def test_tf32_path_ties_and_zero_x():
+    """All-equal scores rank by feature index on the TF32 path too."""
+    from streamtopk_sae import _capi, native
+    B, d, F, k = 16, 128, 3000, 32
+    X = torch.zeros(B, d, device="cuda")
+    W = torch.randn(F, d, device="cuda")
+    b = torch.zeros(F, device="cuda")
+    V, I = native.streamtopk_cuda_exact_forward(X, W, b, k, flags=_capi.STK_FLAG_TF32)
+    torch.cuda.synchronize()
+    assert torch.equal(I.cpu(), torch.arange(k, dtype=torch.int32).expand(B, k))
+    assert torch.all(V == 0)
+
+
+@pytest.mark.parametrize("B,d,F,k", [(128, 2048, 262144, 64), (128, 768, 65536, 32), (300, 256, 50000, 128)])
+def test_working_memory_is_the_workspace(B, d, F, k):
+    """Peak device memory of a call = inputs + V/I + the workspace the C ABI reports
+    (the reference's run_memory.py 'working memory'); no F-sized scratch."""
+    import streamtopk_sae as stk
+    from streamtopk_sae import _capi
+    X, W, b = stk.make_inputs(B, d, F, dtype=torch.bfloat16, seed=1, device="cuda")
+    stk.topk_sae_cuda_exact(X, W, b, k)          # first call: library and module setup
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats()
+    base = torch.cuda.memory_allocated()
+    stk.topk_sae_cuda_exact(X, W, b, k)
+    torch.cuda.synchronize()
+    working = torch.cuda.max_memory_allocated() - base - B * k * 8
+    ws = _capi.workspace_bytes(B, d, F, k, _capi.STK_BF16)
+    assert ws - 4096 <= working <= ws + 4096, (working, ws)
+    assert ws < 64 << 20 or B > 256
