@@ -83,6 +83,45 @@ def profiled_traffic(config_id, n_gpus):
     return None
 
 
+def float64_row_scores(X, W, b, rows, chunk=32768):
+    """float64 scores of the sampled rows over all features (on X's device)."""
+    import torch
+    Xs = X[rows].double()
+    out = torch.empty((len(rows), W.shape[0]), dtype=torch.float64, device=X.device)
+    for f0 in range(0, W.shape[0], chunk):
+        f1 = min(W.shape[0], f0 + chunk)
+        out[:, f0:f1] = Xs @ W[f0:f1].double().T + b[f0:f1].double()
+    return out
+
+
+def rows_match(V, I, S, k, rtol):
+    """Tie-aware check of sampled output rows against their float64 scores S.
+
+    Per row (v_k = k-th largest score, tau = rtol * max |top-k score|): sorted
+    values within tau of the true top-k, distinct indices, every predicted index
+    scoring >= v_k - tau, every index scoring > v_k + tau predicted, and each
+    value within tau of the score at its index.
+    """
+    import torch
+    for r in range(S.shape[0]):
+        top, _ = torch.topk(S[r], k)
+        vk = top[-1]
+        tau = rtol * max(float(top.abs().max()), 1e-30)
+        pv = V[r].double()
+        idx = I[r].long()
+        if int(idx.min()) < 0 or int(idx.max()) >= S.shape[1] or torch.unique(idx).numel() != k:
+            return False
+        si = S[r][idx]
+        if float((torch.sort(pv, descending=True).values - top).abs().max()) > tau:
+            return False
+        if float((pv - si).abs().max()) > tau or bool((si < vk - tau).any()):
+            return False
+        must = torch.nonzero(S[r] > vk + tau).flatten()
+        if must.numel() and not bool(torch.isin(must, idx).all()):
+            return False
+    return True
+
+
 class ClockSampler:
     """nvidia-smi samples of one GPU while the timed region runs."""
 
@@ -290,6 +329,15 @@ def run_b200(args, cfg):
     dtype = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}[cfg["dtype"]]
     X, W, b = stk.make_inputs(B, d, F, dtype=dtype, seed=0, device=dev, w_init=cfg["w_init"])
     f0, f1 = stk_shard.shard_bounds(F, world, rank)
+    # Correctness of what is timed (outside the timed region): float64 scores of
+    # a few rows over all F, and at N > 1 the single-GPU encode of the full
+    # W_enc on rank 0 (every rank holds the full W_enc before slicing).
+    check_rows = sorted({0, B // 3, (2 * B) // 3, B - 1})
+    S_rows = float64_row_scores(X, W, b, check_rows) if rank == 0 else None
+    single_gpu = None
+    if world > 1 and rank == 0:
+        single_gpu = stk.topk_sae_cuda_exact(X, W, b, k)
+        torch.cuda.synchronize(dev)
     if world > 1:
         W = W[f0:f1].clone()
         b = b[f0:f1].clone()
@@ -381,6 +429,20 @@ def run_b200(args, cfg):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     el_ms = float(t.item())
     value = B * args.steps / (el_ms / 1e3)
+
+    # ---------------- parity of the timed step (one more, untimed, call on every rank)
+    Vp, Ip = step(X)
+    torch.cuda.synchronize(dev)
+    parity = None
+    if rank == 0:
+        rtol = 1e-5 if cfg["dtype"] == "fp32" else 1e-3
+        parity = {"rows_vs_float64": rows_match(Vp[check_rows].cpu(), Ip[check_rows].cpu(), S_rows.cpu(), k, rtol),
+                  "rows_checked": len(check_rows), "rtol": rtol}
+        if single_gpu is not None:
+            parity["bitwise_vs_single_gpu"] = bool(torch.equal(Vp, single_gpu[0]) and torch.equal(Ip, single_gpu[1]))
+        parity["ok"] = all(v for kk, v in parity.items() if kk in ("rows_vs_float64", "bitwise_vs_single_gpu"))
+        S_rows = single_gpu = None
+    del Vp, Ip
 
     # ---------------- end to end through the public API, host buffers
     Xh = X.cpu().pin_memory()
@@ -493,6 +555,7 @@ def run_b200(args, cfg):
                               "streamtopk_sae.shard.ShardedEncoder.encode in a CUDA graph (graph.CapturedEncode)") +
                              (", X of step i+1 uploaded on a copy stream during step i, V/I read back on another"
                               if overlap else ", copies and kernels serialised on one stream"))},
+            "parity": parity,
             "gpu_launches": launches, "graph_steps": G, "clocks": clk.summary(),
             "exchange": (None if world == 1 else
                          "direct peer stores over NVLink (stk_exchange_*)" if enc.transport in ("p2p", "auto") else

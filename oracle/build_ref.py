@@ -12,7 +12,7 @@ also runs on the GPU box's host CPU.  Output goes only to ``oracle/_ref/``
 (git-ignored; it travels to the GPU box with the snapshot).  No reference
 source is copied into this repository.
 
-Usage: python oracle/build_ref.py [--ref /path/to/reference]
+Usage: python oracle/build_ref.py --ref <reference tree>   (or STK_REFERENCE_ROOT=<reference tree>)
 """
 import argparse
 import os
@@ -47,11 +47,12 @@ def build(ref_root: str, verbose: bool = False) -> str:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("STK_REFERENCE_ROOT"),
+                    help="root of the reference tree (default: $STK_REFERENCE_ROOT)")
     ap.add_argument("-v", action="store_true")
     a = ap.parse_args()
-    if not os.path.isdir(a.ref):
-        print(f"reference tree {a.ref} absent; skipping oracle/_ref build")
+    if not a.ref or not os.path.isdir(a.ref):
+        print(f"reference tree {a.ref!r} absent; skipping oracle/_ref build")
         return 0
     print(build(a.ref, a.v))
     return 0

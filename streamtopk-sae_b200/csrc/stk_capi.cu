@@ -854,16 +854,19 @@ int noalloc_scratch(void** out) {
 extern "C" int stk_exact_forward_noalloc(const void* X, const void* W, const float* b, float* V, int32_t* I,
                                          int64_t B, int64_t d, int64_t F, int64_t k, int dtype, int flags,
                                          void* stream) {
-  size_t need = 0;
-  if (stk_workspace_bytes(B, d, F, k, dtype, &need) == STK_OK && need > kNoAllocScratchBytes) {
-    return fail(STK_ENOSPACE, "stk_exact_forward_noalloc: this shape needs " + std::to_string(need) +
-                                  " bytes of scratch; the built-in scratch holds " +
-                                  std::to_string(kNoAllocScratchBytes) +
-                                  " bytes (use stk_exact_forward with a caller-allocated workspace)");
-  }
   void* scratch = nullptr;
   int rc = noalloc_scratch(&scratch);
   if (rc) return rc;
-  // Argument errors are reported by stk_exact_forward with the usual messages.
-  return stk_exact_forward(X, W, b, V, I, B, d, F, k, dtype, flags, scratch, kNoAllocScratchBytes, stream);
+  // Argument errors are reported by stk_exact_forward with the usual messages;
+  // it also checks this call's own plan (flags included) against the array.
+  rc = stk_exact_forward(X, W, b, V, I, B, d, F, k, dtype, flags, scratch, kNoAllocScratchBytes, stream);
+  if (rc == STK_ENOSPACE) {
+    Plan pl;
+    if (plan(X, W, B, d, F, k, dtype, flags, &pl) == STK_OK)
+      return fail(STK_ENOSPACE, "stk_exact_forward_noalloc: this shape needs " + std::to_string(pl.ws) +
+                                    " bytes of scratch; the built-in scratch holds " +
+                                    std::to_string(kNoAllocScratchBytes) +
+                                    " bytes (use stk_exact_forward with a caller-allocated workspace)");
+  }
+  return rc;
 }

@@ -8,13 +8,14 @@ selection fused into the GEMM epilogue.  ``shard`` adds the multi-GPU
 F-sharded encoder (one process per GPU; the per-rank key lists are exchanged
 by direct peer stores between the GPUs, or by an NCCL all-gather, then merged).
 """
-from streamtopk_sae.ops import topk_sae_cpu, topk_sae_cuda_approx, topk_sae_cuda_exact
+from streamtopk_sae.ops import check_device_errors, topk_sae_cpu, topk_sae_cuda_approx, topk_sae_cuda_exact
 from streamtopk_sae.utils import make_inputs, recall_at_k
 
 __all__ = [
     "topk_sae_cpu",
     "topk_sae_cuda_exact",
     "topk_sae_cuda_approx",
+    "check_device_errors",
     "recall_at_k",
     "make_inputs",
 ]

@@ -9,6 +9,15 @@ libstk_b200.so through its C ABI; there is no other compute path.
 Extensions (keyword-only, off by default so behaviour matches the reference):
   allow_any_k  accept any 1 <= k <= 128 instead of {1,2,4,8,16,32,64,128}
   allow_any_d  lift the exact path's d <= 4096 limit
+
+Device-side errors.  The kernels bound every wait (pipeline barriers: 4 s; the
+sampled-threshold barrier: 200 us, after which the kernel simply runs without
+the threshold).  A pipeline wait that runs out -- in practice only when the GPU
+is time-sliced away for seconds -- ends the kernel early and sets a device
+error word; the op itself cannot see it without synchronising.  Callers that
+need the guarantee call ``check_device_errors()`` at a synchronisation point
+they already have (it synchronises the current stream, reads and clears the
+word, and raises RuntimeError if a kernel reported an error).
 """
 from __future__ import annotations
 
@@ -60,6 +69,15 @@ def topk_sae_cuda_approx(X, W_enc, b_enc, k, c, candidate_buffer=None, *, allow_
     if candidate_buffer is not None:
         native.streamtopk_cuda_approx_forward(X, W_enc, b_enc, k, c, candidate_buffer)
     return native.approx_topk_forward(X, W_enc, b_enc, k, c, flags=_flags(allow_any_k, True))
+
+
+def check_device_errors(device=None):
+    """Synchronise the current stream of `device` and raise RuntimeError if a
+    library kernel reported a device-side error (a bounded wait that ran out)
+    since the last check; the error word is cleared."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        _capi.device_error(torch.cuda.current_stream(dev).cuda_stream)
 
 
 def topk_sae_cpu(X, W_enc, b_enc, k):

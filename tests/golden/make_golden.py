@@ -3,8 +3,10 @@
 Run in a container where the reference tree exists (it is not needed at test
 time):
 
-    python oracle/build_ref.py            # compiles the reference CPU op into oracle/_ref/
-    python tests/golden/make_golden.py    # writes tests/golden/golden_cpu.npz
+    python oracle/build_ref.py --ref <reference tree>          # reference CPU op -> oracle/_ref/
+    python tests/golden/make_golden.py --ref <reference tree>  # writes tests/golden/golden_cpu.npz
+
+(or set STK_REFERENCE_ROOT instead of passing --ref)
 
 Every output in the fixture is produced by the reference's own code:
   * ``streamtopk_cpu_forward`` compiled from the reference sources
@@ -83,7 +85,8 @@ SYN_CASES = {
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("STK_REFERENCE_ROOT"), required="STK_REFERENCE_ROOT" not in os.environ,
+                    help="root of the reference tree (default: $STK_REFERENCE_ROOT)")
     ap.add_argument("--out", default=os.path.join(HERE, "golden_cpu.npz"))
     a = ap.parse_args()
     import torch

@@ -40,3 +40,29 @@ def check(V, I, Xr, Wr, br, k, rtol, oracle_res=None):
 def no_device_error():
     from streamtopk_sae import _capi
     assert _capi.device_error(torch.cuda.current_stream().cuda_stream) == 0
+
+
+class HostRows:
+    """Row access to a (F, d) matrix held on the host in a 16-bit torch dtype.
+
+    The float64 oracle (oracle.exact_topk_f64 / check_topk) slices W by row
+    ranges and by index arrays; this returns those rows as float32 numpy arrays
+    (exactly the values the GPU read), so matrices of several GB need not be
+    expanded to float32 all at once.
+    """
+
+    def __init__(self, t):
+        self.t = t.detach().cpu().contiguous()
+        self.shape = tuple(self.t.shape)
+
+    def __getitem__(self, key):
+        if isinstance(key, np.ndarray):
+            key = torch.from_numpy(key.astype(np.int64))
+        return self.t[key].float().numpy()
+
+
+def sample_rows(n_rows, B, seed=0):
+    """Sorted row sample (always includes the first and last row)."""
+    rng = np.random.default_rng(seed)
+    rows = set(rng.choice(B, size=min(n_rows, B), replace=False).tolist()) | {0, B - 1}
+    return np.array(sorted(rows), dtype=np.int64)
