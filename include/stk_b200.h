@@ -50,7 +50,9 @@ enum stk_flags {
   STK_FLAG_ANY_D = 2, /* lift the reference's d <= 4096 limit */
   STK_FLAG_SIMT = 4,    /* force the fp32 SIMT kernel (testing / comparison) */
   STK_FLAG_NO_PILOT = 8, /* skip the sampled threshold floor (testing / comparison) */
-  STK_FLAG_TF32 = 16     /* fp32 inputs on tensor cores: 3-pass TF32 (hi*hi + hi*lo + lo*hi), d % 4 == 0 */
+  STK_FLAG_TF32 = 16,    /* fp32 inputs on tensor cores: 3-pass TF32 (hi*hi + hi*lo + lo*hi), d % 4 == 0 */
+  STK_FLAG_SEPARATE_FINISH = 32 /* finish the rows in a second kernel even where the score kernel
+                                   could do it in its tail (testing / comparison) */
 };
 
 /* Library version (major * 10000 + minor * 100 + patch). */
@@ -109,9 +111,12 @@ STK_API int stk_approx_candidates(const void* X, const void* W, const float* b, 
 STK_API int stk_candidates_workspace_bytes(int64_t B, int64_t d, int64_t F, int64_t c, int dtype, size_t* bytes);
 
 /*
- * One F-shard of a multi-GPU encode: the best L = stk_list_len(k) keys per row
- * of this shard, with feature indices offset by `index_offset`, written as
- * sorted 64-bit keys to keys_out (B, L).  Keys from several shards are
+ * One F-shard of a multi-GPU encode: per row of this shard, with feature
+ * indices offset by `index_offset`, sorted 64-bit keys in keys_out (B, L),
+ * L = stk_list_len(k): the shard's exact top k, then further keys of the
+ * shard in descending order (not necessarily the next best), then empty keys
+ * (0).  Key = (order-preserving bits of the fp32 score << 32) | ~feature.
+ * keys_out must be 16-byte aligned.  Keys from several shards are
  * combined by stk_merge_keys.  (No reference counterpart: the reference has no
  * multi-GPU path.)
  */
@@ -122,8 +127,9 @@ STK_API int stk_shard_forward(const void* X, const void* W_shard, const float* b
 /*
  * Final merge of n key lists per row: lists (n, B, L) as written by
  * stk_shard_forward (e.g. after an all-gather), L = stk_list_len(k).
- * Writes V (B, k) fp32 and I (B, k) int32.  Replaces the reference's merge
- * pass (streamtopk_exact.cu:429-499) for the cross-GPU step.
+ * Writes V (B, k) fp32 and I (B, k) int32.  lists must be 16-byte aligned.
+ * Replaces the reference's merge pass (streamtopk_exact.cu:429-499) for the
+ * cross-GPU step.
  */
 STK_API int stk_merge_keys(const uint64_t* lists, int64_t nlists, int64_t B, int64_t k, float* V, int32_t* I,
                    void* stream);
@@ -156,15 +162,21 @@ STK_API int stk_exact_forward_noalloc(const void* X, const void* W, const float*
  * top-L key lists, merge).  One process per GPU, all GPUs on one node with
  * peer access (NVLink); at most 8 ranks.  Replaces the all-gather + merge of
  * stk_shard_forward / stk_merge_keys with peer stores: each rank writes its
- * lists straight into every rank's receive buffer and bumps that rank's
- * arrival counter; each rank's final merge waits for all ranks' rows (bounded
- * by wait_seconds, after which it reports device error 3 through
- * stk_device_error and the exchange must be destroyed and re-created).
+ * rows' best keys straight into every rank's receive buffer and sets a per-row
+ * flag there to the step number; each rank waits for all ranks' rows (bounded
+ * by wait_seconds) and finishes them.  All of this runs in the tail of the
+ * score kernel when its units are all resident at once (one launch per step),
+ * else in one finish kernel after it.  A wait that runs out reports device
+ * error 3 through stk_device_error; that step's rows are then finished over
+ * the ranks whose rows had arrived.  Steps are tagged with their absolute
+ * number, so rows that arrive late are never taken for a later step's rows
+ * (a rank that skipped a step entirely leaves the ranks one step apart, and
+ * every later step times out until the exchange is re-created).
  *
  * Setup (collective: every rank, same world / max_rows / k):
  *   stk_exchange_bytes -> allocate a 256-byte aligned device buffer of that size
  *     (plain cudaMalloc-backed memory: cudaIpcGetMemHandle must accept it)
- *   stk_exchange_create (clears its counters, synchronously)
+ *   stk_exchange_create (clears its flags, synchronously)
  *   stk_exchange_ipc_handle -> share the STK_IPC_HANDLE_BYTES handle + offset
  *     with every rank (any host transport)
  *   stk_exchange_connect with all ranks' handles / offsets (rank order)
@@ -193,8 +205,9 @@ STK_API int stk_exchange_destroy(stk_exchange* ex);
  * Profiling hook (no reference counterpart).  stk_profile_begin arms CUDA
  * events around each kernel launched by the calls that follow (up to
  * max_launches launches, any thread); stk_profile_end synchronises them and
- * returns, per kernel kind (0 fused tcgen05 score kernel, 1 SIMT score
- * kernel, 2 merge kernel, 3 exchange publish + final merge), the summed
+ * returns, per kernel kind (0 fused tcgen05 score kernel, its finish step
+ * included when it runs in the kernel's tail; 1 SIMT score kernel; 2 standalone
+ * finish kernel; 3 standalone finish kernel with the exchange), the summed
  * device time in ms and the number of launches.  No work is skipped or reordered.
  */
 STK_API int stk_profile_begin(int64_t max_launches);

@@ -208,14 +208,19 @@ struct Plan {
   stk::UnitGrid grid;
   int ctas;
   bool pilot;
+  bool fin_fused;  // the fused kernel finishes the rows itself (all units resident at once)
   size_t ws_partials;
   size_t ws_app;
-  size_t ws_pilot;
+  size_t ws_sync;   // zeroed per call: barrier counters, then the pilot histogram and row maxima
   size_t ws_split;  // TF32: round_tf32(X) and its residual, each 256-byte aligned
   size_t ws;
 };
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Counters at the start of the zeroed sync region: [0] pilot arrivals,
+// [1] finish-barrier arrivals; the pilot histogram follows at kSyncBytes.
+constexpr size_t kSyncBytes = 256;
 
 int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t k, int dtype, int flags, Plan* pl) {
   int sms = 0;
@@ -236,9 +241,13 @@ int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t 
   // pays off when each CTA streams several chunks after its sample.
   pl->pilot = pl->tc && pl->grid.units <= pl->ctas && pl->grid.m_tiles <= 2 &&
               pl->grid.nchunks >= 4 * (int64_t)pl->grid.segs && !(flags & STK_FLAG_NO_PILOT);
-  pl->ws_pilot = pl->pilot ? (size_t)pl->grid.m_tiles * stk::kRows * (stk::kPilotBins + 1) * 4 + 256 : 0;
+  // One unit per CTA and every CTA resident (one per SM): the fused kernel
+  // meets at a grid barrier and finishes the rows itself, no second launch.
+  pl->fin_fused = pl->tc && pl->grid.units <= pl->ctas && !(flags & STK_FLAG_SEPARATE_FINISH);
+  const size_t pilot_bytes = pl->pilot ? (size_t)pl->grid.m_tiles * stk::kRows * (stk::kPilotBins + 1) * 4 : 0;
+  pl->ws_sync = (pl->pilot || pl->fin_fused) ? ((kSyncBytes + pilot_bytes + 255) & ~size_t(255)) : 0;
   pl->ws_split = pl->tf32 ? 2 * (((size_t)B * d * 4 + 255) & ~size_t(255)) : 0;
-  pl->ws = pl->ws_partials + pl->ws_app + pl->ws_pilot + pl->ws_split;
+  pl->ws = pl->ws_partials + pl->ws_app + pl->ws_sync + pl->ws_split;
   return STK_OK;
 }
 
@@ -257,7 +266,8 @@ bool fused_override(int L, int* nt, int* stages, int* app, int* app_smem) {
 }
 
 int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint64_t* partials, uint64_t* app,
-              int64_t B, int64_t d, int64_t F, int64_t k, int dtype, uint32_t index_offset, cudaStream_t stream) {
+              int64_t B, int64_t d, int64_t F, int64_t k, int dtype, uint32_t index_offset,
+              const stk::FinishArgs* fin, cudaStream_t stream) {
   // Defaults: 256-feature tiles, append slots in shared memory where 3
   // pipeline stages still fit.  When a CTA's unit fits in one such tile (F
   // small per CTA, e.g. one shard of a multi-GPU encode) 128-feature tiles
@@ -278,7 +288,7 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   if (pl.tf32) {
     // X is split once per call into round_tf32(X) and its residual (L2-resident,
     // re-read by every tile); W is split tile by tile inside the kernel.
-    uint8_t* split = reinterpret_cast<uint8_t*>(partials) + pl.ws_partials + pl.ws_app + pl.ws_pilot;
+    uint8_t* split = reinterpret_cast<uint8_t*>(partials) + pl.ws_partials + pl.ws_app + pl.ws_sync;
     float* xh = reinterpret_cast<float*>(split);
     float* xl = reinterpret_cast<float*>(split + pl.ws_split / 2);
     cudaError_t se = stk::launch_split_tf32(static_cast<const float*>(X), xh, xl, B * d, stream);
@@ -314,13 +324,23 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   p.pilot_hist = nullptr;
   p.pilot_rowmax = nullptr;
   p.pilot_count = nullptr;
-  if (pl.pilot) {
+  p.tail_count = nullptr;
+  p.finish = 0;
+  std::memset(&p.fin, 0, sizeof p.fin);
+  if (pl.ws_sync) {
     uint8_t* base = reinterpret_cast<uint8_t*>(partials) + pl.ws_partials + pl.ws_app;
-    p.pilot_hist = reinterpret_cast<uint32_t*>(base);
-    p.pilot_rowmax = p.pilot_hist + (size_t)pl.grid.m_tiles * stk::kRows * stk::kPilotBins;
-    p.pilot_count = p.pilot_rowmax + (size_t)pl.grid.m_tiles * stk::kRows;
-    cudaError_t me = cudaMemsetAsync(base, 0, pl.ws_pilot, stream);
-    if (me != cudaSuccess) return cuda_fail(me, "cudaMemsetAsync(pilot)");
+    p.pilot_count = reinterpret_cast<uint32_t*>(base);
+    p.tail_count = p.pilot_count + 1;
+    if (pl.pilot) {
+      p.pilot_hist = reinterpret_cast<uint32_t*>(base + kSyncBytes);
+      p.pilot_rowmax = p.pilot_hist + (size_t)pl.grid.m_tiles * stk::kRows * stk::kPilotBins;
+    }
+    cudaError_t me = cudaMemsetAsync(base, 0, pl.ws_sync, stream);
+    if (me != cudaSuccess) return cuda_fail(me, "cudaMemsetAsync(sync)");
+  }
+  if (fin) {
+    p.finish = 1;
+    p.fin = *fin;
   }
   cudaError_t e = cudaErrorInvalidValue;
   ProfScope prof(kProfFused, stream);
@@ -366,15 +386,57 @@ int run_simt(const Plan& pl, const void* X, const void* W, const float* b, uint6
   return STK_OK;
 }
 
-int run_merge(int L, const uint64_t* lists, int nlists, int64_t list_stride, int64_t rows, int64_t k, float* V,
-              int32_t* I, uint64_t* keys_out, cudaStream_t stream) {
+// Standalone finish kernel (kind: kProfMerge, or kProfExchange with the
+// exchange).  With the exchange every CTA must be resident at once (each
+// publishes all of its rows before it waits), so the grid is capped.
+int run_finish(int L, const stk::FinishArgs& fa, cudaStream_t stream) {
+  int sms = 0;
+  int rc = device_sms(&sms);
+  if (rc) return rc;
+  int64_t grid = fa.rows;
+  if (fa.use_ex && grid > 4 * (int64_t)sms) grid = 4 * (int64_t)sms;
+  if (grid > 0x7fffffff) grid = 0x7fffffff;
   cudaError_t e = cudaErrorInvalidValue;
-  ProfScope prof(kProfMerge, stream);
-  if (L == 32) e = stk::launch_merge<32>(lists, nlists, list_stride, rows, (int)k, V, I, keys_out, stream);
-  if (L == 64) e = stk::launch_merge<64>(lists, nlists, list_stride, rows, (int)k, V, I, keys_out, stream);
-  if (L == 128) e = stk::launch_merge<128>(lists, nlists, list_stride, rows, (int)k, V, I, keys_out, stream);
-  if (e != cudaSuccess) return cuda_fail(e, "merge_lists_kernel launch");
+  ProfScope prof(fa.use_ex ? kProfExchange : kProfMerge, stream);
+  if (L == 32) e = stk::launch_finish<32>(fa, (int)grid, stream);
+  if (L == 64) e = stk::launch_finish<64>(fa, (int)grid, stream);
+  if (L == 128) e = stk::launch_finish<128>(fa, (int)grid, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "finish_kernel launch");
   return STK_OK;
+}
+
+stk::FinishArgs finish_args(const uint64_t* lists, int nlists, int64_t stride, int64_t rows, int64_t k, float* V,
+                            int32_t* I, uint64_t* keys_out, const stk::ExchangeDev* ex) {
+  stk::FinishArgs fa;
+  std::memset(&fa, 0, sizeof fa);
+  fa.lists = lists;
+  fa.nlists = nlists;
+  fa.stride = stride;
+  fa.rows = rows;
+  fa.k = (int)k;
+  fa.V = V;
+  fa.I = I;
+  fa.keys_out = keys_out;
+  fa.use_ex = ex != nullptr;
+  if (ex) fa.ex = *ex;
+  return fa;
+}
+
+// Scores + per-unit lists, then the finish step: in the fused kernel's tail
+// when its units are all resident at once, else as a second kernel.
+int score_and_finish(const Plan& pl, const void* X, const void* W, const float* b, float* V, int32_t* I,
+                     uint64_t* keys_out, int64_t B, int64_t d, int64_t F, int64_t k, int dtype, uint32_t index_offset,
+                     const stk::ExchangeDev* ex, void* workspace, cudaStream_t stream) {
+  uint64_t* partials = static_cast<uint64_t*>(workspace);
+  uint64_t* app = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + pl.ws_partials);
+  const stk::FinishArgs fa = finish_args(partials, pl.grid.segs, (int64_t)pl.grid.m_tiles * stk::kRows, B, k, V, I,
+                                         keys_out, ex);
+  int rc = pl.tc ? run_fused(pl, X, W, b, partials, app, B, d, F, k, dtype, index_offset,
+                             pl.fin_fused ? &fa : nullptr, stream)
+                 : run_simt(pl, X, W, b, partials, app, B, d, F, k, dtype, index_offset, stream);
+  if (rc) return rc;
+  if (pl.tc && pl.fin_fused) return STK_OK;
+  return run_finish(pl.L, fa, stream);
 }
 
 int check_common(const char* op, int64_t B, int64_t d, int64_t F, int dtype) {
@@ -395,13 +457,7 @@ int encode(const void* X, const void* W, const float* b, float* V, int32_t* I, u
   if (B == 0) return STK_OK;
   if (workspace_bytes < pl.ws || (pl.ws && workspace == nullptr))
     return fail(STK_ENOSPACE, "workspace too small (need " + std::to_string(pl.ws) + " bytes)");
-  uint64_t* partials = static_cast<uint64_t*>(workspace);
-  uint64_t* app = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + pl.ws_partials);
-  rc = pl.tc ? run_fused(pl, X, W, b, partials, app, B, d, F, k, dtype, index_offset, stream)
-             : run_simt(pl, X, W, b, partials, app, B, d, F, k, dtype, index_offset, stream);
-  if (rc) return rc;
-  return run_merge(pl.L, partials, pl.grid.segs, (int64_t)pl.grid.m_tiles * stk::kRows, B, k, V, I, keys_out,
-                   stream);
+  return score_and_finish(pl, X, W, b, V, I, keys_out, B, d, F, k, dtype, index_offset, nullptr, workspace, stream);
 }
 
 }  // namespace
@@ -467,22 +523,10 @@ int stk_shard_forward(const void* X, const void* W_shard, const float* b_shard, 
   if (index_offset < 0 || index_offset + F_shard > 0x7fffffffLL)
     return fail(STK_EINVAL, "index_offset + F_shard must fit int32 indices");
   if (!keys_out) return fail(STK_EINVAL, "keys_out is NULL");
-  // V/I of the shard-local merge are not needed; only the sorted keys.
-  const int L = list_len(k);
-  Plan pl;
-  rc = plan(X, W_shard, B, d, F_shard, k, dtype, flags, &pl);
-  if (rc) return rc;
-  if (B == 0) return STK_OK;
-  if (workspace_bytes < pl.ws || (pl.ws && workspace == nullptr))
-    return fail(STK_ENOSPACE, "workspace too small (need " + std::to_string(pl.ws) + " bytes)");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  uint64_t* partials = static_cast<uint64_t*>(workspace);
-  uint64_t* app = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + pl.ws_partials);
-  rc = pl.tc ? run_fused(pl, X, W_shard, b_shard, partials, app, B, d, F_shard, k, dtype, (uint32_t)index_offset, s)
-             : run_simt(pl, X, W_shard, b_shard, partials, app, B, d, F_shard, k, dtype, (uint32_t)index_offset, s);
-  if (rc) return rc;
-  return run_merge(L, partials, pl.grid.segs, (int64_t)pl.grid.m_tiles * stk::kRows, B, 0, nullptr, nullptr,
-                   keys_out, s);
+  if (reinterpret_cast<uintptr_t>(keys_out) & 15) return fail(STK_EINVAL, "keys_out must be 16-byte aligned");
+  // Only the sorted keys leave this call (no V/I).
+  return encode(X, W_shard, b_shard, nullptr, nullptr, keys_out, B, d, F_shard, k, dtype, flags,
+                (uint32_t)index_offset, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 int stk_merge_keys(const uint64_t* lists, int64_t nlists, int64_t B, int64_t k, float* V, int32_t* I,
@@ -490,7 +534,10 @@ int stk_merge_keys(const uint64_t* lists, int64_t nlists, int64_t B, int64_t k, 
   if (k < 1 || k > 128) return fail(STK_EINVAL, "k out of range");
   if (nlists < 1) return fail(STK_EINVAL, "nlists must be >= 1");
   if (B < 0) return fail(STK_EINVAL, "B must be >= 0");
-  return run_merge(list_len(k), lists, (int)nlists, B, B, k, V, I, nullptr, static_cast<cudaStream_t>(stream));
+  if (nlists > 0x7fffffff) return fail(STK_EINVAL, "nlists out of range");
+  if (reinterpret_cast<uintptr_t>(lists) & 15) return fail(STK_EINVAL, "lists must be 16-byte aligned");
+  return run_finish(list_len(k), finish_args(lists, (int)nlists, B, B, k, V, I, nullptr, nullptr),
+                    static_cast<cudaStream_t>(stream));
 }
 
 // Plan of the candidates path: one unit per 128-feature tile, list length L >= c.
@@ -507,7 +554,8 @@ int candidates_plan(const void* X, const void* W, int64_t B, int64_t d, int64_t 
   pl->pilot = false;
   pl->ws_partials = (partial_bytes(pl->grid, pl->L) + 255) & ~size_t(255);
   pl->ws_app = ((size_t)pl->ctas * stk::kAppendBytesPerCta + 255) & ~size_t(255);
-  pl->ws_pilot = 0;
+  pl->ws_sync = 0;
+  pl->fin_fused = false;
   pl->tf32 = false;
   pl->ws_split = 0;
   pl->ws = pl->ws_partials + pl->ws_app;
@@ -544,7 +592,7 @@ int stk_approx_candidates(const void* X, const void* W, const float* b, float* c
   uint64_t* partials = static_cast<uint64_t*>(workspace);
   uint64_t* app = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + pl.ws_partials);
   // Every tile keeps its best L >= c scores per row (k = c); no threshold floor.
-  rc = pl.tc ? run_fused(pl, X, W, b, partials, app, B, d, F, c, dtype, 0u, s)
+  rc = pl.tc ? run_fused(pl, X, W, b, partials, app, B, d, F, c, dtype, 0u, nullptr, s)
              : run_simt(pl, X, W, b, partials, app, B, d, F, c, dtype, 0u, s);
   if (rc) return rc;
   cudaError_t e = stk::launch_candidates_out(partials, pl.L, pl.grid.m_tiles, pl.grid.segs, B, (int)c, cand_vals,
@@ -623,15 +671,16 @@ struct stk_exchange {
 
 namespace {
 
+// recv [2][world][max_rows][L] keys, flag [2][world][max_rows] u64, state (256 B).
 struct ExchangeLayout {
-  size_t recv, arrive, state, total;
+  size_t recv, flag, state, total;
 };
 
 ExchangeLayout exchange_layout(int world, int64_t max_rows, int L) {
   ExchangeLayout x;
   x.recv = 0;
-  x.arrive = (size_t(2) * world * max_rows * L * 8 + 255) & ~size_t(255);
-  x.state = x.arrive + ((size_t(2) * world * 8 + 255) & ~size_t(255));
+  x.flag = (size_t(2) * world * max_rows * L * 8 + 255) & ~size_t(255);
+  x.state = x.flag + ((size_t(2) * world * max_rows * 8 + 255) & ~size_t(255));
   x.total = x.state + 256;
   return x;
 }
@@ -673,9 +722,9 @@ int stk_exchange_create(int rank, int world, int64_t max_rows, int64_t k, void* 
   cudaError_t e = cudaGetDevice(&device);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   char* base = static_cast<char*>(buffer);
-  // Counters and the step start at zero; synchronous, so that no peer can
+  // Flags and the step start at zero; synchronous, so that no peer can
   // store into the buffer before it is cleared.
-  e = cudaMemset(base + lay.arrive, 0, lay.total - lay.arrive);
+  e = cudaMemset(base + lay.flag, 0, lay.total - lay.flag);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return cuda_fail(e, "exchange buffer clear");
   stk_exchange* x = new (std::nothrow) stk_exchange();
@@ -683,14 +732,14 @@ int stk_exchange_create(int rank, int world, int64_t max_rows, int64_t k, void* 
   x->device = device;
   x->L = L;
   x->dev.recv = reinterpret_cast<uint64_t*>(base + lay.recv);
-  x->dev.arrive = reinterpret_cast<unsigned long long*>(base + lay.arrive);
+  x->dev.flag = reinterpret_cast<unsigned long long*>(base + lay.flag);
   x->dev.state = reinterpret_cast<unsigned long long*>(base + lay.state);
   x->dev.rank = rank;
   x->dev.world = world;
   x->dev.max_rows = max_rows;
   x->dev.wait_ns = (unsigned long long)(wait_seconds * 1e9);
   x->dev.peer_recv[rank] = x->dev.recv;
-  x->dev.peer_arrive[rank] = x->dev.arrive;
+  x->dev.peer_flag[rank] = x->dev.flag;
   *out = x;
   return STK_OK;
 }
@@ -724,7 +773,7 @@ int stk_exchange_connect(stk_exchange* x, const void* handles, const int64_t* of
     x->mapped[p] = m;
     char* peer = static_cast<char*>(m) + offsets[p];
     x->dev.peer_recv[p] = reinterpret_cast<uint64_t*>(peer + lay.recv);
-    x->dev.peer_arrive[p] = reinterpret_cast<unsigned long long*>(peer + lay.arrive);
+    x->dev.peer_flag[p] = reinterpret_cast<unsigned long long*>(peer + lay.flag);
   }
   return STK_OK;
 }
@@ -756,31 +805,11 @@ int stk_exchange_forward(stk_exchange* x, const void* X, const void* W_shard, co
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (device != x->device) return fail(STK_EINVAL, "current device is not the exchange's device");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  uint64_t* partials = static_cast<uint64_t*>(workspace);
-  int nlists = 0;
-  int64_t stride = 0;
-  if (F_shard > 0) {
-    uint64_t* app = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + pl.ws_partials);
-    rc = pl.tc ? run_fused(pl, X, W_shard, b_shard, partials, app, B, d, F_shard, k, dtype, (uint32_t)index_offset, s)
-               : run_simt(pl, X, W_shard, b_shard, partials, app, B, d, F_shard, k, dtype, (uint32_t)index_offset,
-                          s);
-    if (rc) return rc;
-    nlists = pl.grid.segs;
-    stride = (int64_t)pl.grid.m_tiles * stk::kRows;
-  }
-  {
-    ProfScope prof(kProfExchange, s);
-    e = cudaErrorInvalidValue;
-    if (x->L == 32) e = stk::launch_publish<32>(partials, nlists, stride, B, (int)k, x->dev, s);
-    if (x->L == 64) e = stk::launch_publish<64>(partials, nlists, stride, B, (int)k, x->dev, s);
-    if (x->L == 128) e = stk::launch_publish<128>(partials, nlists, stride, B, (int)k, x->dev, s);
-    if (e != cudaSuccess) return cuda_fail(e, "publish_kernel launch");
-    if (x->L == 32) e = stk::launch_exchange_merge<32>(x->dev, B, (int)k, V, I, s);
-    if (x->L == 64) e = stk::launch_exchange_merge<64>(x->dev, B, (int)k, V, I, s);
-    if (x->L == 128) e = stk::launch_exchange_merge<128>(x->dev, B, (int)k, V, I, s);
-    if (e != cudaSuccess) return cuda_fail(e, "exchange_merge_kernel launch");
-  }
-  return STK_OK;
+  if (F_shard > 0)
+    return score_and_finish(pl, X, W_shard, b_shard, V, I, nullptr, B, d, F_shard, k, dtype, (uint32_t)index_offset,
+                            &x->dev, workspace, s);
+  // Empty shard: publish empty lists (every rank's finish waits for all ranks).
+  return run_finish(x->L, finish_args(nullptr, 0, 0, B, k, V, I, nullptr, &x->dev), s);
 }
 
 int stk_exchange_destroy(stk_exchange* x) {

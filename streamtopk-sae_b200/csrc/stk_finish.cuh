@@ -1,0 +1,269 @@
+// Finish step of an encode: the top-k of each row over the sorted key lists the
+// score kernel left per work unit (pass 2 of the reference,
+// streamtopk_sae/csrc/cuda/streamtopk_exact.cu:429-499), optionally followed by
+// the cross-GPU exchange of the F-sharded encode.
+//
+// Runs either in the tail of the fused score kernel (all CTAs meet at a bounded
+// grid barrier once every unit's lists are stored, then each CTA finishes rows
+// blockIdx.x, blockIdx.x + gridDim.x, ...) or as the standalone finish_kernel
+// after a score kernel whose units cannot all be resident at once.  Both give
+// bit-identical results: keys are unique, so a row's top-k is unique.
+//
+// Per row:
+//   1. tau = the k-th largest list head.  The k largest heads are k distinct
+//      keys, so the row's k-th key is >= tau (tau = 1, every key, when fewer
+//      than k lists are non-empty).
+//   2. Every key >= tau is gathered into shared memory (one thread per list; a
+//      list is read 4 keys at a time until a key below tau: lists are sorted).
+//      The score kernel's lists are sparse -- each key passed the row's
+//      threshold floor -- so this is ~1.3 k keys per row on Gaussian data.
+//   3. Each candidate's position in the row's sorted result is the number of
+//      larger candidates (keys are distinct): one thread per candidate.
+//   More candidates than kFinishCap (adversarial inputs): the lists are folded
+//   instead, warp by warp, with a warp-cooperative bitonic merge.
+//
+// Exchange (ExchangeDev, one process per GPU): a row's best L keys are stored
+// into slot [step & 1][rank] of every rank's receive buffer (plain stores into
+// the peers' memory over NVLink, CUDA IPC mappings), and after a system-scope
+// fence a per-row flag in the peer's memory is set to step + 1.  Each rank then
+// waits (bounded) until the flags of all ranks' copies of its rows read
+// step + 1, and finishes the rows over the world lists.  The step tag is
+// absolute, so rows that arrive after a wait gave up can never be taken for a
+// later step's rows; double buffering by step parity is race-free because a
+// rank starts step s + 2 only after its step s + 1, which needed every rank's
+// step s + 1 rows, which each rank stores only after finishing its step s.
+#pragma once
+#include "stk_kernels.cuh"
+
+namespace stk {
+
+constexpr int kFinishCap = 1024;      // candidates ranked by counting
+constexpr int kFinishMaxLists = 256;  // lists whose heads are held in shared memory
+constexpr int kFoldBatch = 8;         // lists loaded per warp and memory round trip (fold)
+constexpr int kFinishMaxWarps = 8;    // fold tree buffer: kFinishMaxWarps * L <= kFinishCap
+
+struct FinishSmem {
+  uint64_t heads[kFinishMaxLists];
+  uint64_t cand[kFinishCap];
+  uint64_t best[128];
+  uint64_t tau;
+  int cnt;
+  uint32_t valid;
+};
+
+// g_device_error: the device error word, defined by the translation unit
+// that includes this header (stk_kernels.cu), ahead of the include.
+__device__ __forceinline__ void raise_device_error(unsigned code) { atomicCAS(&g_device_error, 0u, code); }
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ bool list_on(uint32_t mask, int s) { return s >= 32 || ((mask >> s) & 1u); }
+
+// Best L keys of row b over the nlists sorted lists (list s of row b at
+// lists[(s * stride + b) * L], L keys, descending, empty keys 0 at the end),
+// written to sm.best[0..L) descending with empty keys after the last one.
+// Lists s < 32 whose bit is clear in list_mask count as empty.  Every thread of
+// the CTA calls it (nthreads = blockDim.x, at most kFinishMaxWarps warps); it
+// ends with a __syncthreads.  Lists must be 16-byte aligned.
+template <int L>
+__device__ void select_row(const uint64_t* __restrict__ lists, int nlists, int64_t stride, int64_t b, int k,
+                           uint32_t list_mask, FinishSmem& sm, int tid, int nthreads) {
+  const bool use_heads = nlists <= kFinishMaxLists;
+  if (tid == 0) {
+    sm.tau = 1ull;
+    sm.cnt = 0;
+  }
+  if (use_heads)
+    for (int s = tid; s < nlists; s += nthreads)
+      sm.heads[s] = list_on(list_mask, s)
+                        ? (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(lists + ((int64_t)s * stride + b) * L))
+                        : 0ull;
+  __syncthreads();
+  if (use_heads) {
+    for (int s = tid; s < nlists; s += nthreads) {
+      const uint64_t h = sm.heads[s];
+      if (h == 0ull) continue;
+      int r = 0;
+      for (int j = 0; j < nlists; ++j) r += sm.heads[j] > h ? 1 : 0;
+      if (r == k - 1) sm.tau = h;
+    }
+  }
+  __syncthreads();
+  const uint64_t tau = sm.tau;
+  if (use_heads) {
+    for (int s = tid; s < nlists; s += nthreads) {
+      if (sm.heads[s] < tau) continue;  // empty lists too (tau >= 1)
+      const uint64_t* ps = lists + ((int64_t)s * stride + b) * L;
+      for (int q = 0; q < L; q += 4) {
+        const ulonglong2 u0 = __ldcg(reinterpret_cast<const ulonglong2*>(ps + q));
+        const ulonglong2 u1 = __ldcg(reinterpret_cast<const ulonglong2*>(ps + q + 2));
+        const uint64_t kk[4] = {u0.x, u0.y, u1.x, u1.y};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (kk[j] >= tau) {
+            const int pos = atomicAdd(&sm.cnt, 1);
+            if (pos < kFinishCap) sm.cand[pos] = kk[j];
+          }
+        }
+        if (kk[3] < tau) break;  // sorted: the rest is smaller
+      }
+    }
+  }
+  __syncthreads();
+  const int C = use_heads ? sm.cnt : kFinishCap + 1;
+  if (C <= kFinishCap) {
+    for (int i = tid; i < C; i += nthreads) {
+      const uint64_t key = sm.cand[i];
+      int r = 0;
+      for (int j = 0; j < C; ++j) r += sm.cand[j] > key ? 1 : 0;
+      if (r < L) sm.best[r] = key;
+    }
+    for (int i = C + tid; i < L; i += nthreads) sm.best[i] = 0ull;
+    __syncthreads();
+    return;
+  }
+  // Fold: warp w merges lists w, w + nw, ... into its best L (a list whose
+  // best key does not beat the warp's current L-th is skipped), then warp 0
+  // merges the warps' results.
+  constexpr int E = L / 32;
+  const int warp = tid >> 5, lane = tid & 31, nw = nthreads >> 5;
+  uint64_t acc[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) acc[e] = 0ull;
+  for (int s0 = warp; s0 < nlists; s0 += nw * kFoldBatch) {
+    uint64_t buf[kFoldBatch][E];
+#pragma unroll
+    for (int q = 0; q < kFoldBatch; ++q) {
+      const int s = s0 + q * nw;
+      const bool on = s < nlists && list_on(list_mask, s) && (!use_heads || sm.heads[s] >= tau);
+      const uint64_t* ps = lists + ((int64_t)s * stride + b) * L;
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+        buf[q][e] = on ? (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(ps + e * 32 + lane)) : 0ull;
+    }
+#pragma unroll
+    for (int q = 0; q < kFoldBatch; ++q) {
+      const uint64_t hi = __shfl_sync(0xffffffffu, buf[q][0], 0);
+      const uint64_t lo = __shfl_sync(0xffffffffu, acc[E - 1], 31);
+      if (hi > lo) warp_merge_lists<E>(acc, buf[q], lane);
+    }
+  }
+  uint64_t* red = sm.cand;  // [nw][L]
+#pragma unroll
+  for (int e = 0; e < E; ++e) red[warp * L + e * 32 + lane] = acc[e];
+  __syncthreads();
+  if (warp == 0) {
+    for (int w = 1; w < nw; ++w) {
+      uint64_t u[E];
+#pragma unroll
+      for (int e = 0; e < E; ++e) u[e] = red[w * L + e * 32 + lane];
+      warp_merge_lists<E>(acc, u, lane);
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) sm.best[e * 32 + lane] = acc[e];
+  }
+  __syncthreads();
+}
+
+// Writes the row's result from sm.best: V/I (first k; empty keys as
+// (-FLT_MAX, -1)) and/or its L keys.
+template <int L>
+__device__ __forceinline__ void write_row(const FinishArgs& fa, const FinishSmem& sm, int64_t b, int tid,
+                                          int nthreads) {
+  for (int i = tid; i < L; i += nthreads) {
+    const uint64_t key = sm.best[i];
+    if (fa.V != nullptr && i < fa.k) {
+      fa.V[b * fa.k + i] = key ? key_value(key) : -3.402823466e+38f;
+      fa.I[b * fa.k + i] = key ? key_index(key) : -1;
+    }
+    if (fa.keys_out != nullptr) fa.keys_out[b * L + i] = key;
+  }
+}
+
+// Stores sm.best (row b) into slot [slot][rank] of every rank's receive
+// buffer and sets the row's flag there to `tag` (warp p -> rank p).
+template <int L>
+__device__ __forceinline__ void publish_row(const ExchangeDev& ex, const FinishSmem& sm, int slot,
+                                            unsigned long long tag, int64_t b, int tid, int nthreads) {
+  const int warp = tid >> 5, lane = tid & 31, nw = nthreads >> 5;
+  for (int p = warp; p < ex.world; p += nw) {
+    const int64_t at = ((int64_t)slot * ex.world + ex.rank) * ex.max_rows + b;
+    uint64_t* dst = ex.peer_recv[p] + at * L;
+#pragma unroll
+    for (int e = 0; e < L / 32; ++e)
+      __stcg(reinterpret_cast<unsigned long long*>(dst + e * 32 + lane), (unsigned long long)sm.best[e * 32 + lane]);
+    __threadfence_system();
+    __syncwarp();
+    if (lane == 0) st_release_sys_u64(ex.peer_flag[p] + at, tag);
+  }
+}
+
+// Finishes rows row0, row0 + row_step, ... < fa.rows.  Every thread of the
+// CTA calls it.  With the exchange, all of this CTA's rows are published
+// before any wait, so CTAs that run at the same time on different GPUs never
+// wait on each other in a cycle.
+template <int L>
+__device__ void finish_rows(const FinishArgs& fa, FinishSmem& sm, int64_t row0, int64_t row_step, int tid,
+                            int nthreads) {
+  unsigned long long step = 0;
+  int slot = 0;
+  if (fa.use_ex) {
+    step = *reinterpret_cast<volatile unsigned long long*>(fa.ex.state);
+    slot = (int)(step & 1ull);
+  }
+  for (int64_t b = row0; b < fa.rows; b += row_step) {
+    select_row<L>(fa.lists, fa.nlists, fa.stride, b, fa.k, 0xffffffffu, sm, tid, nthreads);
+    if (fa.use_ex)
+      publish_row<L>(fa.ex, sm, slot, step + 1ull, b, tid, nthreads);
+    else
+      write_row<L>(fa, sm, b, tid, nthreads);
+    __syncthreads();
+  }
+  if (!fa.use_ex) return;
+  const ExchangeDev& ex = fa.ex;
+  const unsigned long long t0 = global_timer_ns();
+  for (int64_t b = row0; b < fa.rows; b += row_step) {
+    if (tid == 0) sm.valid = 0u;
+    __syncthreads();
+    if (tid < ex.world) {
+      const unsigned long long* f = ex.flag + ((int64_t)slot * ex.world + tid) * ex.max_rows + b;
+      bool ok = true;
+      while (ld_acquire_sys_u64(f) != step + 1ull) {
+        if (global_timer_ns() - t0 > ex.wait_ns) {
+          ok = false;
+          break;
+        }
+        __nanosleep(64);
+      }
+      if (ok)
+        atomicOr(&sm.valid, 1u << tid);
+      else
+        raise_device_error(kErrExchangeTimeout);
+    }
+    __syncthreads();
+    select_row<L>(ex.recv + (int64_t)slot * ex.world * ex.max_rows * L, ex.world, ex.max_rows, b, fa.k, sm.valid, sm,
+                  tid, nthreads);
+    write_row<L>(fa, sm, b, tid, nthreads);
+    __syncthreads();
+  }
+  // Every CTA of this step has passed its waits: the last one advances the step.
+  if (tid == 0) {
+    __threadfence();
+    const unsigned long long done = atomicAdd(ex.state + 1, 1ull);
+    if (done == (unsigned long long)gridDim.x - 1ull) {
+      ex.state[1] = 0ull;
+      __threadfence();
+      ex.state[0] = step + 1ull;
+    }
+  }
+}
+
+}  // namespace stk

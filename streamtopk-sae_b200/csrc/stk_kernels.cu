@@ -9,9 +9,13 @@
 //   simt_topk_kernel   the same contract with fp32 SIMT FMA: fp32 inputs and
 //                      shapes TMA cannot describe (d not a multiple of 8,
 //                      unaligned bases).
-//   merge_lists_kernel per-row top-k of several sorted key lists (CTA partials,
-//                      or the lists all-gathered from other GPUs).  Replaces
-//                      the reference's pass-2 merge (streamtopk_exact.cu:429-499).
+//   finish_kernel      per-row top-k of several sorted key lists (the units'
+//                      lists of a score kernel that did not finish its rows
+//                      itself, or lists all-gathered from other GPUs), with the
+//                      optional cross-GPU exchange (stk_finish.cuh).  The fused
+//                      kernel runs the same finish in its tail when all of its
+//                      units are resident at once.  Replaces the reference's
+//                      pass-2 merge (streamtopk_exact.cu:429-499).
 //
 // Work decomposition shared by the two score kernels: the batch is cut into
 // M tiles of 128 rows; F is cut into `segs` contiguous feature ranges whose
@@ -23,10 +27,12 @@
 #include "stk_kernels.cuh"
 
 namespace stk {
-
 __device__ unsigned int g_device_error = 0;
+}  // namespace stk
 
-__device__ __forceinline__ void raise_device_error(unsigned code) { atomicCAS(&g_device_error, 0u, code); }
+#include "stk_finish.cuh"
+
+namespace stk {
 
 __device__ __forceinline__ void unit_range(const UnitGrid& g, int u, int& m, int64_t& f_begin, int64_t& f_end) {
   const int seg = u / g.m_tiles;
@@ -529,6 +535,7 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
       if (cur.last_of_unit()) {
         acc.finish();
         store_partials<L>(top_s, p.partials + (int64_t)cur.u * kRows * L, q * 32, lane);
+        __threadfence();  // the lists are read by other CTAs in the finish step
       }
 #pragma unroll
       for (int c = 0; c < NT / 32; ++c) bcur[c] = bnext[c];
@@ -546,6 +553,26 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+  if (p.finish) {
+    // Finish step in this kernel: once every CTA's lists are stored (bounded
+    // grid barrier; the grid is one CTA per SM), CTA c finishes rows c,
+    // c + gridDim.x, ...  The pipeline's shared memory is free by now.
+    fence_proxy_async_smem();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      atomicAdd(p.tail_count, 1u);
+      const unsigned long long t0 = global_timer_ns();
+      while (ld_acquire_u32(p.tail_count) < gridDim.x) {
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+          raise_device_error(kErrFinishBarrier);
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    __syncthreads();
+    finish_rows<L>(p.fin, *reinterpret_cast<FinishSmem*>(smem), blockIdx.x, gridDim.x, threadIdx.x, blockDim.x);
   }
 }
 
@@ -647,314 +674,15 @@ __global__ void __launch_bounds__(kSimtThreads, 1) simt_topk_kernel(const T* __r
 }
 
 // ---------------------------------------------------------------------------
-// Merge kernel: one CTA (16 warps) per row.  List s of row b starts at
-// lists[(s * list_stride + b) * L]; each list holds L keys, descending.
-// Warp w folds lists w, w+16, ... (next list prefetched), then a 4-level tree
-// in shared memory folds the 16 warp results.  Launched with programmatic
+// Standalone finish kernel (stk_finish.cuh).  Launched with programmatic
 // dependent launch after the score kernel: griddepcontrol.wait blocks until
 // that grid has completed and its writes are visible (a no-op otherwise).
 // ---------------------------------------------------------------------------
-constexpr int kMergeWarps = 16;
-constexpr int kMergeBatch = 8;
-
-// Folds the nlists sorted lists of row b (list s at lists[(s*list_stride + b)*L])
-// into the best L keys, left in warp 0's acc.  Warp w folds lists w, w+16, ...;
-// kMergeBatch lists are loaded at once (one memory round trip per batch) and a
-// list whose best key does not beat the current L-th best is skipped; a 4-level
-// tree in shared memory folds the 16 warp results.  All threads must call it.
 template <int L>
-__device__ __forceinline__ void fold_row(const uint64_t* __restrict__ lists, int nlists, int64_t list_stride,
-                                         int64_t b, uint64_t (&acc)[L / 32], uint64_t (*red)[L], int warp,
-                                         int lane) {
-  constexpr int E = L / 32;
-#pragma unroll
-  for (int e = 0; e < E; ++e) acc[e] = kEmptyKey;
-  for (int s0 = warp; s0 < nlists; s0 += kMergeWarps * kMergeBatch) {
-    uint64_t buf[kMergeBatch][E];
-#pragma unroll
-    for (int q = 0; q < kMergeBatch; ++q) {
-      const int s = s0 + q * kMergeWarps;
-      const uint64_t* ps = lists + ((int64_t)s * list_stride + b) * L;
-#pragma unroll
-      for (int e = 0; e < E; ++e)
-        buf[q][e] = s < nlists ? (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(ps + e * 32 + lane))
-                               : kEmptyKey;
-    }
-#pragma unroll
-    for (int q = 0; q < kMergeBatch; ++q) {
-      const uint64_t best = __shfl_sync(0xffffffffu, buf[q][0], 0);
-      const uint64_t worst = __shfl_sync(0xffffffffu, acc[E - 1], 31);
-      if (best > worst) warp_merge_lists<E>(acc, buf[q], lane);
-    }
-  }
-#pragma unroll
-  for (int e = 0; e < E; ++e) red[warp][e * 32 + lane] = acc[e];
-  __syncthreads();
-#pragma unroll
-  for (int half = kMergeWarps / 2; half >= 1; half >>= 1) {
-    if (warp < half) {
-      uint64_t cur[E];
-#pragma unroll
-      for (int e = 0; e < E; ++e) cur[e] = red[warp + half][e * 32 + lane];
-      warp_merge_lists<E>(acc, cur, lane);
-#pragma unroll
-      for (int e = 0; e < E; ++e) red[warp][e * 32 + lane] = acc[e];
-    }
-    __syncthreads();
-  }
-}
-
-template <int L>
-__device__ __forceinline__ void write_row(const uint64_t (&acc)[L / 32], int64_t b, int k, float* __restrict__ V,
-                                          int32_t* __restrict__ I, uint64_t* __restrict__ keys_out, int lane) {
-#pragma unroll
-  for (int e = 0; e < L / 32; ++e) {
-    const int i = e * 32 + lane;
-    const uint64_t key = acc[e];
-    if (i < k) {
-      V[b * k + i] = key ? key_value(key) : -3.402823466e+38f;
-      I[b * k + i] = key ? key_index(key) : -1;
-    }
-    if (keys_out) keys_out[b * L + i] = key;
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Select merge of one row.  The lists of the score kernel's units are sparse
-// (every key passed the row's threshold floor, most lists hold a few keys), so
-// instead of folding all of them:
-//  1. tau = the k-th largest list head: the k largest heads are k distinct
-//     keys, so the row's k-th key is >= tau (tau = 1, every key, when fewer
-//     than k lists are non-empty);
-//  2. every key >= tau is gathered into shared memory (a list whose head is
-//     below tau is skipped; a list is read until its first 32-key chunk that
-//     is not all >= tau) -- ~1.3 k candidates per row on Gaussian data;
-//  3. each candidate's rank is the number of larger candidates (keys are
-//     distinct), which is also its position in the row's sorted result.
-// More than kSelectCap candidates or lists: the caller folds instead.
-// ---------------------------------------------------------------------------
-constexpr int kSelectCap = kMergeWarps * 32;
-
-template <int L>
-struct MergeSmem {
-  uint64_t red[kMergeWarps][L];  // fold_row (fallback)
-  uint64_t heads[kSelectCap];
-  uint64_t cand[kSelectCap];
-  uint64_t tau;
-  int cnt;
-};
-
-// Returns the number of candidates (in sm.cand, unsorted), or -1 when the row
-// must be folded instead.  All threads of the CTA must call it.
-template <int L>
-__device__ __forceinline__ int select_candidates(const uint64_t* __restrict__ lists, int nlists, int64_t list_stride,
-                                                 int64_t b, int k, MergeSmem<L>& sm, int tid, int warp, int lane) {
-  if (nlists > kSelectCap) return -1;
-  if (tid == 0) {
-    sm.tau = 1ull;
-    sm.cnt = 0;
-  }
-  if (tid < nlists)
-    sm.heads[tid] = (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(lists + ((int64_t)tid * list_stride + b) * L));
-  __syncthreads();
-  if (tid < nlists) {
-    const uint64_t h = sm.heads[tid];
-    if (h != 0ull) {
-      int r = 0;
-      for (int j = 0; j < nlists; ++j) r += sm.heads[j] > h ? 1 : 0;
-      if (r == k - 1) sm.tau = h;
-    }
-  }
-  __syncthreads();
-  const uint64_t tau = sm.tau;
-  for (int s0 = warp; s0 < nlists; s0 += kMergeWarps * kMergeBatch) {
-    uint64_t buf[kMergeBatch];
-#pragma unroll
-    for (int q = 0; q < kMergeBatch; ++q) {
-      const int s = s0 + q * kMergeWarps;
-      buf[q] = (s < nlists && sm.heads[s] >= tau)
-                   ? (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(
-                         lists + ((int64_t)s * list_stride + b) * L + lane))
-                   : 0ull;
-    }
-#pragma unroll
-    for (int q = 0; q < kMergeBatch; ++q) {
-      const int s = s0 + q * kMergeWarps;
-      if (s >= nlists || sm.heads[s] < tau) continue;  // warp-uniform
-      const uint64_t* ps = lists + ((int64_t)s * list_stride + b) * L;
-      uint64_t key = buf[q];
-      for (int e = 0;;) {
-        const bool take = key >= tau;
-        const unsigned m = __ballot_sync(0xffffffffu, take);
-        int base = 0;
-        if (lane == 0 && m != 0u) base = atomicAdd(&sm.cnt, __popc(m));
-        base = __shfl_sync(0xffffffffu, base, 0);
-        if (take) {
-          const int pos = base + __popc(m & ((1u << lane) - 1u));
-          if (pos < kSelectCap) sm.cand[pos] = key;
-        }
-        if (m != 0xffffffffu || ++e == L / 32) break;  // sorted: the next chunk holds smaller keys
-        key = (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(ps + e * 32 + lane));
-      }
-    }
-  }
-  __syncthreads();
-  const int C = sm.cnt;
-  return C > kSelectCap ? -1 : C;
-}
-
-// Position of `key` in the descending order of the C distinct candidates.
-__device__ __forceinline__ int candidate_rank(const uint64_t* cand, int C, uint64_t key) {
-  int r = 0;
-  for (int j = 0; j < C; ++j) r += cand[j] > key ? 1 : 0;
-  return r;
-}
-
-// ---------------------------------------------------------------------------
-// Merge kernel: one CTA (16 warps) per row.  Launched with programmatic
-// dependent launch after the score kernel: griddepcontrol.wait blocks until
-// that grid has completed and its writes are visible (a no-op otherwise).
-// Writes the row's top k (V, I) and, if keys_out, its best keys in slots
-// [0, L) (the top min(L, #candidates), then empty keys: at least the top k).
-// ---------------------------------------------------------------------------
-template <int L>
-__global__ void __launch_bounds__(kMergeWarps * 32) merge_lists_kernel(const uint64_t* __restrict__ lists, int nlists,
-                                                                        int64_t list_stride, int64_t rows, int k,
-                                                                        float* __restrict__ V, int32_t* __restrict__ I,
-                                                                        uint64_t* __restrict__ keys_out) {
-  __shared__ MergeSmem<L> sm;
+__global__ void __launch_bounds__(kFinishThreads) finish_kernel(const FinishArgs fa) {
+  __shared__ FinishSmem sm;
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int64_t b = blockIdx.x;
-  if (b >= rows) return;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int C = select_candidates<L>(lists, nlists, list_stride, b, k, sm, tid, warp, lane);
-  if (C < 0) {
-    uint64_t acc[L / 32];
-    fold_row<L>(lists, nlists, list_stride, b, acc, sm.red, warp, lane);
-    if (warp == 0) write_row<L>(acc, b, k, V, I, keys_out, lane);
-    return;
-  }
-  if (tid < C) {
-    const uint64_t key = sm.cand[tid];
-    const int r = candidate_rank(sm.cand, C, key);
-    if (r < k) {
-      V[b * k + r] = key_value(key);
-      I[b * k + r] = key_index(key);
-    }
-    if (keys_out && r < L) keys_out[b * L + r] = key;
-  } else {
-    if (tid < k) {
-      V[b * k + tid] = -3.402823466e+38f;
-      I[b * k + tid] = -1;
-    }
-    if (keys_out && tid < L) keys_out[b * L + tid] = 0ull;
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Publish kernel (F-sharded encode): folds this rank's CTA lists of row b like
-// the merge kernel; then warp p stores the row's best L keys into slot
-// [step & 1][rank] of rank p's receive buffer (a peer store over NVLink for
-// p != rank) and, after a system-scope fence, adds 1 to rank p's arrival
-// counter for this rank.
-// ---------------------------------------------------------------------------
-template <int L>
-__global__ void __launch_bounds__(kMergeWarps * 32) publish_kernel(const uint64_t* __restrict__ lists, int nlists,
-                                                                    int64_t list_stride, int64_t rows, int k,
-                                                                    const ExchangeDev ex) {
-  __shared__ MergeSmem<L> sm;
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  // The final merge (launched as this grid's programmatic dependent) may now
-  // be scheduled: it synchronises on the arrival counters, not on this grid.
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  const int64_t b = blockIdx.x;
-  if (b >= rows) return;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const unsigned long long step = *reinterpret_cast<volatile unsigned long long*>(ex.state);
-  const int slot = (int)(step & 1ull);
-  // The row's list into sm.red[0]: its top min(L, #candidates) keys, then empty
-  // keys (at least the top k, which is all the final merge needs).
-  const int tid = threadIdx.x;
-  const int C = select_candidates<L>(lists, nlists, list_stride, b, k, sm, tid, warp, lane);
-  if (C < 0) {
-    uint64_t acc[L / 32];
-    fold_row<L>(lists, nlists, list_stride, b, acc, sm.red, warp, lane);  // ends with red[0] = the row's list
-  } else {
-    if (tid < C) {
-      const uint64_t key = sm.cand[tid];
-      const int r = candidate_rank(sm.cand, C, key);
-      if (r < L) sm.red[0][r] = key;
-    } else if (tid < L) {
-      sm.red[0][tid] = 0ull;
-    }
-    __syncthreads();
-  }
-  uint64_t (&red)[kMergeWarps][L] = sm.red;
-  if (warp < ex.world) {
-    uint64_t* dst = ex.peer_recv[warp] + (((int64_t)slot * ex.world + ex.rank) * ex.max_rows + b) * L;
-#pragma unroll
-    for (int e = 0; e < L / 32; ++e)
-      __stcg(reinterpret_cast<unsigned long long*>(dst + e * 32 + lane), (unsigned long long)red[0][e * 32 + lane]);
-    __threadfence_system();
-    __syncwarp();
-    if (lane == 0) {
-      __threadfence_system();  // cumulative: the whole warp's stores precede the count
-      atomicAdd_system(ex.peer_arrive[warp] + slot * ex.world + ex.rank, 1ull);
-    }
-  }
-}
-
-__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// ---------------------------------------------------------------------------
-// Final merge of the exchange: one CTA per row waits (bounded) until every
-// rank's rows of this step have arrived, folds the world lists, writes V/I;
-// the last CTA clears the slot's counters and advances the step counter.
-// ---------------------------------------------------------------------------
-template <int L>
-__global__ void __launch_bounds__(kMergeWarps * 32) exchange_merge_kernel(const ExchangeDev ex, int64_t rows, int k,
-                                                                           float* __restrict__ V,
-                                                                           int32_t* __restrict__ I) {
-  __shared__ uint64_t red[kMergeWarps][L];
-  __shared__ int timed_out;
-  const int64_t b = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const unsigned long long step = *reinterpret_cast<volatile unsigned long long*>(ex.state);
-  const int slot = (int)(step & 1ull);
-  if (threadIdx.x == 0) {
-    timed_out = 0;
-    const unsigned long long t0 = global_timer_ns();
-    for (int p = 0; p < ex.world; ++p) {
-      while (ld_acquire_sys_u64(ex.arrive + slot * ex.world + p) < (unsigned long long)rows) {
-        if (global_timer_ns() - t0 > ex.wait_ns) {
-          timed_out = 1;
-          break;
-        }
-        __nanosleep(128);
-      }
-      if (timed_out) break;
-    }
-    if (timed_out) raise_device_error(kErrExchangeTimeout);
-  }
-  __syncthreads();
-  uint64_t acc[L / 32];
-  fold_row<L>(ex.recv + (int64_t)slot * ex.world * ex.max_rows * L, ex.world, ex.max_rows, b, acc, red, warp, lane);
-  if (warp == 0) write_row<L>(acc, b, k, V, I, nullptr, lane);
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned long long done = atomicAdd(ex.state + 1, 1ull);
-    if (done == (unsigned long long)gridDim.x - 1) {
-      // Every CTA of this step has passed its wait: reset for step + 2.
-      for (int p = 0; p < ex.world; ++p) ex.arrive[slot * ex.world + p] = 0ull;
-      ex.state[1] = 0ull;
-      __threadfence();
-      ex.state[0] = step + 1ull;
-    }
-  }
+  finish_rows<L>(fa, sm, blockIdx.x, gridDim.x, threadIdx.x, blockDim.x);
 }
 
 // ---------------------------------------------------------------------------
@@ -999,46 +727,11 @@ cudaError_t launch_simt(const void* X, const void* W, const SimtParams& p, int g
 }
 
 template <int L>
-cudaError_t launch_publish(const uint64_t* lists, int nlists, int64_t list_stride, int64_t rows, int k,
-                           const ExchangeDev& ex, cudaStream_t stream) {
-  if (rows <= 0) return cudaSuccess;
+cudaError_t launch_finish(const FinishArgs& fa, int grid, cudaStream_t stream) {
+  if (fa.rows <= 0 || grid <= 0) return cudaSuccess;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)rows);
-  cfg.blockDim = dim3(kMergeWarps * 32);
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, publish_kernel<L>, lists, nlists, list_stride, rows, k, ex);
-}
-
-template <int L>
-cudaError_t launch_exchange_merge(const ExchangeDev& ex, int64_t rows, int k, float* V, int32_t* I,
-                                  cudaStream_t stream) {
-  if (rows <= 0) return cudaSuccess;
-  // Programmatic dependent of the publish kernel: all publish CTAs are
-  // resident (or done) before any of these CTAs starts spinning.
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)rows);
-  cfg.blockDim = dim3(kMergeWarps * 32);
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, exchange_merge_kernel<L>, ex, rows, k, V, I);
-}
-
-template <int L>
-cudaError_t launch_merge(const uint64_t* lists, int nlists, int64_t list_stride, int64_t rows, int k, float* V,
-                         int32_t* I, uint64_t* keys_out, cudaStream_t stream) {
-  if (rows <= 0) return cudaSuccess;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)rows);
-  cfg.blockDim = dim3(kMergeWarps * 32);
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kFinishThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -1046,7 +739,7 @@ cudaError_t launch_merge(const uint64_t* lists, int nlists, int64_t list_stride,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, merge_lists_kernel<L>, lists, nlists, list_stride, rows, k, V, I, keys_out);
+  return cudaLaunchKernelEx(&cfg, finish_kernel<L>, fa);
 }
 
 #define STK_INST_FUSED(L, NT, S, A, SM)                                                                            \
@@ -1065,11 +758,7 @@ STK_FUSED_TF32_CONFIGS(STK_INST_FUSED_TF32)
   template cudaError_t launch_simt<__half, L>(const void*, const void*, const SimtParams&, int, cudaStream_t);  \
   template cudaError_t launch_simt<__nv_bfloat16, L>(const void*, const void*, const SimtParams&, int,          \
                                                      cudaStream_t);                                             \
-  template cudaError_t launch_merge<L>(const uint64_t*, int, int64_t, int64_t, int, float*, int32_t*, uint64_t*, \
-                                       cudaStream_t);                                                           \
-  template cudaError_t launch_publish<L>(const uint64_t*, int, int64_t, int64_t, int, const ExchangeDev&,       \
-                                         cudaStream_t);                                                         \
-  template cudaError_t launch_exchange_merge<L>(const ExchangeDev&, int64_t, int, float*, int32_t*, cudaStream_t);
+  template cudaError_t launch_finish<L>(const FinishArgs&, int, cudaStream_t);
 STK_INST_SIMT(32)
 STK_INST_SIMT(64)
 STK_INST_SIMT(128)

@@ -37,6 +37,43 @@ constexpr int kPilotGroup = 8;   // scores per histogrammed group maximum
 constexpr int kPilotBins = 1 << kPilotBits;
 constexpr unsigned long long kPilotWaitNs = 200000;  // give up (no floor) after 200 us
 
+// Direct GPU-to-GPU exchange of per-rank key lists (F-sharded encode, one
+// process per GPU on one node).  Each rank owns one exchange buffer:
+//   recv  [2][world][max_rows][L] keys   (slot = step & 1)
+//   flag  [2][world][max_rows] u64        (step + 1 once rank p's row arrived)
+//   state [2] u64: step counter, CTAs done with the current step
+// peer_recv / peer_flag[p] are rank p's recv / flag mapped into this process
+// (CUDA IPC); entry `rank` is the local buffer.
+constexpr int kMaxWorld = 8;
+struct ExchangeDev {
+  uint64_t* peer_recv[kMaxWorld];
+  unsigned long long* peer_flag[kMaxWorld];
+  uint64_t* recv;
+  unsigned long long* flag;
+  unsigned long long* state;
+  int rank, world;
+  int64_t max_rows;
+  unsigned long long wait_ns;
+};
+constexpr unsigned kErrExchangeTimeout = 3;
+constexpr unsigned kErrFinishBarrier = 4;  // the fused kernel's CTAs did not all reach the finish step in time
+
+// Finish step (stk_finish.cuh): per-row top-k over the units' sorted lists
+// (list s of row b at lists[(s * stride + b) * L]), results to V/I and/or
+// keys_out, optionally through the exchange.
+struct FinishArgs {
+  const uint64_t* lists;
+  int nlists;
+  int64_t stride;
+  int64_t rows;
+  int k;
+  float* V;            // (rows, k) or null
+  int32_t* I;          // (rows, k) or null
+  uint64_t* keys_out;  // (rows, L) or null: the row's top k, then further real keys descending, then empty keys
+  int use_ex;
+  ExchangeDev ex;
+};
+
 struct FusedParams {
   UnitGrid grid;
   const float* bias;
@@ -45,6 +82,9 @@ struct FusedParams {
   uint32_t* pilot_hist;    // [m_tiles][128][kPilotBins] counts, zeroed by the host; null = no pilot
   uint32_t* pilot_rowmax;  // [m_tiles][128] highest bin seen per row
   uint32_t* pilot_count;   // CTAs that finished their sample
+  uint32_t* tail_count;    // CTAs whose lists are stored (finish barrier); zeroed by the host
+  int finish;              // 1: the kernel finishes the rows itself (fin), after a grid barrier
+  FinishArgs fin;
   int64_t B, F;
   int k;
   int num_kb;          // ceil(d / 64)
@@ -134,36 +174,13 @@ cudaError_t launch_split_tf32(const float* X, float* Xh, float* Xl, int64_t n, c
 template <typename T, int L>
 cudaError_t launch_simt(const void* X, const void* W, const SimtParams& p, int grid, cudaStream_t stream);
 
+// Standalone finish (after a score kernel that does not finish its rows
+// itself, or over lists all-gathered from other GPUs): a programmatic
+// dependent launch of `grid` CTAs of kFinishThreads.
+constexpr int kFinishThreads = 256;
 template <int L>
-cudaError_t launch_merge(const uint64_t* lists, int nlists, int64_t list_stride, int64_t rows, int k, float* V,
-                         int32_t* I, uint64_t* keys_out, cudaStream_t stream);
+cudaError_t launch_finish(const FinishArgs& fa, int grid, cudaStream_t stream);
 
-// Direct GPU-to-GPU exchange of per-rank key lists (F-sharded encode, one
-// process per GPU on one node).  Each rank owns one exchange buffer:
-//   recv   [2][world][max_rows][L] keys   (slot = step & 1)
-//   arrive [2][world] u64 row counters     (rows received from each rank)
-//   state  [2] u64: step counter, CTAs done in the current final merge
-// peer_recv / peer_arrive[p] are rank p's recv / arrive mapped into this
-// process (CUDA IPC); entry `rank` is the local buffer.
-constexpr int kMaxWorld = 8;
-struct ExchangeDev {
-  uint64_t* peer_recv[kMaxWorld];
-  unsigned long long* peer_arrive[kMaxWorld];
-  uint64_t* recv;
-  unsigned long long* arrive;
-  unsigned long long* state;
-  int rank, world;
-  int64_t max_rows;
-  unsigned long long wait_ns;
-};
-constexpr unsigned kErrExchangeTimeout = 3;
-
-template <int L>
-cudaError_t launch_publish(const uint64_t* lists, int nlists, int64_t list_stride, int64_t rows, int k,
-                           const ExchangeDev& ex, cudaStream_t stream);
-template <int L>
-cudaError_t launch_exchange_merge(const ExchangeDev& ex, int64_t rows, int k, float* V, int32_t* I,
-                                  cudaStream_t stream);
 
 // Per-tile candidates of the approximate path: partials[(tile * m_tiles + m) *
 // 128 + r][0..L) -> cand_vals / cand_idxs [(row) * tiles + tile][0..c),

@@ -11,12 +11,19 @@ Each rank holds the contiguous feature range [f0, f1) of W_enc / b_enc
      group (NCCL over NVLink on B200; gloo works for host-side tests).
   3. ``stk_merge_keys`` on every rank: top-k of world * L keys per row.
 
-With ``transport="p2p"`` steps 2-3 run as two library kernels instead
-(``PeerExchange``, C ABI stk_exchange_*): a publish kernel merges the local
-lists and stores each row's keys straight into every rank's receive buffer
-(CUDA IPC mappings, peer stores over NVLink) and bumps that rank's arrival
-counter; the final merge waits (bounded) for all ranks' rows and merges.  No
-NCCL call and no host involvement per step.
+With ``transport="p2p"`` steps 2-3 run inside the library instead
+(``PeerExchange``, C ABI stk_exchange_*): the score kernel finishes its rows
+in its own tail and stores each row's best keys straight into every rank's
+receive buffer (CUDA IPC mappings, peer stores over NVLink) with a per-row flag
+set to the step number, then waits (bounded) for all ranks' rows and merges
+them -- one kernel launch per step, no NCCL call and no host involvement.
+
+Device-side errors: a wait for another rank's rows that runs out (default
+10 s) sets device error 3 and that step's rows are finished over the ranks
+whose rows had arrived.  The kernels cannot raise; ``check_device_errors()``
+(at a synchronisation point the caller already has) reads the error word and
+raises.  Steps are tagged with their absolute number, so rows that arrive late
+are never taken for a later step's rows.
 
 Keys order by (score desc, feature index asc), so the result is identical to
 the single-GPU encode for any world size.  The reference has no multi-GPU
@@ -151,6 +158,13 @@ class PeerExchange:
                                                  ws.data_ptr(), nbytes, stream))
         return V, I
 
+    def check_device_errors(self):
+        """Synchronise this rank's stream and raise RuntimeError if a library
+        kernel reported a device-side error since the last check (code 3: a wait
+        for another rank's rows ran out)."""
+        with torch.cuda.device(self.device):
+            _capi.device_error(torch.cuda.current_stream(self.device).cuda_stream)
+
     def close(self):
         if self.handle is None:
             return
@@ -170,6 +184,14 @@ class ShardedEncoder:
     W_enc / b_enc; F_total: the full F; k: top-k.  ``encode(X)`` takes the
     replicated (B, d) batch and returns (values fp32 (B, k), indices int32
     (B, k)), identical on every rank.
+
+    ``encode`` is asynchronous and does not read the device error word (that
+    would synchronise every step).  With the p2p transport a rank that stalls
+    for longer than the exchange's wait limit makes the other ranks finish that
+    step without its rows and set device error 3; call ``check_device_errors()``
+    at a synchronisation point to turn that into an exception.  After a rank has
+    skipped a step entirely the ranks stay a step apart: ``close()`` on every
+    rank and encode again (a fresh exchange is set up collectively).
     """
 
     def __init__(self, W_shard, b_shard, F_total, f_offset, k, group=None, mode="exact", c=None,
@@ -215,6 +237,13 @@ class ShardedEncoder:
                 self.fallback_reason = str(e)
                 return None
         return self.exchange
+
+    def check_device_errors(self):
+        """Synchronise the current stream of this rank's device and raise
+        RuntimeError if a library kernel reported a device-side error."""
+        dev = self.W.device
+        with torch.cuda.device(dev):
+            _capi.device_error(torch.cuda.current_stream(dev).cuda_stream)
 
     def close(self):
         """Release the p2p exchange (collective); a no-op for the NCCL transport."""

@@ -218,6 +218,26 @@ def test_sampled_floor_changes_nothing(B, d, F, k):
         check(V1, I1, Xr, Wr, br, k, RTOL["bf16"])
 
 
+@pytest.mark.parametrize("B,d,F,k", [(128, 512, 60000, 64), (256, 256, 40000, 32), (200, 128, 30000, 128),
+                                     (7, 64, 300, 16), (128, 64, 6000, 128), (1, 64, 100000, 1)])
+def test_fused_finish_equals_separate_finish(B, d, F, k):
+    """The finish step in the fused kernel's tail (grid barrier, per-row select in
+    the same launch) and the standalone finish kernel give bit-identical rows."""
+    from streamtopk_sae import _capi, native
+    X, W, b = oracle.gaussian_inputs(B, d, F, seed=B + F)
+    if F == 6000:   # scores rise with the index: every list is full, the fold path runs
+        X[:] = 1.0
+        W[:] = 0.0
+        b = np.arange(F, dtype=np.float32) * 1e-3
+    Xt, Wt, bt, Xr, Wr, br = device_inputs(X, W, b, "bf16")
+    V1, I1 = native.streamtopk_cuda_exact_forward(Xt, Wt, bt, k)
+    V2, I2 = native.streamtopk_cuda_exact_forward(Xt, Wt, bt, k, flags=_capi.STK_FLAG_SEPARATE_FINISH)
+    torch.cuda.synchronize()
+    no_device_error()
+    assert torch.equal(V1, V2) and torch.equal(I1, I2)
+    check(V1, I1, Xr, Wr, br, k, RTOL["bf16"])
+
+
 @pytest.mark.parametrize("k", [16, 64, 128])
 def test_exchange_single_rank_equals_exact(k):
     """A one-rank peer exchange (publish kernel into its own receive buffer, arrival
@@ -239,11 +259,14 @@ def test_exchange_single_rank_equals_exact(k):
         ws = torch.empty(max(wsb, 8), dtype=torch.uint8, device="cuda")
         stream = torch.cuda.current_stream().cuda_stream
         Ve, Ie = stk.topk_sae_cuda_exact(X, W, b, k)
-        for _ in range(3):   # both receive slots and the step counter
+        # both receive slots and the step counter; the finish in the score
+        # kernel's tail and in the standalone finish kernel, alternately
+        for step in range(4):
             V = torch.empty((B, k), dtype=torch.float32, device="cuda")
             I = torch.empty((B, k), dtype=torch.int32, device="cuda")
+            flags = _capi.STK_FLAG_SEPARATE_FINISH if step % 2 else 0
             _capi.check(lib.stk_exchange_forward(h, X.data_ptr(), W.data_ptr(), b.data_ptr(), V.data_ptr(),
-                                                 I.data_ptr(), B, d, F, k, 0, _capi.STK_BF16, 0, ws.data_ptr(),
+                                                 I.data_ptr(), B, d, F, k, 0, _capi.STK_BF16, flags, ws.data_ptr(),
                                                  wsb, stream))
             torch.cuda.synchronize()
             assert torch.equal(V, Ve) and torch.equal(I, Ie)
