@@ -212,7 +212,7 @@ struct Plan {
   size_t ws_partials;
   size_t ws_app;
   size_t ws_sync;   // zeroed per call: barrier counters, then the pilot histogram and row maxima
-  size_t ws_split;  // TF32: round_tf32(X) and its residual, each 256-byte aligned
+  size_t ws_split;  // TF32: X's residual X - trunc13(X), 256-byte aligned
   size_t ws;
 };
 
@@ -246,22 +246,23 @@ int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t 
   pl->fin_fused = pl->tc && pl->grid.units <= pl->ctas && !(flags & STK_FLAG_SEPARATE_FINISH);
   const size_t pilot_bytes = pl->pilot ? (size_t)pl->grid.m_tiles * stk::kRows * (stk::kPilotBins + 1) * 4 : 0;
   pl->ws_sync = (pl->pilot || pl->fin_fused) ? ((kSyncBytes + pilot_bytes + 255) & ~size_t(255)) : 0;
-  pl->ws_split = pl->tf32 ? 2 * (((size_t)B * d * 4 + 255) & ~size_t(255)) : 0;
+  pl->ws_split = pl->tf32 ? (((size_t)B * d * 4 + 255) & ~size_t(255)) : 0;
   pl->ws = pl->ws_partials + pl->ws_app + pl->ws_sync + pl->ws_split;
   return STK_OK;
 }
 
-// Optional override of the fused tile configuration, "L,NT,STAGES,A,APP_SMEM",
-// for tuning.
-bool fused_override(int L, int* nt, int* stages, int* app, int* app_smem) {
+// Optional override of the fused tile configuration,
+// "L,NT,STAGES,A,APP_SMEM,TOPG", for tuning.
+bool fused_override(int L, int* nt, int* stages, int* app, int* app_smem, int* topg) {
   const char* s = std::getenv("STK_FUSED_CFG");
   if (!s) return false;
-  int l = 0, n = 0, st = 0, a = 0, sm = 0;
-  if (std::sscanf(s, "%d,%d,%d,%d,%d", &l, &n, &st, &a, &sm) != 5 || l != L) return false;
+  int l = 0, n = 0, st = 0, a = 0, sm = 0, tg = 0;
+  if (std::sscanf(s, "%d,%d,%d,%d,%d,%d", &l, &n, &st, &a, &sm, &tg) != 6 || l != L) return false;
   *nt = n;
   *stages = st;
   *app = a;
   *app_smem = sm;
+  *topg = tg;
   return true;
 }
 
@@ -277,23 +278,25 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
       32 * (pl.grid.fixed_chunks > 0 ? (int64_t)pl.grid.fixed_chunks
                                      : (pl.grid.nchunks + pl.grid.segs - 1) / pl.grid.segs);
   const bool narrow = unit_feats <= 256;
-  int nt = narrow ? 128 : 256;
-  int stages = narrow ? (pl.L == 128 ? 3 : pl.L == 64 ? 4 : 5) : (pl.L == 128 ? 2 : 3);
+  // TF32 (two accumulators per buffer): always 128-feature tiles.
+  const bool nt128 = narrow || pl.tf32;
+  int nt = nt128 ? 128 : 256;
+  int stages = nt128 ? (pl.L == 128 ? 3 : pl.L == 64 ? 4 : 5) : (pl.L == 128 ? 2 : 3);
   int nslots = pl.L == 64 ? 16 : 32;
   int app_smem = pl.L == 128 ? 0 : 1;
-  fused_override(pl.L, &nt, &stages, &nslots, &app_smem);
+  int topg = 0;
+  fused_override(pl.L, &nt, &stages, &nslots, &app_smem, &topg);
   CUtensorMap tx, txl, tw, tw32;
   const bool bf16 = dtype == STK_BF16;
   int rc = STK_OK;
   if (pl.tf32) {
-    // X is split once per call into round_tf32(X) and its residual (L2-resident,
-    // re-read by every tile); W is split tile by tile inside the kernel.
-    uint8_t* split = reinterpret_cast<uint8_t*>(partials) + pl.ws_partials + pl.ws_app + pl.ws_sync;
-    float* xh = reinterpret_cast<float*>(split);
-    float* xl = reinterpret_cast<float*>(split + pl.ws_split / 2);
-    cudaError_t se = stk::launch_split_tf32(static_cast<const float*>(X), xh, xl, B * d, stream);
-    if (se != cudaSuccess) return cuda_fail(se, "split_tf32_kernel launch");
-    rc = make_map_f32(&tx, xh, B, d, stk::kRows);
+    // X's residual X - trunc13(X) is computed once per call (L2-resident,
+    // re-read by every tile); W's residual tile by tile inside the kernel.  The
+    // raw X and W are the hi operands (the tensor core reads them as TF32).
+    float* xl = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(partials) + pl.ws_partials + pl.ws_app + pl.ws_sync);
+    cudaError_t se = stk::launch_residual_tf32(static_cast<const float*>(X), xl, B * d, stream);
+    if (se != cudaSuccess) return cuda_fail(se, "residual_tf32_kernel launch");
+    rc = make_map_f32(&tx, X, B, d, stk::kRows);
     if (!rc) rc = make_map_f32(&txl, xl, B, d, stk::kRows);
     if (!rc) rc = make_map_f32(&tw, W, F, d, nt);
     if (!rc) rc = make_map_f32(&tw32, W, F, d, 32);
@@ -344,14 +347,16 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   }
   cudaError_t e = cudaErrorInvalidValue;
   ProfScope prof(kProfFused, stream);
-#define STK_TRY_FUSED(Lc, NTc, Sc, Ac, SMc)                                                           \
-  if (!pl.tf32 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc)    \
-    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, false>(tx, txl, tw, tw32, p, pl.ctas, stream);
+#define STK_TRY_FUSED(Lc, NTc, Sc, Ac, SMc, TGc)                                                      \
+  if (!pl.tf32 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc &&  \
+      (topg != 0) == TGc)                                                                               \
+    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, TGc, false>(tx, txl, tw, tw32, p, pl.ctas, stream);
   STK_FUSED_CONFIGS(STK_TRY_FUSED)
 #undef STK_TRY_FUSED
-#define STK_TRY_FUSED_TF32(Lc, NTc, Sc, Ac, SMc)                                                      \
-  if (pl.tf32 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc)     \
-    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, true>(tx, txl, tw, tw32, p, pl.ctas, stream);
+#define STK_TRY_FUSED_TF32(Lc, NTc, Sc, Ac, SMc, TGc)                                                 \
+  if (pl.tf32 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc &&   \
+      (topg != 0) == TGc)                                                                               \
+    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, TGc, true>(tx, txl, tw, tw32, p, pl.ctas, stream);
   STK_FUSED_TF32_CONFIGS(STK_TRY_FUSED_TF32)
 #undef STK_TRY_FUSED_TF32
   if (e != cudaSuccess) return cuda_fail(e, "fused_topk_kernel launch");

@@ -171,6 +171,24 @@ __device__ __forceinline__ bool pilot_bound(const uint32_t* __restrict__ hist, u
   return false;
 }
 
+// One 32-column chunk of scores of an accumulator buffer (this warp's 32
+// lanes): the accumulator itself, or for TF32 the sum of the Xh*Wh accumulator
+// and the cross-term accumulator NT columns after it.
+template <bool TF32, int NT>
+__device__ __forceinline__ void load_chunk(uint32_t tcol, int c, uint32_t (&v)[32]) {
+  tmem_ld32(tcol + (uint32_t)(c * 32), v);
+  if constexpr (TF32) {
+    uint32_t u[32];
+    tmem_ld32(tcol + (uint32_t)(NT + c * 32), u);
+    tmem_wait_ld(v);
+    tmem_wait_ld(u);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(u[j]));
+  } else {
+    tmem_wait_ld(v);
+  }
+}
+
 // b[i] for a runtime i < N without dynamic register indexing.
 template <int N>
 __device__ __forceinline__ float pick(const float (&b)[N], int i) {
@@ -197,21 +215,31 @@ __device__ __forceinline__ void load_bias_tile(const float* __restrict__ bias, i
 //   warps 2..5: epilogue, warp w reads TMEM lanes 32*(w%4)..+31 (= batch rows)
 // ---------------------------------------------------------------------------
 // TF32 = false: 16-bit X / W, K = 64 per stage, 128-byte swizzle, warps 0 TMA,
-// 1 MMA, 2-5 epilogue.  TF32 = true (fp32 inputs): K = 16 per stage, 64-byte
-// swizzle; a stage holds round_tf32(X) and its residual (both precomputed,
-// two maps) and a W tile that warps 2-3 split in place into round_tf32(W) and
-// its residual; the MMA issuer accumulates Xh*Wh + Xh*Wl + Xl*Wh (the dropped
-// Xl*Wl term is ~2^-22 of |x||w|); warps 4-7 are the epilogue.
-template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TF32>
+// 1 MMA, 2-5 epilogue.  TF32 = true (fp32 inputs, 3-pass TF32): K = 16 per
+// stage, 64-byte swizzle.  The tensor core reads an fp32 operand as TF32 by
+// ignoring its low 13 mantissa bits, so the raw X and W tiles serve as the
+// "hi" parts h = trunc13(v) as they are; a stage also holds X's residual
+// X - trunc13(X) (precomputed once per call, second map) and W's residual,
+// written next to the W tile by warps 2-3.  The MMA issuer accumulates Xh*Wh
+// into one TMEM accumulator and Xh*Wl + Xl*Wh into a second one (kept apart so
+// that the small terms do not add to the rounding of the large accumulator);
+// the epilogue (warps 4-7) adds the two.  The dropped Xl*Wl term is below
+// 2^-20 of |x||w|.
+template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPG, bool TF32>
 __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
     fused_topk_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_xl,
                       const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_w32,
                       const FusedParams p) {
-  using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM>;
+  using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM, TOPG>;
   constexpr int kSplitThreads = 64;                 // warps 2-3 (TF32)
   constexpr int kFirstEpiWarp = TF32 ? 4 : 2;
   constexpr uint32_t kWRowBytes = TF32 ? 64u : 128u;  // bytes of one W row in a stage
   constexpr int kKPerStage = TF32 ? 16 : 64;        // elements of K per stage
+  // TMEM: two accumulator buffers (tile parity), each NT columns, or for TF32
+  // each 2 x NT (Xh*Wh, then the cross terms).
+  constexpr uint32_t kAccCols = TF32 ? 2 * NT : NT;
+  constexpr uint32_t kTmemCols = TF32 ? 512u : (uint32_t)Cfg::kTmemCols;
+  static_assert(!TF32 || NT <= 128, "TF32 needs 4 x NT TMEM columns");
   uint8_t* smem = stk_smem + ((1024u - (smem_u32(stk_smem) & 1023u)) & 1023u);
   uint64_t* top = reinterpret_cast<uint64_t*>(smem + Cfg::kTopOff);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOff);
@@ -251,7 +279,7 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
     tma_prefetch_desc(&tmap_w32);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -324,7 +352,7 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t d_tmem = tmem_base + (uint32_t)(a * NT);
+          const uint32_t d_tmem = tmem_base + (uint32_t)a * kAccCols;
           const uint32_t idesc = TF32 ? make_idesc_tf32(128u, (uint32_t)w)
                                       : make_idesc_f16((uint32_t)p.ab_format, 128u, (uint32_t)w);
           for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
@@ -343,9 +371,10 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
               const uint64_t dwl = smem_desc_sw64(sx + Cfg::kXBytes + NT * kWRowBytes);
 #pragma unroll
               for (int kk = 0; kk < 2; ++kk) {
-                umma_tf32(d_tmem, dxh + 2 * kk, dwh + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
-                umma_tf32(d_tmem, dxh + 2 * kk, dwl + 2 * kk, idesc, 1u);
-                umma_tf32(d_tmem, dxl + 2 * kk, dwh + 2 * kk, idesc, 1u);
+                const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
+                umma_tf32(d_tmem, dxh + 2 * kk, dwh + 2 * kk, idesc, acc);
+                umma_tf32(d_tmem + NT, dxh + 2 * kk, dwl + 2 * kk, idesc, acc);
+                umma_tf32(d_tmem + NT, dxl + 2 * kk, dwh + 2 * kk, idesc, 1u);
               }
             } else {
               const uint64_t dx = smem_desc_sw128(sx);
@@ -372,9 +401,9 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
     // ------------------------------------------------------------ W splitter (TF32)
     // Walks the producer's stage sequence; every thread waits for the stage's
     // TMA itself (so that the loaded bytes are visible to its own reads),
-    // rewrites its share of the W tile as round_tf32(W) and writes the
-    // residual round_tf32(W - that) to the tile's second half, then makes the
-    // writes visible to the tensor core and arrives on split_done.
+    // writes the residual W - trunc13(W) of its share of the W tile to the
+    // tile's second half (the raw tile is the hi operand as it is), then makes
+    // the writes visible to the tensor core and arrives on split_done.
     const int st = (warp - 2) * 32 + lane;
     uint32_t it = 0;
     bool ok = true;
@@ -390,21 +419,16 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
             ok = false;
             break;
           }
-          float4* wh = reinterpret_cast<float4*>(smem + s * Cfg::kStageBytes + Cfg::kXBytes);
-          float4* wl = wh + NT * (kWRowBytes / 16);
+          const float4* wh = reinterpret_cast<const float4*>(smem + s * Cfg::kStageBytes + Cfg::kXBytes);
+          float4* wl = reinterpret_cast<float4*>(smem + s * Cfg::kStageBytes + Cfg::kXBytes) + NT * (kWRowBytes / 16);
 #pragma unroll 4
           for (int i = st; i < NT * (int)(kWRowBytes / 16); i += kSplitThreads) {
             const float4 v = wh[i];
-            float4 h, l;
-            h.x = round_tf32(v.x);
-            h.y = round_tf32(v.y);
-            h.z = round_tf32(v.z);
-            h.w = round_tf32(v.w);
-            l.x = round_tf32(v.x - h.x);
-            l.y = round_tf32(v.y - h.y);
-            l.z = round_tf32(v.z - h.z);
-            l.w = round_tf32(v.w - h.w);
-            wh[i] = h;
+            float4 l;
+            l.x = v.x - trunc_tf32(v.x);
+            l.y = v.y - trunc_tf32(v.y);
+            l.z = v.z - trunc_tf32(v.z);
+            l.w = v.w - trunc_tf32(v.w);
             wl[i] = l;
           }
           fence_proxy_async_smem();
@@ -424,7 +448,7 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
     const uint32_t top_s = (uint32_t)(reinterpret_cast<uint8_t*>(top) - stk_smem);
     const uint32_t app_s = (uint32_t)(reinterpret_cast<uint8_t*>(smem + Cfg::kAppOff) - stk_smem);
     uint64_t* app_cta = p.app + (size_t)blockIdx.x * (kAppendMax * kRows);
-    RowTopK<L, A, APP_SMEM> acc;
+    RowTopK<L, A, APP_SMEM, TOPG> acc;
     uint32_t tile = 0;
     bool ok = true;
     TileWalk<NT> cur;
@@ -435,7 +459,8 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
       TileWalk<NT> nxt = cur;
       nxt.next(g);
       if (nxt.valid(g)) load_bias_tile<NT>(p.bias, nxt.ft, nxt.width(), p.F, lane, bnext);
-      if (cur.first_of_unit()) acc.init(top_s, app_s, app_cta, r, p.k);
+      if (cur.first_of_unit())
+        acc.init(top_s, p.partials + ((int64_t)cur.u * kRows + r) * L, app_s, app_cta, r, p.k);
       const bool row_ok = (int64_t)cur.m * kRows + r < p.B;
       const int w = cur.width();
       const int a = tile & 1;
@@ -456,7 +481,7 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
       }
       tc_fence_after();
       const int nchunk = w / 32;
-      const uint32_t tcol = t_lane + (uint32_t)(a * NT);
+      const uint32_t tcol = t_lane + (uint32_t)a * kAccCols;
       if (p.pilot_hist != nullptr && cur.first_of_unit()) {
         // Sample: histogram the first chunks of this tile (they stay in TMEM
         // and are offered below), meet the other CTAs, read back a floor.
@@ -466,8 +491,7 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
 #pragma unroll 1
         for (int c = 0; c < p.pilot_chunks && c < nchunk; ++c) {
           uint32_t v[32];
-          tmem_ld32(tcol + (uint32_t)(c * 32), v);
-          tmem_wait_ld(v);
+          load_chunk<TF32, NT>(tcol, c, v);
           const int64_t f = cur.ft + 32 * c;
           const float bl = pick<NT / 32>(bcur, c);
           const uint32_t valid = row_ok ? feature_mask(f, p.F) : 0u;
@@ -517,8 +541,7 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
 #pragma unroll 1
       for (int c = 0; c < nchunk; ++c) {
         uint32_t v[32];
-        tmem_ld32(tcol + (uint32_t)(c * 32), v);
-        tmem_wait_ld(v);
+        load_chunk<TF32, NT>(tcol, c, v);
         if (c == nchunk - 1) {
           tc_fence_before();
           __syncwarp();
@@ -534,7 +557,7 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
       }
       if (cur.last_of_unit()) {
         acc.finish();
-        store_partials<L>(top_s, p.partials + (int64_t)cur.u * kRows * L, q * 32, lane);
+        if constexpr (!TOPG) store_partials<L>(top_s, p.partials + (int64_t)cur.u * kRows * L, q * 32, lane);
         __threadfence();  // the lists are read by other CTAs in the finish step
       }
 #pragma unroll
@@ -552,7 +575,7 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    tmem_dealloc(tmem_base, kTmemCols);
   }
   if (p.finish) {
     // Finish step in this kernel: once every CTA's lists are stored (bounded
@@ -613,7 +636,7 @@ __global__ void __launch_bounds__(kSimtThreads, 1) simt_topk_kernel(const T* __r
     int64_t fb, fe;
     unit_range(g, u, m, fb, fe);
     const int64_t row0 = (int64_t)m * kRows;
-    if (tid < kRows) acc.init(top_s, 0u, app_cta, tid, p.k);
+    if (tid < kRows) acc.init(top_s, nullptr, 0u, app_cta, tid, p.k);
     for (int64_t ft = fb; ft < fe; ft += Cfg::kNT) {
       const int w = (int)min((int64_t)Cfg::kNT, fe - ft);
       float c[8][8];
@@ -688,31 +711,28 @@ __global__ void __launch_bounds__(kFinishThreads) finish_kernel(const FinishArgs
 // ---------------------------------------------------------------------------
 // Explicit instantiations and launch helpers (host side of this TU).
 // ---------------------------------------------------------------------------
-template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TF32>
+template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPG, bool TF32>
 cudaError_t launch_fused(const CUtensorMap& tx, const CUtensorMap& txl, const CUtensorMap& tw, const CUtensorMap& tw32,
                          const FusedParams& p, int grid, cudaStream_t stream) {
-  using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM>;
-  auto kern = fused_topk_kernel<L, NT, STAGES, A, APP_SMEM, TF32>;
+  using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM, TOPG>;
+  auto kern = fused_topk_kernel<L, NT, STAGES, A, APP_SMEM, TOPG, TF32>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   if (e != cudaSuccess) return e;
   kern<<<grid, TF32 ? kFusedThreads + 64 : kFusedThreads, Cfg::kSmemBytes, stream>>>(tx, txl, tw, tw32, p);
   return cudaGetLastError();
 }
 
-__global__ void split_tf32_kernel(const float* __restrict__ X, float* __restrict__ Xh, float* __restrict__ Xl,
-                                  int64_t n) {
+__global__ void residual_tf32_kernel(const float* __restrict__ X, float* __restrict__ Xl, int64_t n) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const float x = X[i];
-    const float h = round_tf32(x);
-    Xh[i] = h;
-    Xl[i] = round_tf32(x - h);
+    Xl[i] = x - trunc_tf32(x);
   }
 }
 
-cudaError_t launch_split_tf32(const float* X, float* Xh, float* Xl, int64_t n, cudaStream_t stream) {
+cudaError_t launch_residual_tf32(const float* X, float* Xl, int64_t n, cudaStream_t stream) {
   if (n <= 0) return cudaSuccess;
   const int64_t blocks = (n + 255) / 256;
-  split_tf32_kernel<<<(unsigned)(blocks < 1184 ? blocks : 1184), 256, 0, stream>>>(X, Xh, Xl, n);
+  residual_tf32_kernel<<<(unsigned)(blocks < 1184 ? blocks : 1184), 256, 0, stream>>>(X, Xl, n);
   return cudaGetLastError();
 }
 
@@ -742,15 +762,15 @@ cudaError_t launch_finish(const FinishArgs& fa, int grid, cudaStream_t stream) {
   return cudaLaunchKernelEx(&cfg, finish_kernel<L>, fa);
 }
 
-#define STK_INST_FUSED(L, NT, S, A, SM)                                                                            \
-  template cudaError_t launch_fused<L, NT, S, A, SM, false>(const CUtensorMap&, const CUtensorMap&,              \
-                                                            const CUtensorMap&, const CUtensorMap&,              \
-                                                            const FusedParams&, int, cudaStream_t);
+#define STK_INST_FUSED(L, NT, S, A, SM, TG)                                                                    \
+  template cudaError_t launch_fused<L, NT, S, A, SM, TG, false>(const CUtensorMap&, const CUtensorMap&,        \
+                                                                const CUtensorMap&, const CUtensorMap&,        \
+                                                                const FusedParams&, int, cudaStream_t);
 STK_FUSED_CONFIGS(STK_INST_FUSED)
-#define STK_INST_FUSED_TF32(L, NT, S, A, SM)                                                                       \
-  template cudaError_t launch_fused<L, NT, S, A, SM, true>(const CUtensorMap&, const CUtensorMap&,               \
-                                                           const CUtensorMap&, const CUtensorMap&,               \
-                                                           const FusedParams&, int, cudaStream_t);
+#define STK_INST_FUSED_TF32(L, NT, S, A, SM, TG)                                                               \
+  template cudaError_t launch_fused<L, NT, S, A, SM, TG, true>(const CUtensorMap&, const CUtensorMap&,         \
+                                                               const CUtensorMap&, const CUtensorMap&,         \
+                                                               const FusedParams&, int, cudaStream_t);
 STK_FUSED_TF32_CONFIGS(STK_INST_FUSED_TF32)
 
 #define STK_INST_SIMT(L)                                                                                         \

@@ -318,3 +318,23 @@ def test_working_memory_is_the_workspace(B, d, F, k):
     ws = _capi.workspace_bytes(B, d, F, k, _capi.STK_BF16)
     assert ws - 4096 <= working <= ws + 4096, (working, ws)
     assert ws < 64 << 20 or B > 256
+
+
+@pytest.mark.parametrize("cfg", ["32,256,4,32,1,1", "32,128,6,32,1,1", "64,256,4,16,1,1", "64,128,6,16,1,1",
+                                 "128,256,4,32,1,1", "128,128,6,32,1,1", "64,128,4,16,1,0", "128,128,3,32,0,0"])
+def test_tile_configurations_agree(cfg, monkeypatch):
+    """Every instantiated tile configuration (top lists in shared or in global
+    memory, 128- or 256-feature tiles, pipeline depth) gives the default's rows
+    bit for bit."""
+    from streamtopk_sae import native
+    L = int(cfg.split(",")[0])
+    k = {32: 32, 64: 64, 128: 128}[L]
+    X, W, b = oracle.gaussian_inputs(200, 320, 50000, seed=L)
+    Xt, Wt, bt, Xr, Wr, br = device_inputs(X, W, b, "bf16")
+    V0, I0 = native.streamtopk_cuda_exact_forward(Xt, Wt, bt, k)
+    monkeypatch.setenv("STK_FUSED_CFG", cfg)
+    V1, I1 = native.streamtopk_cuda_exact_forward(Xt, Wt, bt, k)
+    torch.cuda.synchronize()
+    no_device_error()
+    assert torch.equal(V0, V1) and torch.equal(I0, I1)
+    check(V1, I1, Xr, Wr, br, k, RTOL["bf16"])
