@@ -46,7 +46,8 @@ enum stk_dtype { STK_F32 = 0, STK_F16 = 1, STK_BF16 = 2 };
 
 /* Flags for the *_forward calls. */
 enum stk_flags {
-  STK_FLAG_ANY_K = 1, /* accept any 1 <= k <= 128, not only {1,2,4,8,16,32,64,128} */
+  STK_FLAG_ANY_K = 1, /* accept any 1 <= k <= 128, not only {1,2,4,8,16,32,64,128}; and any
+                         k <= F when F <= 4096 (whole-row sort, no workspace) */
   STK_FLAG_ANY_D = 2, /* lift the reference's d <= 4096 limit */
   STK_FLAG_SIMT = 4,    /* force the fp32 SIMT kernel (testing / comparison) */
   STK_FLAG_NO_PILOT = 8, /* skip the sampled threshold floor (testing / comparison) */

@@ -479,7 +479,11 @@ int stk_workspace_bytes(int64_t B, int64_t d, int64_t F, int64_t k, int dtype, s
   if (!bytes) return fail(STK_EINVAL, "bytes is NULL");
   int rc = check_common("stk_workspace_bytes", B, d, F, dtype);
   if (rc) return rc;
-  if (k < 1 || list_len(k) == 0) return fail(STK_EINVAL, "k out of range");
+  if (k < 1 || (list_len(k) == 0 && !(k <= F && F <= stk::kFullSortMaxF))) return fail(STK_EINVAL, "k out of range");
+  if (list_len(k) == 0) {  // whole-row sort: no workspace
+    *bytes = 0;
+    return STK_OK;
+  }
   // Sized for every path a call with these shapes may take: fp32 inputs
   // include the split X of the TF32 path (STK_FLAG_TF32 is a call flag).
   Plan pl;
@@ -500,7 +504,20 @@ int stk_exact_forward(const void* X, const void* W, const float* b, float* V, in
   if (!(flags & STK_FLAG_ANY_K) && !ref_k(k))
     return fail(STK_EINVAL, "streamtopk_cuda_exact: unsupported k=" + std::to_string(k) +
                                 ". Supported: 1,2,4,8,16,32,64,128.");
-  if (k > 128) return fail(STK_EINVAL, "streamtopk_cuda_exact: unsupported k=" + std::to_string(k) + " (k <= 128)");
+  if (k > 128) {
+    // Extension (STK_FLAG_ANY_K): k beyond the streaming lists for small F, by
+    // sorting whole rows (no workspace).
+    if (F > stk::kFullSortMaxF)
+      return fail(STK_EINVAL, "streamtopk_cuda_exact: unsupported k=" + std::to_string(k) +
+                                  " (k <= 128, or any k <= F when F <= " + std::to_string(stk::kFullSortMaxF) + ")");
+    if (B == 0) return STK_OK;
+    if (B > 0x7fffffffLL) return fail(STK_EINVAL, "B too large for the whole-row sort");
+    cudaError_t e = stk::launch_fullsort(X, W, b, V, I, B, d, (int)F, (int)k,
+                                         dtype == STK_F32 ? 0 : dtype == STK_F16 ? 1 : 2,
+                                         static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "fullsort_kernel launch");
+    return STK_OK;
+  }
   return encode(X, W, b, V, I, nullptr, B, d, F, k, dtype, flags, 0u, workspace, workspace_bytes,
                 static_cast<cudaStream_t>(stream));
 }

@@ -783,6 +783,74 @@ STK_INST_SIMT(32)
 STK_INST_SIMT(64)
 STK_INST_SIMT(128)
 
+// ---------------------------------------------------------------------------
+// Whole-row sort for small F (k up to F <= kFullSortMaxF, beyond the list
+// lengths of the streaming kernels): one CTA per row computes all F scores
+// (one warp per feature, lanes across d, fp32 accumulation) as 64-bit keys in
+// shared memory, sorts them with a block-wide bitonic network and writes the
+// first k.  Same key order as every other path (score, then smaller index).
+// ---------------------------------------------------------------------------
+constexpr int kFullSortThreads = 256;
+
+template <typename T>
+__global__ void __launch_bounds__(kFullSortThreads) fullsort_kernel(const T* __restrict__ X, const T* __restrict__ W,
+                                                                     const float* __restrict__ bias, float* __restrict__ V,
+                                                                     int32_t* __restrict__ I, int64_t d, int F, int k) {
+  __shared__ uint64_t keys[kFullSortMaxF];
+  const int64_t row = blockIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  int n = 1;
+  while (n < F) n <<= 1;
+  const T* x = X + row * d;
+  for (int f = warp; f < n; f += kFullSortThreads / 32) {
+    float acc = 0.f;
+    if (f < F) {
+      const T* w = W + (int64_t)f * d;
+      for (int64_t j = lane; j < d; j += 32) acc = fmaf(to_f32(x[j]), to_f32(w[j]), acc);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    }
+    if (lane == 0) keys[f] = f < F ? make_key(acc + bias[f], (uint32_t)f) : kEmptyKey;
+  }
+  __syncthreads();
+  for (int size = 2; size <= n; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = tid; i < n; i += kFullSortThreads) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const uint64_t a = keys[i], c = keys[j];
+          const bool desc = (i & size) == 0;
+          if (desc ? (a < c) : (a > c)) {
+            keys[i] = c;
+            keys[j] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int i = tid; i < k; i += kFullSortThreads) {
+    V[row * k + i] = key_value(keys[i]);
+    I[row * k + i] = key_index(keys[i]);
+  }
+}
+
+cudaError_t launch_fullsort(const void* X, const void* W, const float* bias, float* V, int32_t* I, int64_t B,
+                            int64_t d, int F, int k, int dtype, cudaStream_t stream) {
+  if (B <= 0) return cudaSuccess;
+  const unsigned grid = (unsigned)B;
+  if (dtype == 0)
+    fullsort_kernel<float><<<grid, kFullSortThreads, 0, stream>>>(static_cast<const float*>(X),
+                                                                  static_cast<const float*>(W), bias, V, I, d, F, k);
+  else if (dtype == 1)
+    fullsort_kernel<__half><<<grid, kFullSortThreads, 0, stream>>>(static_cast<const __half*>(X),
+                                                                   static_cast<const __half*>(W), bias, V, I, d, F, k);
+  else
+    fullsort_kernel<__nv_bfloat16><<<grid, kFullSortThreads, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(X), static_cast<const __nv_bfloat16*>(W), bias, V, I, d, F, k);
+  return cudaGetLastError();
+}
+
 __global__ void candidates_out_kernel(const uint64_t* __restrict__ partials, int L, int m_tiles, int64_t tiles,
                                       int64_t rows, int c, float* __restrict__ vals, int32_t* __restrict__ idxs) {
   const int64_t total = rows * tiles * c;

@@ -188,6 +188,12 @@ template <int L>
 cudaError_t launch_finish(const FinishArgs& fa, int grid, cudaStream_t stream);
 
 
+// Exact top-k of rows over F <= kFullSortMaxF features by a whole-row sort,
+// any 1 <= k <= F (dtype: 0 fp32, 1 fp16, 2 bf16; grid.x = B must fit).
+constexpr int kFullSortMaxF = 4096;
+cudaError_t launch_fullsort(const void* X, const void* W, const float* bias, float* V, int32_t* I, int64_t B,
+                            int64_t d, int F, int k, int dtype, cudaStream_t stream);
+
 // Per-tile candidates of the approximate path: partials[(tile * m_tiles + m) *
 // 128 + r][0..L) -> cand_vals / cand_idxs [(row) * tiles + tile][0..c),
 // empty keys as (-FLT_MAX, -1).

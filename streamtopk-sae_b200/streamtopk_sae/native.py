@@ -54,7 +54,7 @@ def streamtopk_cuda_exact_forward(X, W_enc, b_enc, k, flags=0):
     k = int(k)
     _require(1 <= k <= F, "k out of range")
     _require(d <= 4096 or (flags & _capi.STK_FLAG_ANY_D), "d exceeds D_MAX=4096")
-    _require(k in (1, 2, 4, 8, 16, 32, 64, 128) or ((flags & _capi.STK_FLAG_ANY_K) and k <= 128),
+    _require(k in (1, 2, 4, 8, 16, 32, 64, 128) or ((flags & _capi.STK_FLAG_ANY_K) and (k <= 128 or F <= 4096)),
              f"streamtopk_cuda_exact: unsupported k={k}. Supported: 1,2,4,8,16,32,64,128.")
     V = torch.empty((B, k), dtype=torch.float32, device=X.device)
     I = torch.empty((B, k), dtype=torch.int32, device=X.device)

@@ -7,7 +7,8 @@ streamtopk_sae/ops.py:43-83 in the reference.  Both run the sm_100a kernels of
 libstk_b200.so through its C ABI; there is no other compute path.
 
 Extensions (keyword-only, off by default so behaviour matches the reference):
-  allow_any_k  accept any 1 <= k <= 128 instead of {1,2,4,8,16,32,64,128}
+  allow_any_k  accept any 1 <= k <= 128 instead of {1,2,4,8,16,32,64,128}, and
+               any k <= F when F <= 4096 (whole-row sort; e.g. k = F = 4096)
   allow_any_d  lift the exact path's d <= 4096 limit
 
 Device-side errors.  The kernels bound every wait (pipeline barriers: 4 s; the

@@ -75,6 +75,26 @@ def test_config2_edge_set(case, dtype_name):
     check(V, I, Xr, Wr, br, k, RTOL[dtype_name])
 
 
+@pytest.mark.parametrize("dtype_name", ["fp32", "fp16", "bf16"])
+def test_config2_k_equals_F_4096(dtype_name):
+    """configs[1]'s edge case k = F for F = 4096 (the reference rejects it:
+    streamtopk_exact.cu:818-830; allowed here under allow_any_k by sorting
+    whole rows)."""
+    import streamtopk_sae as stk
+    B, d, F = 128, 768, 4096
+    X, W, b = _inputs(B, d, F, dtype_name, 6, "normal_1_over_d")
+    with pytest.raises(RuntimeError, match="unsupported k=4096"):
+        stk.topk_sae_cuda_exact(X, W, b, F)
+    V, I = stk.topk_sae_cuda_exact(X, W, b, F, allow_any_k=True)
+    torch.cuda.synchronize()
+    no_device_error()
+    Xr, Wr, br = _host(X, W, b)
+    check(V, I, Xr, Wr, br, F, RTOL[dtype_name])
+    assert torch.equal(torch.sort(I.long(), dim=1).values.cpu(), torch.arange(F).expand(B, F))
+    V2, I2 = stk.topk_sae_cuda_exact(X, W, b, 300, allow_any_k=True)   # k > 128 below F
+    assert torch.equal(I2, I[:, :300]) and torch.equal(V2, V[:, :300])
+
+
 def test_config3_full_F():
     """The north-star workload on one GPU, every row checked."""
     import streamtopk_sae as stk
