@@ -577,6 +577,75 @@ def run_b200(args, cfg):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# Memory mode: the reference's working-memory and max-F benchmarks
+# (bench/run_memory.py:40-70, bench/run_max_F.py:29-60 in the reference), each
+# cell measured in a fresh subprocess so the caching allocator starts clean.
+# ---------------------------------------------------------------------------
+MEMORY_CELLS = [dict(CONFIGS[2], dtype="bf16"), dict(CONFIGS[2], dtype="fp16"), dict(CONFIGS[2], dtype="fp32"),
+                CONFIGS[3], CONFIGS[4], CONFIGS[5]]
+MAX_F_CONFIGS = [dict(B=128, d=768, k=32, dtype="bf16"), dict(B=2048, d=768, k=32, dtype="bf16"),
+                 dict(B=128, d=2048, k=64, dtype="bf16")]   # the reference's two, plus the north-star shape
+
+
+def _memory_cell(mode, B, d, F, k, dtype, c):
+    """One cell in this (fresh) process: peak device memory of one call minus
+    inputs and outputs = the call's working memory (the library's workspace)."""
+    import torch
+    import streamtopk_sae as stk
+    dt = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}[dtype]
+    try:
+        torch.cuda.empty_cache()
+        torch.cuda.reset_peak_memory_stats()
+        X, W, b = stk.make_inputs(B, d, F, dtype=dt, seed=0, device="cuda")
+        base = torch.cuda.max_memory_allocated()
+        torch.cuda.reset_peak_memory_stats()
+        if mode == "approx":
+            V, I = stk.topk_sae_cuda_approx(X, W, b, k, c)
+        else:
+            V, I = stk.topk_sae_cuda_exact(X, W, b, k)
+        torch.cuda.synchronize()
+        peak = torch.cuda.max_memory_allocated()
+        out = B * k * 8
+        return {"status": "ok", "baseline_mem_mb": base / 1e6, "peak_mem_mb": peak / 1e6,
+                "working_mem_mb": (peak - base - out) / 1e6}
+    except torch.cuda.OutOfMemoryError:
+        return {"status": "OOM"}
+
+
+def _run_cell(mode, B, d, F, k, dtype, c=0, timeout=600):
+    cmd = [sys.executable, os.path.abspath(__file__), "--_memory-cell", mode, str(B), str(d), str(F), str(k), dtype,
+           str(c)]
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, cwd=REPO)
+    except subprocess.TimeoutExpired:
+        return {"status": "TIMEOUT"}
+    if r.returncode != 0:
+        return {"status": "ERR:" + r.stderr.strip()[-300:]}
+    return json.loads(r.stdout.strip().splitlines()[-1])
+
+
+def run_memory(args):
+    """Working memory per BASELINE config and the largest F (powers of two)
+    that fits one GPU, one JSON line each."""
+    for cfg in MEMORY_CELLS:
+        res = _run_cell(cfg["mode"], cfg["B"], cfg["d"], cfg["F"], cfg["k"], cfg["dtype"], cfg.get("c", 0))
+        print(json.dumps({"kind": "working_memory", **{kk: cfg[kk] for kk in ("mode", "B", "d", "F", "k", "dtype")},
+                          "c": cfg.get("c"), **res}), flush=True)
+    for cfg in MAX_F_CONFIGS:
+        lo, hi, best = 14, 30, None
+        while lo <= hi:
+            mid = (lo + hi) // 2
+            res = _run_cell("exact", cfg["B"], cfg["d"], 1 << mid, cfg["k"], cfg["dtype"])
+            if res.get("status") == "ok":
+                best, lo = 1 << mid, mid + 1
+            else:
+                hi = mid - 1
+        print(json.dumps({"kind": "max_F", **cfg, "max_F": best, "search": "powers of two 2^14..2^30, "
+                          "binary search, one subprocess per probe (reference bench/run_max_F.py)"}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -595,7 +664,18 @@ def main():
                          "peer mappings cannot be set up)")
     ap.add_argument("--shape", default=None,
                     help="B,d,F,k override of the config's shape (small cases for ncu captures)")
+    ap.add_argument("--memory", action="store_true",
+                    help="working memory per BASELINE config and the largest F per GPU (reference run_memory / "
+                         "run_max_F), one JSON line each")
+    ap.add_argument("--_memory-cell", nargs=7, default=None, help=argparse.SUPPRESS)
     args = ap.parse_args()
+    if args._memory_cell:
+        m, B, d, F, k, dt, c = args._memory_cell
+        sys.path.insert(0, os.path.join(REPO, "streamtopk-sae_b200"))
+        print(json.dumps(_memory_cell(m, int(B), int(d), int(F), int(k), dt, int(c))))
+        return 0
+    if args.memory:
+        return run_memory(args)
     cfg = dict(CONFIGS[args.config])
     if args.shape:
         cfg["B"], cfg["d"], cfg["F"], cfg["k"] = (int(v) for v in args.shape.split(","))

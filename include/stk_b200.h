@@ -49,9 +49,10 @@ enum stk_flags {
   STK_FLAG_ANY_K = 1, /* accept any 1 <= k <= 128, not only {1,2,4,8,16,32,64,128}; and any
                          k <= F when F <= 4096 (whole-row sort, no workspace) */
   STK_FLAG_ANY_D = 2, /* lift the reference's d <= 4096 limit */
-  STK_FLAG_SIMT = 4,    /* force the fp32 SIMT kernel (testing / comparison) */
+  STK_FLAG_SIMT = 4,    /* force the fp32-FMA SIMT kernel (testing / comparison, or bit-faithful fp32) */
   STK_FLAG_NO_PILOT = 8, /* skip the sampled threshold floor (testing / comparison) */
-  STK_FLAG_TF32 = 16,    /* fp32 inputs on tensor cores: 3-pass TF32 (hi*hi + hi*lo + lo*hi), d % 4 == 0 */
+  STK_FLAG_TF32 = 16,    /* fp32 inputs on tensor cores (3-pass TF32) also for d > 2048 (the default up to
+                            d = 2048, d % 4 == 0); otherwise fp32 uses the SIMT kernel */
   STK_FLAG_SEPARATE_FINISH = 32 /* finish the rows in a second kernel even where the score kernel
                                    could do it in its tail (testing / comparison) */
 };

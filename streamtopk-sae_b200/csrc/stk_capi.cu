@@ -218,6 +218,8 @@ struct Plan {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+constexpr int64_t kTf32DefaultMaxD = 2048;
+
 // Counters at the start of the zeroed sync region: [0] pilot arrivals,
 // [1] finish-barrier arrivals; the pilot histogram follows at kSyncBytes.
 constexpr size_t kSyncBytes = 256;
@@ -228,7 +230,12 @@ int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t 
   if (rc) return rc;
   pl->L = list_len(k);
   const bool aligned = (X == nullptr || aligned16(X)) && (W == nullptr || aligned16(W));
-  pl->tf32 = dtype == STK_F32 && (flags & STK_FLAG_TF32) && (d % 4 == 0) && !(flags & STK_FLAG_SIMT) && aligned;
+  // fp32 inputs run on tensor cores (3-pass TF32) by default up to d =
+  // kTf32DefaultMaxD, where its accuracy is shown against float64 to hold the
+  // fp32 tolerance; beyond that only on request (STK_FLAG_TF32).  STK_FLAG_SIMT
+  // forces fp32 FMA.
+  pl->tf32 = dtype == STK_F32 && ((flags & STK_FLAG_TF32) || d <= kTf32DefaultMaxD) && (d % 4 == 0) &&
+             !(flags & STK_FLAG_SIMT) && aligned;
   pl->tc = ((dtype == STK_BF16 || dtype == STK_F16) && (d % 8 == 0) && !(flags & STK_FLAG_SIMT) && aligned) ||
            pl->tf32;
   pl->grid = make_grid(B, F, sms);
@@ -251,18 +258,17 @@ int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t 
   return STK_OK;
 }
 
-// Optional override of the fused tile configuration,
-// "L,NT,STAGES,A,APP_SMEM,TOPG", for tuning.
-bool fused_override(int L, int* nt, int* stages, int* app, int* app_smem, int* topg) {
+// Optional override of the fused tile configuration, "L,NT,STAGES,A,APP_SMEM",
+// for tuning.
+bool fused_override(int L, int* nt, int* stages, int* app, int* app_smem) {
   const char* s = std::getenv("STK_FUSED_CFG");
   if (!s) return false;
-  int l = 0, n = 0, st = 0, a = 0, sm = 0, tg = 0;
-  if (std::sscanf(s, "%d,%d,%d,%d,%d,%d", &l, &n, &st, &a, &sm, &tg) != 6 || l != L) return false;
+  int l = 0, n = 0, st = 0, a = 0, sm = 0;
+  if (std::sscanf(s, "%d,%d,%d,%d,%d", &l, &n, &st, &a, &sm) != 5 || l != L) return false;
   *nt = n;
   *stages = st;
   *app = a;
   *app_smem = sm;
-  *topg = tg;
   return true;
 }
 
@@ -284,8 +290,7 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   int stages = nt128 ? (pl.L == 128 ? 3 : pl.L == 64 ? 4 : 5) : (pl.L == 128 ? 2 : 3);
   int nslots = pl.L == 64 ? 16 : 32;
   int app_smem = pl.L == 128 ? 0 : 1;
-  int topg = 0;
-  fused_override(pl.L, &nt, &stages, &nslots, &app_smem, &topg);
+  fused_override(pl.L, &nt, &stages, &nslots, &app_smem);
   CUtensorMap tx, txl, tw, tw32;
   const bool bf16 = dtype == STK_BF16;
   int rc = STK_OK;
@@ -347,16 +352,14 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   }
   cudaError_t e = cudaErrorInvalidValue;
   ProfScope prof(kProfFused, stream);
-#define STK_TRY_FUSED(Lc, NTc, Sc, Ac, SMc, TGc)                                                      \
-  if (!pl.tf32 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc &&  \
-      (topg != 0) == TGc)                                                                               \
-    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, TGc, false>(tx, txl, tw, tw32, p, pl.ctas, stream);
+#define STK_TRY_FUSED(Lc, NTc, Sc, Ac, SMc)                                                           \
+  if (!pl.tf32 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc)    \
+    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, false>(tx, txl, tw, tw32, p, pl.ctas, stream);
   STK_FUSED_CONFIGS(STK_TRY_FUSED)
 #undef STK_TRY_FUSED
-#define STK_TRY_FUSED_TF32(Lc, NTc, Sc, Ac, SMc, TGc)                                                 \
-  if (pl.tf32 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc &&   \
-      (topg != 0) == TGc)                                                                               \
-    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, TGc, true>(tx, txl, tw, tw32, p, pl.ctas, stream);
+#define STK_TRY_FUSED_TF32(Lc, NTc, Sc, Ac, SMc)                                                      \
+  if (pl.tf32 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc)     \
+    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, true>(tx, txl, tw, tw32, p, pl.ctas, stream);
   STK_FUSED_TF32_CONFIGS(STK_TRY_FUSED_TF32)
 #undef STK_TRY_FUSED_TF32
   if (e != cudaSuccess) return cuda_fail(e, "fused_topk_kernel launch");

@@ -137,29 +137,17 @@ __device__ __forceinline__ uint64_t& top_slot(uint32_t top, int s, int r) {
   return smem_keys(top)[s * kRows + (r ^ (s & 31))];
 }
 
-// Slot s of row r's top list: in shared memory (swizzled, at byte offset
-// top_off) or, TOPG, in global memory (the row's L contiguous keys at topg --
-// the unit's output slot itself, L2-resident, touched only by this thread).
-template <bool TOPG>
-__device__ __forceinline__ uint64_t& top_ref(uint32_t top_off, uint64_t* topg, int s, int r) {
-  if constexpr (TOPG)
-    return topg[s];
-  else
-    return top_slot(top_off, s, r);
-}
-
 // Merge row r's n waiting survivors (A append slots, unsorted) into its sorted
 // top list and return the new threshold: the value of the (kth+1)-th best key,
 // never below floor_thr (a lower bound known from elsewhere, -inf if none).
 // The append slots are in shared memory (APP_SMEM, app_off = byte offset from
 // stk_smem) or in global memory (app_g).  Kept out of line: it runs rarely and
 // is large.
-template <int L, int A, bool APP_SMEM, bool TOPG>
-__device__ __noinline__ float merge_survivors(uint32_t top_off, uint64_t* topg, uint32_t app_off,
-                                              const uint64_t* __restrict__ app_g, int r, int n, int kth,
-                                              float floor_thr) {
+template <int L, int A, bool APP_SMEM>
+__device__ __noinline__ float merge_survivors(uint32_t top_off, uint32_t app_off, const uint64_t* __restrict__ app_g,
+                                              int r, int n, int kth, float floor_thr) {
   static_assert(A == 16 || A == 32, "append slots");
-#define TOP(s) top_ref<TOPG>(top_off, topg, (s), r)
+#define TOP(s) top_slot(top_off, (s), r)
   uint64_t a[A];
 #pragma unroll
   for (int s = 0; s < A; ++s) {
@@ -227,10 +215,9 @@ __device__ __forceinline__ float pick32(const float (&vals)[32], int j) {
   return (j & 1) ? t2[1] : t2[0];
 }
 
-template <int L, int A, bool APP_SMEM, bool TOPG = false>
+template <int L, int A, bool APP_SMEM>
 struct RowTopK {
-  uint32_t top;     // byte offset of top[0] from stk_smem (!TOPG)
-  uint64_t* topg;   // the row's list in global memory (TOPG)
+  uint32_t top;     // byte offset of top[0] from stk_smem
   uint32_t app_s;   // byte offset of the shared append slots (APP_SMEM)
   uint64_t* app_g;  // global append slots (!APP_SMEM)
   int r;            // row within the M tile
@@ -239,10 +226,8 @@ struct RowTopK {
   float floor_thr;  // known lower bound of the row's k-th score (-inf if none)
   int kth;          // k - 1
 
-  __device__ __forceinline__ void init(uint32_t top_, uint64_t* topg_, uint32_t app_s_, uint64_t* app_g_, int row,
-                                       int k) {
+  __device__ __forceinline__ void init(uint32_t top_, uint32_t app_s_, uint64_t* app_g_, int row, int k) {
     top = top_;
-    topg = topg_;
     app_s = app_s_;
     app_g = app_g_;
     r = row;
@@ -250,17 +235,12 @@ struct RowTopK {
     thr = -__int_as_float(0x7f800000);
     floor_thr = thr;
     kth = k - 1;
-    if constexpr (TOPG) {
 #pragma unroll 4
-      for (int s = 0; s < L / 2; ++s) reinterpret_cast<ulonglong2*>(topg)[s] = make_ulonglong2(0ull, 0ull);
-    } else {
-#pragma unroll 4
-      for (int s = 0; s < L; ++s) top_slot(top, s, r) = kEmptyKey;
-    }
+    for (int s = 0; s < L; ++s) top_slot(top, s, r) = kEmptyKey;
   }
 
   __device__ __forceinline__ void flush() {
-    thr = merge_survivors<L, A, APP_SMEM, TOPG>(top, topg, app_s, app_g, r, cnt, kth, floor_thr);
+    thr = merge_survivors<L, A, APP_SMEM>(top, app_s, app_g, r, cnt, kth, floor_thr);
     cnt = 0;
   }
 

@@ -225,12 +225,12 @@ __device__ __forceinline__ void load_bias_tile(const float* __restrict__ bias, i
 // that the small terms do not add to the rounding of the large accumulator);
 // the epilogue (warps 4-7) adds the two.  The dropped Xl*Wl term is below
 // 2^-20 of |x||w|.
-template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPG, bool TF32>
+template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TF32>
 __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
     fused_topk_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_xl,
                       const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_w32,
                       const FusedParams p) {
-  using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM, TOPG>;
+  using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM>;
   constexpr int kSplitThreads = 64;                 // warps 2-3 (TF32)
   constexpr int kFirstEpiWarp = TF32 ? 4 : 2;
   constexpr uint32_t kWRowBytes = TF32 ? 64u : 128u;  // bytes of one W row in a stage
@@ -448,7 +448,7 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
     const uint32_t top_s = (uint32_t)(reinterpret_cast<uint8_t*>(top) - stk_smem);
     const uint32_t app_s = (uint32_t)(reinterpret_cast<uint8_t*>(smem + Cfg::kAppOff) - stk_smem);
     uint64_t* app_cta = p.app + (size_t)blockIdx.x * (kAppendMax * kRows);
-    RowTopK<L, A, APP_SMEM, TOPG> acc;
+    RowTopK<L, A, APP_SMEM> acc;
     uint32_t tile = 0;
     bool ok = true;
     TileWalk<NT> cur;
@@ -459,8 +459,7 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
       TileWalk<NT> nxt = cur;
       nxt.next(g);
       if (nxt.valid(g)) load_bias_tile<NT>(p.bias, nxt.ft, nxt.width(), p.F, lane, bnext);
-      if (cur.first_of_unit())
-        acc.init(top_s, p.partials + ((int64_t)cur.u * kRows + r) * L, app_s, app_cta, r, p.k);
+      if (cur.first_of_unit()) acc.init(top_s, app_s, app_cta, r, p.k);
       const bool row_ok = (int64_t)cur.m * kRows + r < p.B;
       const int w = cur.width();
       const int a = tile & 1;
@@ -557,7 +556,7 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
       }
       if (cur.last_of_unit()) {
         acc.finish();
-        if constexpr (!TOPG) store_partials<L>(top_s, p.partials + (int64_t)cur.u * kRows * L, q * 32, lane);
+        store_partials<L>(top_s, p.partials + (int64_t)cur.u * kRows * L, q * 32, lane);
         __threadfence();  // the lists are read by other CTAs in the finish step
       }
 #pragma unroll
@@ -636,7 +635,7 @@ __global__ void __launch_bounds__(kSimtThreads, 1) simt_topk_kernel(const T* __r
     int64_t fb, fe;
     unit_range(g, u, m, fb, fe);
     const int64_t row0 = (int64_t)m * kRows;
-    if (tid < kRows) acc.init(top_s, nullptr, 0u, app_cta, tid, p.k);
+    if (tid < kRows) acc.init(top_s, 0u, app_cta, tid, p.k);
     for (int64_t ft = fb; ft < fe; ft += Cfg::kNT) {
       const int w = (int)min((int64_t)Cfg::kNT, fe - ft);
       float c[8][8];
@@ -711,11 +710,11 @@ __global__ void __launch_bounds__(kFinishThreads) finish_kernel(const FinishArgs
 // ---------------------------------------------------------------------------
 // Explicit instantiations and launch helpers (host side of this TU).
 // ---------------------------------------------------------------------------
-template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPG, bool TF32>
+template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TF32>
 cudaError_t launch_fused(const CUtensorMap& tx, const CUtensorMap& txl, const CUtensorMap& tw, const CUtensorMap& tw32,
                          const FusedParams& p, int grid, cudaStream_t stream) {
-  using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM, TOPG>;
-  auto kern = fused_topk_kernel<L, NT, STAGES, A, APP_SMEM, TOPG, TF32>;
+  using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM>;
+  auto kern = fused_topk_kernel<L, NT, STAGES, A, APP_SMEM, TF32>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   if (e != cudaSuccess) return e;
   kern<<<grid, TF32 ? kFusedThreads + 64 : kFusedThreads, Cfg::kSmemBytes, stream>>>(tx, txl, tw, tw32, p);
@@ -762,15 +761,15 @@ cudaError_t launch_finish(const FinishArgs& fa, int grid, cudaStream_t stream) {
   return cudaLaunchKernelEx(&cfg, finish_kernel<L>, fa);
 }
 
-#define STK_INST_FUSED(L, NT, S, A, SM, TG)                                                                    \
-  template cudaError_t launch_fused<L, NT, S, A, SM, TG, false>(const CUtensorMap&, const CUtensorMap&,        \
-                                                                const CUtensorMap&, const CUtensorMap&,        \
-                                                                const FusedParams&, int, cudaStream_t);
+#define STK_INST_FUSED(L, NT, S, A, SM)                                                                      \
+  template cudaError_t launch_fused<L, NT, S, A, SM, false>(const CUtensorMap&, const CUtensorMap&,            \
+                                                            const CUtensorMap&, const CUtensorMap&,            \
+                                                            const FusedParams&, int, cudaStream_t);
 STK_FUSED_CONFIGS(STK_INST_FUSED)
-#define STK_INST_FUSED_TF32(L, NT, S, A, SM, TG)                                                               \
-  template cudaError_t launch_fused<L, NT, S, A, SM, TG, true>(const CUtensorMap&, const CUtensorMap&,         \
-                                                               const CUtensorMap&, const CUtensorMap&,         \
-                                                               const FusedParams&, int, cudaStream_t);
+#define STK_INST_FUSED_TF32(L, NT, S, A, SM)                                                                 \
+  template cudaError_t launch_fused<L, NT, S, A, SM, true>(const CUtensorMap&, const CUtensorMap&,             \
+                                                           const CUtensorMap&, const CUtensorMap&,             \
+                                                           const FusedParams&, int, cudaStream_t);
 STK_FUSED_TF32_CONFIGS(STK_INST_FUSED_TF32)
 
 #define STK_INST_SIMT(L)                                                                                         \
