@@ -598,7 +598,8 @@ def _memory_cell(mode, B, d, F, k, dtype, c):
         torch.cuda.empty_cache()
         torch.cuda.reset_peak_memory_stats()
         X, W, b = stk.make_inputs(B, d, F, dtype=dt, seed=0, device="cuda")
-        base = torch.cuda.max_memory_allocated()
+        torch.cuda.synchronize()
+        base = torch.cuda.memory_allocated()   # the inputs (generation temporaries are freed)
         torch.cuda.reset_peak_memory_stats()
         if mode == "approx":
             V, I = stk.topk_sae_cuda_approx(X, W, b, k, c)

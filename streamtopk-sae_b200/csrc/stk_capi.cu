@@ -199,7 +199,9 @@ stk::UnitGrid make_tile_grid(int64_t B, int64_t F) {
   return g;
 }
 
-size_t partial_bytes(const stk::UnitGrid& g, int L) { return (size_t)g.units * stk::kRows * L * sizeof(uint64_t); }
+size_t partial_bytes(const stk::UnitGrid& g, int pitch) {
+  return (size_t)g.units * stk::kRows * pitch * sizeof(uint64_t);
+}
 
 struct Plan {
   bool tc;    // tcgen05 path
@@ -209,6 +211,7 @@ struct Plan {
   int ctas;
   bool pilot;
   bool fin_fused;  // the fused kernel finishes the rows itself (all units resident at once)
+  int pitch;       // keys per row list in the partials: L, or L + kAppendMax (sorted tail run, fused finish)
   size_t ws_partials;
   size_t ws_app;
   size_t ws_sync;   // zeroed per call: barrier counters, then the pilot histogram and row maxima
@@ -242,7 +245,6 @@ int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t 
   pl->ctas = pl->grid.units < sms ? pl->grid.units : sms;
   // partial lists, then one append buffer per CTA, then (optionally) the
   // pilot histogram, row maxima and arrival counter (256-byte aligned parts)
-  pl->ws_partials = (partial_bytes(pl->grid, pl->L) + 255) & ~size_t(255);
   pl->ws_app = ((size_t)pl->ctas * stk::kAppendBytesPerCta + 255) & ~size_t(255);
   // The sample step needs one unit per CTA (all CTAs resident together) and
   // pays off when each CTA streams several chunks after its sample.
@@ -251,6 +253,10 @@ int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t 
   // One unit per CTA and every CTA resident (one per SM): the fused kernel
   // meets at a grid barrier and finishes the rows itself, no second launch.
   pl->fin_fused = pl->tc && pl->grid.units <= pl->ctas && !(flags & STK_FLAG_SEPARATE_FINISH);
+  // With the fused finish each row list carries its last survivors as a sorted
+  // second run (no final merge in the score kernel).
+  pl->pitch = (pl->fin_fused && !std::getenv("STK_FULL_FLUSH")) ? pl->L + stk::kAppendMax : pl->L;
+  pl->ws_partials = (partial_bytes(pl->grid, pl->pitch) + 255) & ~size_t(255);
   const size_t pilot_bytes = pl->pilot ? (size_t)pl->grid.m_tiles * stk::kRows * (stk::kPilotBins + 1) * 4 : 0;
   pl->ws_sync = (pl->pilot || pl->fin_fused) ? ((kSyncBytes + pilot_bytes + 255) & ~size_t(255)) : 0;
   pl->ws_split = pl->tf32 ? (((size_t)B * d * 4 + 255) & ~size_t(255)) : 0;
@@ -334,6 +340,7 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   p.pilot_count = nullptr;
   p.tail_count = nullptr;
   p.finish = 0;
+  p.list_pitch = pl.pitch;
   std::memset(&p.fin, 0, sizeof p.fin);
   if (pl.ws_sync) {
     uint8_t* base = reinterpret_cast<uint8_t*>(partials) + pl.ws_partials + pl.ws_app;
@@ -413,13 +420,15 @@ int run_finish(int L, const stk::FinishArgs& fa, cudaStream_t stream) {
   return STK_OK;
 }
 
-stk::FinishArgs finish_args(const uint64_t* lists, int nlists, int64_t stride, int64_t rows, int64_t k, float* V,
-                            int32_t* I, uint64_t* keys_out, const stk::ExchangeDev* ex) {
+stk::FinishArgs finish_args(const uint64_t* lists, int nlists, int64_t stride, int pitch, int tail, int64_t rows,
+                            int64_t k, float* V, int32_t* I, uint64_t* keys_out, const stk::ExchangeDev* ex) {
   stk::FinishArgs fa;
   std::memset(&fa, 0, sizeof fa);
   fa.lists = lists;
   fa.nlists = nlists;
   fa.stride = stride;
+  fa.pitch = pitch;
+  fa.tail = tail;
   fa.rows = rows;
   fa.k = (int)k;
   fa.V = V;
@@ -437,8 +446,8 @@ int score_and_finish(const Plan& pl, const void* X, const void* W, const float* 
                      const stk::ExchangeDev* ex, void* workspace, cudaStream_t stream) {
   uint64_t* partials = static_cast<uint64_t*>(workspace);
   uint64_t* app = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace) + pl.ws_partials);
-  const stk::FinishArgs fa = finish_args(partials, pl.grid.segs, (int64_t)pl.grid.m_tiles * stk::kRows, B, k, V, I,
-                                         keys_out, ex);
+  const stk::FinishArgs fa = finish_args(partials, pl.grid.segs, (int64_t)pl.grid.m_tiles * stk::kRows, pl.pitch,
+                                         pl.pitch - pl.L, B, k, V, I, keys_out, ex);
   int rc = pl.tc ? run_fused(pl, X, W, b, partials, app, B, d, F, k, dtype, index_offset,
                              pl.fin_fused ? &fa : nullptr, stream)
                  : run_simt(pl, X, W, b, partials, app, B, d, F, k, dtype, index_offset, stream);
@@ -561,7 +570,7 @@ int stk_merge_keys(const uint64_t* lists, int64_t nlists, int64_t B, int64_t k, 
   if (B < 0) return fail(STK_EINVAL, "B must be >= 0");
   if (nlists > 0x7fffffff) return fail(STK_EINVAL, "nlists out of range");
   if (reinterpret_cast<uintptr_t>(lists) & 15) return fail(STK_EINVAL, "lists must be 16-byte aligned");
-  return run_finish(list_len(k), finish_args(lists, (int)nlists, B, B, k, V, I, nullptr, nullptr),
+  return run_finish(list_len(k), finish_args(lists, (int)nlists, B, list_len(k), 0, B, k, V, I, nullptr, nullptr),
                     static_cast<cudaStream_t>(stream));
 }
 
@@ -577,7 +586,8 @@ int candidates_plan(const void* X, const void* W, int64_t B, int64_t d, int64_t 
   if (pl->grid.units > 0x7fffffff / 2) return fail(STK_EINVAL, "too many candidate tiles");
   pl->ctas = pl->grid.units < sms ? pl->grid.units : sms;
   pl->pilot = false;
-  pl->ws_partials = (partial_bytes(pl->grid, pl->L) + 255) & ~size_t(255);
+  pl->pitch = pl->L;
+  pl->ws_partials = (partial_bytes(pl->grid, pl->pitch) + 255) & ~size_t(255);
   pl->ws_app = ((size_t)pl->ctas * stk::kAppendBytesPerCta + 255) & ~size_t(255);
   pl->ws_sync = 0;
   pl->fin_fused = false;
@@ -834,7 +844,7 @@ int stk_exchange_forward(stk_exchange* x, const void* X, const void* W_shard, co
     return score_and_finish(pl, X, W_shard, b_shard, V, I, nullptr, B, d, F_shard, k, dtype, (uint32_t)index_offset,
                             &x->dev, workspace, s);
   // Empty shard: publish empty lists (every rank's finish waits for all ranks).
-  return run_finish(x->L, finish_args(nullptr, 0, 0, B, k, V, I, nullptr, &x->dev), s);
+  return run_finish(x->L, finish_args(nullptr, 0, 0, x->L, 0, B, k, V, I, nullptr, &x->dev), s);
 }
 
 int stk_exchange_destroy(stk_exchange* x) {

@@ -215,6 +215,34 @@ __device__ __forceinline__ float pick32(const float (&vals)[32], int j) {
   return (j & 1) ? t2[1] : t2[0];
 }
 
+// The n (<= A) unsorted append slots of row r, sorted descending and padded
+// with empty keys to kAppendMax keys, stored at dst (16-byte aligned).  Out of
+// line like merge_survivors: it runs once per unit.
+template <int A, bool APP_SMEM>
+__device__ __noinline__ void store_sorted_tail(uint32_t app_off, const uint64_t* __restrict__ app_g, int r, int n,
+                                               uint64_t* __restrict__ dst) {
+  ulonglong2* d = reinterpret_cast<ulonglong2*>(dst);
+  if (n > 0) {
+    uint64_t a[A];
+#pragma unroll
+    for (int s = 0; s < A; ++s) {
+      if constexpr (APP_SMEM)
+        a[s] = (s < n) ? smem_keys(app_off)[s * kRows + r] : kEmptyKey;
+      else
+        a[s] = (s < n) ? (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(app_g + s * kRows + r))
+                       : kEmptyKey;
+    }
+    sort_desc<A>(a);
+#pragma unroll
+    for (int i = 0; i < A / 2; ++i) d[i] = make_ulonglong2(a[2 * i], a[2 * i + 1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < A / 2; ++i) d[i] = make_ulonglong2(0ull, 0ull);
+  }
+#pragma unroll
+  for (int i = A / 2; i < kAppendMax / 2; ++i) d[i] = make_ulonglong2(0ull, 0ull);
+}
+
 template <int L, int A, bool APP_SMEM>
 struct RowTopK {
   uint32_t top;     // byte offset of top[0] from stk_smem
@@ -296,6 +324,14 @@ struct RowTopK {
 
   __device__ __forceinline__ void finish() {
     if (__any_sync(0xffffffffu, cnt > 0)) flush();
+  }
+
+  // Instead of a final flush: writes the pending survivors, sorted descending
+  // and padded with empty keys to kAppendMax, at dst (16-byte aligned) -- a
+  // second sorted run beside the row's list, which the finish step reads too.
+  __device__ __forceinline__ void store_tail(uint64_t* dst) {
+    store_sorted_tail<A, APP_SMEM>(app_s, app_g, r, cnt, dst);
+    cnt = 0;
   }
 };
 

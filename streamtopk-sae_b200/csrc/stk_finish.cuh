@@ -10,13 +10,19 @@
 // bit-identical results: keys are unique, so a row's top-k is unique.
 //
 // Per row:
-//   1. tau = the k-th largest list head.  The k largest heads are k distinct
-//      keys, so the row's k-th key is >= tau (tau = 1, every key, when fewer
-//      than k lists are non-empty).
-//   2. Every key >= tau is gathered into shared memory (one thread per list; a
-//      list is read 4 keys at a time until a key below tau: lists are sorted).
-//      The score kernel's lists are sparse -- each key passed the row's
-//      threshold floor -- so this is ~1.3 k keys per row on Gaussian data.
+//   1. tau = the larger of the k-th largest list head and the largest k-th key
+//      of any one list.  The k largest heads are k distinct keys, and a list
+//      holds k keys >= its own k-th key, so either way the row's k-th key is
+//      >= tau (tau = 1, every key, when neither bound exists).  The heads bound
+//      is the tight one for the score kernel's many sparse lists, the k-th key
+//      bound for the few full lists of the exchange.
+//   2. Every key >= tau is gathered into shared memory.  Many lists: one
+//      thread per list, 4 keys at a time until a key below tau (lists are
+//      sorted).  The score kernel's lists are sparse -- each key passed the
+//      row's threshold floor -- so this is ~1.3 k keys per row on Gaussian
+//      data.  Few lists (<= kFinishFewLists, e.g. one per GPU): one thread per
+//      4-key chunk, all chunks at once, so a list costs one memory round trip
+//      whatever its depth.
 //   3. Each candidate's position in the row's sorted result is the number of
 //      larger candidates (keys are distinct): one thread per candidate.
 //   More candidates than kFinishCap (adversarial inputs): the lists are folded
@@ -41,8 +47,9 @@ constexpr int kFinishCap = 1024;      // candidates ranked by counting
 constexpr int kFinishMaxLists = 256;  // lists whose heads are held in shared memory
 constexpr int kFoldBatch = 8;         // lists loaded per warp and memory round trip (fold)
 constexpr int kFinishMaxWarps = 8;    // fold tree buffer: kFinishMaxWarps * L <= kFinishCap
+constexpr int kFinishFewLists = 32;   // at most this many lists: gather chunk-parallel
 
-struct FinishSmem {
+struct __align__(16) FinishSmem {
   uint64_t heads[kFinishMaxLists];
   uint64_t cand[kFinishCap];
   uint64_t best[128];
@@ -67,25 +74,35 @@ __device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsign
 
 __device__ __forceinline__ bool list_on(uint32_t mask, int s) { return s >= 32 || ((mask >> s) & 1u); }
 
-// Best L keys of row b over the nlists sorted lists (list s of row b at
-// lists[(s * stride + b) * L], L keys, descending, empty keys 0 at the end),
-// written to sm.best[0..L) descending with empty keys after the last one.
-// Lists s < 32 whose bit is clear in list_mask count as empty.  Every thread of
-// the CTA calls it (nthreads = blockDim.x, at most kFinishMaxWarps warps); it
-// ends with a __syncthreads.  Lists must be 16-byte aligned.
+// Best L keys of row b over nlists lists, written to sm.best[0..L) descending
+// with empty keys after the last one.  List s of row b starts at
+// lists[(s * stride + b) * pitch]: L keys descending (empty keys 0 at the end),
+// then, if tail > 0, a second descending run of `tail` keys (the score kernel's
+// last survivors, stored without a final merge).  Lists s < 32 whose bit is
+// clear in list_mask count as empty.  Every thread of the CTA calls it
+// (nthreads = blockDim.x, at most kFinishMaxWarps warps); it ends with a
+// __syncthreads.  Lists must be 16-byte aligned.
 template <int L>
-__device__ void select_row(const uint64_t* __restrict__ lists, int nlists, int64_t stride, int64_t b, int k,
-                           uint32_t list_mask, FinishSmem& sm, int tid, int nthreads) {
+__device__ void select_row(const uint64_t* __restrict__ lists, int nlists, int64_t stride, int pitch, int tail,
+                           int64_t b, int k, uint32_t list_mask, FinishSmem& sm, int tid, int nthreads) {
   const bool use_heads = nlists <= kFinishMaxLists;
   if (tid == 0) {
     sm.tau = 1ull;
     sm.cnt = 0;
   }
+  uint64_t kth = 0ull;  // largest k-th key of one list among this thread's lists
   if (use_heads)
-    for (int s = tid; s < nlists; s += nthreads)
-      sm.heads[s] = list_on(list_mask, s)
-                        ? (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(lists + ((int64_t)s * stride + b) * L))
-                        : 0ull;
+    for (int s = tid; s < nlists; s += nthreads) {
+      const uint64_t* ps = lists + ((int64_t)s * stride + b) * pitch;
+      const bool on = list_on(list_mask, s);
+      uint64_t h = 0ull;
+      if (on) {
+        h = (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(ps));
+        if (tail > 0) h = kmax(h, (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(ps + L)));
+        if (k <= L) kth = kmax(kth, (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(ps + k - 1)));
+      }
+      sm.heads[s] = h;
+    }
   __syncthreads();
   if (use_heads) {
     for (int s = tid; s < nlists; s += nthreads) {
@@ -93,28 +110,40 @@ __device__ void select_row(const uint64_t* __restrict__ lists, int nlists, int64
       if (h == 0ull) continue;
       int r = 0;
       for (int j = 0; j < nlists; ++j) r += sm.heads[j] > h ? 1 : 0;
-      if (r == k - 1) sm.tau = h;
+      if (r == k - 1) atomicMax(reinterpret_cast<unsigned long long*>(&sm.tau), (unsigned long long)h);
     }
+    if (kth != 0ull) atomicMax(reinterpret_cast<unsigned long long*>(&sm.tau), (unsigned long long)kth);
   }
   __syncthreads();
   const uint64_t tau = sm.tau;
-  if (use_heads) {
+  auto take4 = [&](const uint64_t* p4) {
+    const ulonglong2 u0 = __ldcg(reinterpret_cast<const ulonglong2*>(p4));
+    const ulonglong2 u1 = __ldcg(reinterpret_cast<const ulonglong2*>(p4 + 2));
+    const uint64_t kk[4] = {u0.x, u0.y, u1.x, u1.y};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (kk[j] >= tau) {
+        const int pos = atomicAdd(&sm.cnt, 1);
+        if (pos < kFinishCap) sm.cand[pos] = kk[j];
+      }
+    }
+    return kk[3] >= tau;  // the run may continue past these 4 keys
+  };
+  if (use_heads && nlists <= kFinishFewLists) {
+    const int chunks = (L + tail) / 4;
+    for (int t = tid; t < nlists * chunks; t += nthreads) {
+      const int s = t / chunks, q = (t % chunks) * 4;
+      if (sm.heads[s] < tau) continue;
+      take4(lists + ((int64_t)s * stride + b) * pitch + q);
+    }
+  } else if (use_heads) {
     for (int s = tid; s < nlists; s += nthreads) {
       if (sm.heads[s] < tau) continue;  // empty lists too (tau >= 1)
-      const uint64_t* ps = lists + ((int64_t)s * stride + b) * L;
-      for (int q = 0; q < L; q += 4) {
-        const ulonglong2 u0 = __ldcg(reinterpret_cast<const ulonglong2*>(ps + q));
-        const ulonglong2 u1 = __ldcg(reinterpret_cast<const ulonglong2*>(ps + q + 2));
-        const uint64_t kk[4] = {u0.x, u0.y, u1.x, u1.y};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if (kk[j] >= tau) {
-            const int pos = atomicAdd(&sm.cnt, 1);
-            if (pos < kFinishCap) sm.cand[pos] = kk[j];
-          }
-        }
-        if (kk[3] < tau) break;  // sorted: the rest is smaller
-      }
+      const uint64_t* ps = lists + ((int64_t)s * stride + b) * pitch;
+      for (int q = 0; q < L; q += 4)
+        if (!take4(ps + q)) break;  // sorted: the rest is smaller
+      for (int q = 0; q < tail; q += 4)
+        if (!take4(ps + L + q)) break;
     }
   }
   __syncthreads();
@@ -130,24 +159,31 @@ __device__ void select_row(const uint64_t* __restrict__ lists, int nlists, int64
     __syncthreads();
     return;
   }
-  // Fold: warp w merges lists w, w + nw, ... into its best L (a list whose
-  // best key does not beat the warp's current L-th is skipped), then warp 0
-  // merges the warps' results.
+  // Fold: warp w merges runs w, w + nw, ... (every list's L-key run, then
+  // every list's tail run, each as a sorted list of up to L keys) into its best
+  // L (a run whose best key does not beat the warp's current L-th is skipped),
+  // then warp 0 merges the warps' results.
   constexpr int E = L / 32;
   const int warp = tid >> 5, lane = tid & 31, nw = nthreads >> 5;
+  const int nruns = tail > 0 ? 2 * nlists : nlists;
   uint64_t acc[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) acc[e] = 0ull;
-  for (int s0 = warp; s0 < nlists; s0 += nw * kFoldBatch) {
+  for (int v0 = warp; v0 < nruns; v0 += nw * kFoldBatch) {
     uint64_t buf[kFoldBatch][E];
 #pragma unroll
     for (int q = 0; q < kFoldBatch; ++q) {
-      const int s = s0 + q * nw;
-      const bool on = s < nlists && list_on(list_mask, s) && (!use_heads || sm.heads[s] >= tau);
-      const uint64_t* ps = lists + ((int64_t)s * stride + b) * L;
+      const int v = v0 + q * nw;
+      const bool is_tail = v >= nlists;
+      const int s = is_tail ? v - nlists : v;
+      const bool on = v < nruns && list_on(list_mask, s) && (!use_heads || sm.heads[s] >= tau);
+      const uint64_t* ps = lists + ((int64_t)s * stride + b) * pitch + (is_tail ? L : 0);
+      const int len = is_tail ? tail : L;
 #pragma unroll
       for (int e = 0; e < E; ++e)
-        buf[q][e] = on ? (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(ps + e * 32 + lane)) : 0ull;
+        buf[q][e] = (on && e * 32 + lane < len)
+                        ? (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(ps + e * 32 + lane))
+                        : 0ull;
     }
 #pragma unroll
     for (int q = 0; q < kFoldBatch; ++q) {
@@ -189,21 +225,21 @@ __device__ __forceinline__ void write_row(const FinishArgs& fa, const FinishSmem
 }
 
 // Stores sm.best (row b) into slot [slot][rank] of every rank's receive
-// buffer and sets the row's flag there to `tag` (warp p -> rank p).
+// buffer and sets the row's flag there to `tag`: thread p (of the first
+// warp) writes rank p's copy with 16-byte stores and then the flag with a
+// system-scope release store, so the row is visible to rank p before its flag
+// by program order alone.
 template <int L>
 __device__ __forceinline__ void publish_row(const ExchangeDev& ex, const FinishSmem& sm, int slot,
-                                            unsigned long long tag, int64_t b, int tid, int nthreads) {
-  const int warp = tid >> 5, lane = tid & 31, nw = nthreads >> 5;
-  for (int p = warp; p < ex.world; p += nw) {
-    const int64_t at = ((int64_t)slot * ex.world + ex.rank) * ex.max_rows + b;
-    uint64_t* dst = ex.peer_recv[p] + at * L;
-#pragma unroll
-    for (int e = 0; e < L / 32; ++e)
-      __stcg(reinterpret_cast<unsigned long long*>(dst + e * 32 + lane), (unsigned long long)sm.best[e * 32 + lane]);
-    __threadfence_system();
-    __syncwarp();
-    if (lane == 0) st_release_sys_u64(ex.peer_flag[p] + at, tag);
-  }
+                                            unsigned long long tag, int64_t b, int tid) {
+  if (tid >= ex.world) return;
+  const int p = tid;
+  const int64_t at = ((int64_t)slot * ex.world + ex.rank) * ex.max_rows + b;
+  ulonglong2* dst = reinterpret_cast<ulonglong2*>(ex.peer_recv[p] + at * L);
+  const ulonglong2* src = reinterpret_cast<const ulonglong2*>(sm.best);
+#pragma unroll 8
+  for (int i = 0; i < L / 2; ++i) __stcg(dst + i, src[i]);
+  st_release_sys_u64(ex.peer_flag[p] + at, tag);
 }
 
 // Finishes rows row0, row0 + row_step, ... < fa.rows.  Every thread of the
@@ -220,9 +256,9 @@ __device__ void finish_rows(const FinishArgs& fa, FinishSmem& sm, int64_t row0, 
     slot = (int)(step & 1ull);
   }
   for (int64_t b = row0; b < fa.rows; b += row_step) {
-    select_row<L>(fa.lists, fa.nlists, fa.stride, b, fa.k, 0xffffffffu, sm, tid, nthreads);
+    select_row<L>(fa.lists, fa.nlists, fa.stride, fa.pitch, fa.tail, b, fa.k, 0xffffffffu, sm, tid, nthreads);
     if (fa.use_ex)
-      publish_row<L>(fa.ex, sm, slot, step + 1ull, b, tid, nthreads);
+      publish_row<L>(fa.ex, sm, slot, step + 1ull, b, tid);
     else
       write_row<L>(fa, sm, b, tid, nthreads);
     __syncthreads();
@@ -249,8 +285,8 @@ __device__ void finish_rows(const FinishArgs& fa, FinishSmem& sm, int64_t row0, 
         raise_device_error(kErrExchangeTimeout);
     }
     __syncthreads();
-    select_row<L>(ex.recv + (int64_t)slot * ex.world * ex.max_rows * L, ex.world, ex.max_rows, b, fa.k, sm.valid, sm,
-                  tid, nthreads);
+    select_row<L>(ex.recv + (int64_t)slot * ex.world * ex.max_rows * L, ex.world, ex.max_rows, L, 0, b, fa.k, sm.valid,
+                  sm, tid, nthreads);
     write_row<L>(fa, sm, b, tid, nthreads);
     __syncthreads();
   }

@@ -68,17 +68,18 @@ __device__ __forceinline__ uint32_t feature_mask(int64_t f, int64_t F) {
   return n >= 32 ? 0xffffffffu : (n <= 0 ? 0u : ((1u << n) - 1u));
 }
 
-// Writes the top lists of the 32 rows of this warp (warp-cooperative, coalesced).
+// Writes the top lists of the 32 rows of this warp (warp-cooperative,
+// coalesced); row r's list starts at out_unit[r * pitch].
 template <int L>
-__device__ __forceinline__ void store_partials(uint32_t top, uint64_t* __restrict__ out_unit, int warp_row0,
-                                               int lane) {
+__device__ __forceinline__ void store_partials(uint32_t top, uint64_t* __restrict__ out_unit, int pitch,
+                                               int warp_row0, int lane) {
   __syncwarp();
 #pragma unroll 1
   for (int rr = 0; rr < 32; ++rr) {
     const int r = warp_row0 + rr;
 #pragma unroll
     for (int e = 0; e < L / 32; ++e)
-      out_unit[(int64_t)r * L + e * 32 + lane] = top_slot(top, e * 32 + lane, r);
+      out_unit[(int64_t)r * pitch + e * 32 + lane] = top_slot(top, e * 32 + lane, r);
   }
   __syncwarp();
 }
@@ -555,8 +556,12 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
         acc.offer(vals, p.index_offset + (uint32_t)f, valid);
       }
       if (cur.last_of_unit()) {
-        acc.finish();
-        store_partials<L>(top_s, p.partials + (int64_t)cur.u * kRows * L, q * 32, lane);
+        uint64_t* out_unit = p.partials + (int64_t)cur.u * kRows * p.list_pitch;
+        if (p.list_pitch > L)
+          acc.store_tail(out_unit + (int64_t)r * p.list_pitch + L);  // no final merge: a sorted second run
+        else
+          acc.finish();
+        store_partials<L>(top_s, out_unit, p.list_pitch, q * 32, lane);
         __threadfence();  // the lists are read by other CTAs in the finish step
       }
 #pragma unroll
@@ -689,7 +694,7 @@ __global__ void __launch_bounds__(kSimtThreads, 1) simt_topk_kernel(const T* __r
     }
     if (tid < kRows) {
       acc.finish();
-      store_partials<L>(top_s, p.partials + (int64_t)u * kRows * L, tid & ~31, lane);
+      store_partials<L>(top_s, p.partials + (int64_t)u * kRows * L, L, tid & ~31, lane);
     }
     __syncthreads();
   }
@@ -701,7 +706,7 @@ __global__ void __launch_bounds__(kSimtThreads, 1) simt_topk_kernel(const T* __r
 // that grid has completed and its writes are visible (a no-op otherwise).
 // ---------------------------------------------------------------------------
 template <int L>
-__global__ void __launch_bounds__(kFinishThreads) finish_kernel(const FinishArgs fa) {
+__global__ void __launch_bounds__(kFinishThreads, 2) finish_kernel(const FinishArgs fa) {
   __shared__ FinishSmem sm;
   asm volatile("griddepcontrol.wait;" ::: "memory");
   finish_rows<L>(fa, sm, blockIdx.x, gridDim.x, threadIdx.x, blockDim.x);

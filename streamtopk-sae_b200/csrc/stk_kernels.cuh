@@ -62,9 +62,11 @@ constexpr unsigned kErrFinishBarrier = 4;  // the fused kernel's CTAs did not al
 // (list s of row b at lists[(s * stride + b) * L]), results to V/I and/or
 // keys_out, optionally through the exchange.
 struct FinishArgs {
-  const uint64_t* lists;
-  int nlists;
+  const uint64_t* lists;  // list s of row b at lists[(s * stride + b) * pitch]: L sorted keys, then
+  int nlists;             // `tail` more sorted keys (a second run; 0 or kAppendMax)
   int64_t stride;
+  int pitch;
+  int tail;
   int64_t rows;
   int k;
   float* V;            // (rows, k) or null
@@ -84,6 +86,7 @@ struct FusedParams {
   uint32_t* pilot_count;   // CTAs that finished their sample
   uint32_t* tail_count;    // CTAs whose lists are stored (finish barrier); zeroed by the host
   int finish;              // 1: the kernel finishes the rows itself (fin), after a grid barrier
+  int list_pitch;          // keys per row list in partials: L, or L + kAppendMax with a sorted tail run
   FinishArgs fin;
   int64_t B, F;
   int k;
