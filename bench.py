@@ -465,7 +465,7 @@ def run_b200(args, cfg):
         Vh.copy_(V, non_blocking=True)
         Ih.copy_(I, non_blocking=True)
 
-    overlap = args.e2e_overlap and world == 1
+    overlap = not args.e2e_serial and world == 1
     if overlap:
         # A serving loop: X of step i+1 is uploaded on a copy stream while the
         # kernels of step i run (two device buffers); V/I come back on another.
@@ -656,8 +656,9 @@ def main():
     ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS))
     ap.add_argument("--dtype", default=None, choices=["bf16", "fp16", "fp32"],
                     help="input dtype override (config 2 is a dtype sweep)")
-    ap.add_argument("--e2e-overlap", action="store_true",
-                    help="N=1 e2e: overlap each step's host-to-device copy with the previous step's kernels")
+    ap.add_argument("--e2e-serial", action="store_true",
+                    help="N=1 e2e: serialise each step's copies and kernels on one stream (default: the X upload "
+                         "of step i+1 overlaps the kernels of step i on a copy stream)")
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="omit the timed CPU sample (profiling runs)")
     ap.add_argument("--transport", default="auto", choices=["auto", "p2p", "nccl"],

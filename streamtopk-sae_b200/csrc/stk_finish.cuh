@@ -91,14 +91,32 @@ __device__ void select_row(const uint64_t* __restrict__ lists, int nlists, int64
     sm.cnt = 0;
   }
   uint64_t kth = 0ull;  // largest k-th key of one list among this thread's lists
+  // One list per thread (the common case): its first 4 keys of each run come
+  // with the head in the same memory round trip and are gathered from registers.
+  const bool one_each = use_heads && nlists <= nthreads && nlists > kFinishFewLists;
+  uint64_t first[4] = {0ull, 0ull, 0ull, 0ull}, tfirst[4] = {0ull, 0ull, 0ull, 0ull};
   if (use_heads)
     for (int s = tid; s < nlists; s += nthreads) {
       const uint64_t* ps = lists + ((int64_t)s * stride + b) * pitch;
       const bool on = list_on(list_mask, s);
       uint64_t h = 0ull;
       if (on) {
-        h = (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(ps));
-        if (tail > 0) h = kmax(h, (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(ps + L)));
+        const ulonglong2 u0 = __ldcg(reinterpret_cast<const ulonglong2*>(ps));
+        const ulonglong2 u1 = __ldcg(reinterpret_cast<const ulonglong2*>(ps + 2));
+        first[0] = u0.x;
+        first[1] = u0.y;
+        first[2] = u1.x;
+        first[3] = u1.y;
+        h = first[0];
+        if (tail > 0) {
+          const ulonglong2 t0 = __ldcg(reinterpret_cast<const ulonglong2*>(ps + L));
+          const ulonglong2 t1 = __ldcg(reinterpret_cast<const ulonglong2*>(ps + L + 2));
+          tfirst[0] = t0.x;
+          tfirst[1] = t0.y;
+          tfirst[2] = t1.x;
+          tfirst[3] = t1.y;
+          h = kmax(h, tfirst[0]);
+        }
         if (k <= L) kth = kmax(kth, (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(ps + k - 1)));
       }
       sm.heads[s] = h;
@@ -116,10 +134,7 @@ __device__ void select_row(const uint64_t* __restrict__ lists, int nlists, int64
   }
   __syncthreads();
   const uint64_t tau = sm.tau;
-  auto take4 = [&](const uint64_t* p4) {
-    const ulonglong2 u0 = __ldcg(reinterpret_cast<const ulonglong2*>(p4));
-    const ulonglong2 u1 = __ldcg(reinterpret_cast<const ulonglong2*>(p4 + 2));
-    const uint64_t kk[4] = {u0.x, u0.y, u1.x, u1.y};
+  auto keep4 = [&](const uint64_t (&kk)[4]) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       if (kk[j] >= tau) {
@@ -129,12 +144,28 @@ __device__ void select_row(const uint64_t* __restrict__ lists, int nlists, int64
     }
     return kk[3] >= tau;  // the run may continue past these 4 keys
   };
+  auto take4 = [&](const uint64_t* p4) {
+    const ulonglong2 u0 = __ldcg(reinterpret_cast<const ulonglong2*>(p4));
+    const ulonglong2 u1 = __ldcg(reinterpret_cast<const ulonglong2*>(p4 + 2));
+    const uint64_t kk[4] = {u0.x, u0.y, u1.x, u1.y};
+    return keep4(kk);
+  };
   if (use_heads && nlists <= kFinishFewLists) {
     const int chunks = (L + tail) / 4;
     for (int t = tid; t < nlists * chunks; t += nthreads) {
       const int s = t / chunks, q = (t % chunks) * 4;
       if (sm.heads[s] < tau) continue;
       take4(lists + ((int64_t)s * stride + b) * pitch + q);
+    }
+  } else if (one_each) {
+    if (tid < nlists && sm.heads[tid] >= tau) {
+      const uint64_t* ps = lists + ((int64_t)tid * stride + b) * pitch;
+      if (keep4(first))
+        for (int q = 4; q < L; q += 4)
+          if (!take4(ps + q)) break;  // sorted: the rest is smaller
+      if (tail > 0 && keep4(tfirst))
+        for (int q = 4; q < tail; q += 4)
+          if (!take4(ps + L + q)) break;
     }
   } else if (use_heads) {
     for (int s = tid; s < nlists; s += nthreads) {

@@ -84,8 +84,17 @@ __device__ __forceinline__ void store_partials(uint32_t top, uint64_t* __restric
   __syncwarp();
 }
 
+// Width of the tile starting at ft in the unit range [fb, fe).  (A schedule
+// that ended long units with a narrow tile, to shorten the exposed epilogue of
+// the last tile, measured slower at cfg3: its extra tile re-reads all of X.)
+template <int NT>
+__device__ __forceinline__ int tile_width(int64_t ft, int64_t fb, int64_t fe) {
+  (void)fb;
+  return (int)min((int64_t)NT, fe - ft);
+}
+
 // Walks the tiles of this CTA: units u = blockIdx.x, +gridDim.x, ...; tiles
-// of NT features within each unit's range.
+// of tile_width<NT> features within each unit's range.
 template <int NT>
 struct TileWalk {
   int u, m;
@@ -99,10 +108,10 @@ struct TileWalk {
   }
   __device__ __forceinline__ bool valid(const UnitGrid& g) const { return u < g.units; }
   __device__ __forceinline__ bool first_of_unit() const { return ft == fb; }
-  __device__ __forceinline__ bool last_of_unit() const { return ft + NT >= fe; }
-  __device__ __forceinline__ int width() const { return (int)min((int64_t)NT, fe - ft); }
+  __device__ __forceinline__ int width() const { return tile_width<NT>(ft, fb, fe); }
+  __device__ __forceinline__ bool last_of_unit() const { return ft + width() >= fe; }
   __device__ __forceinline__ void next(const UnitGrid& g) {
-    ft += NT;
+    ft += width();
     if (ft >= fe) {
       u += gridDim.x;
       if (u < g.units) {
@@ -300,8 +309,8 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
         int m;
         int64_t fb, fe;
         unit_range(g, u, m, fb, fe);
-        for (int64_t ft = fb; ft < fe && ok; ft += NT) {
-          const int w = (int)min((int64_t)NT, fe - ft);
+        for (int64_t ft = fb, w = 0; ft < fe && ok; ft += w) {
+          w = tile_width<NT>(ft, fb, fe);
           const uint32_t bytes = Cfg::kXBytes + (uint32_t)w * kWRowBytes;
           for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
             const int s = it % STAGES;
@@ -345,8 +354,8 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
         int m;
         int64_t fb, fe;
         unit_range(g, u, m, fb, fe);
-        for (int64_t ft = fb; ft < fe && ok; ft += NT, ++tile) {
-          const int w = (int)min((int64_t)NT, fe - ft);
+        for (int64_t ft = fb, w = 0; ft < fe && ok; ft += w, ++tile) {
+          w = tile_width<NT>(ft, fb, fe);
           const int a = tile & 1;
           if (!mbar_wait(&acc_empty[a], ((tile >> 1) & 1) ^ 1, abort_flag)) {
             ok = false;
@@ -412,7 +421,8 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
       int m;
       int64_t fb, fe;
       unit_range(g, u, m, fb, fe);
-      for (int64_t ft = fb; ft < fe && ok; ft += NT) {
+      for (int64_t ft = fb, w = 0; ft < fe && ok; ft += w) {
+        w = tile_width<NT>(ft, fb, fe);
         for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
           const int s = it % STAGES;
           const bool got = mbar_wait(&full[s], (it / STAGES) & 1, abort_flag);
