@@ -264,17 +264,19 @@ int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t 
   return STK_OK;
 }
 
-// Optional override of the fused tile configuration, "L,NT,STAGES,A,APP_SMEM",
-// for tuning.
-bool fused_override(int L, int* nt, int* stages, int* app, int* app_smem) {
+// Optional override of the fused tile configuration,
+// "L,NT,STAGES,A,APP_SMEM[,TOPT]", for tuning.
+bool fused_override(int L, int* nt, int* stages, int* app, int* app_smem, int* topt) {
   const char* s = std::getenv("STK_FUSED_CFG");
   if (!s) return false;
-  int l = 0, n = 0, st = 0, a = 0, sm = 0;
-  if (std::sscanf(s, "%d,%d,%d,%d,%d", &l, &n, &st, &a, &sm) != 5 || l != L) return false;
+  int l = 0, n = 0, st = 0, a = 0, sm = 0, tt = 0;
+  const int got = std::sscanf(s, "%d,%d,%d,%d,%d,%d", &l, &n, &st, &a, &sm, &tt);
+  if (got < 5 || l != L) return false;
   *nt = n;
   *stages = st;
   *app = a;
   *app_smem = sm;
+  *topt = got == 6 ? tt : 0;
   return true;
 }
 
@@ -296,7 +298,17 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   int stages = nt128 ? (pl.L == 128 ? 3 : pl.L == 64 ? 4 : 5) : (pl.L == 128 ? 2 : 3);
   int nslots = pl.L == 64 ? 16 : 32;
   int app_smem = pl.L == 128 ? 0 : 1;
-  fused_override(pl.L, &nt, &stages, &nslots, &app_smem);
+  int topt = 0;
+  if (pl.L == 128 && !pl.tf32) {
+    // k > 64: the per-row top-128 lists (128 KB) go to tensor memory beside
+    // 128-column accumulators, and the shared memory holds a six-stage TMA
+    // ring (two stages fit beside the lists in shared memory).
+    nt = 128;
+    stages = 6;
+    app_smem = 1;
+    topt = 1;
+  }
+  fused_override(pl.L, &nt, &stages, &nslots, &app_smem, &topt);
   CUtensorMap tx, txl, tw, tw32;
   const bool bf16 = dtype == STK_BF16;
   int rc = STK_OK;
@@ -359,14 +371,16 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   }
   cudaError_t e = cudaErrorInvalidValue;
   ProfScope prof(kProfFused, stream);
-#define STK_TRY_FUSED(Lc, NTc, Sc, Ac, SMc)                                                           \
-  if (!pl.tf32 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc)    \
-    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, false>(tx, txl, tw, tw32, p, pl.ctas, stream);
+#define STK_TRY_FUSED(Lc, NTc, Sc, Ac, SMc, TTc)                                                      \
+  if (!pl.tf32 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc &&  \
+      (topt != 0) == TTc)                                                                               \
+    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, TTc, false>(tx, txl, tw, tw32, p, pl.ctas, stream);
   STK_FUSED_CONFIGS(STK_TRY_FUSED)
 #undef STK_TRY_FUSED
-#define STK_TRY_FUSED_TF32(Lc, NTc, Sc, Ac, SMc)                                                      \
-  if (pl.tf32 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc)     \
-    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, true>(tx, txl, tw, tw32, p, pl.ctas, stream);
+#define STK_TRY_FUSED_TF32(Lc, NTc, Sc, Ac, SMc, TTc)                                                 \
+  if (pl.tf32 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc &&   \
+      (topt != 0) == TTc)                                                                               \
+    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, TTc, true>(tx, txl, tw, tw32, p, pl.ctas, stream);
   STK_FUSED_TF32_CONFIGS(STK_TRY_FUSED_TF32)
 #undef STK_TRY_FUSED_TF32
   if (e != cudaSuccess) return cuda_fail(e, "fused_topk_kernel launch");

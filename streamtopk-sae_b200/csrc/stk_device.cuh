@@ -73,308 +73,6 @@ __device__ __forceinline__ void cx(uint64_t& a, uint64_t& b) {
 }
 
 // ---------------------------------------------------------------------------
-// Per-thread networks (N is a compile-time power of two; fully unrolled so the
-// arrays stay in registers).
-// ---------------------------------------------------------------------------
-template <int N>
-__device__ __forceinline__ void sort_desc(uint64_t (&a)[N]) {
-#pragma unroll
-  for (int size = 2; size <= N; size <<= 1) {
-#pragma unroll
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-#pragma unroll
-      for (int i = 0; i < N; ++i) {
-        const int j = i ^ stride;
-        if (j > i) {
-          if ((i & size) == 0)
-            cx(a[i], a[j]);  // descending block
-          else
-            cx(a[j], a[i]);  // ascending block
-        }
-      }
-    }
-  }
-}
-
-// Turns a bitonic sequence into a descending one.
-template <int N>
-__device__ __forceinline__ void merge_desc(uint64_t (&a)[N]) {
-#pragma unroll
-  for (int stride = N >> 1; stride > 0; stride >>= 1) {
-#pragma unroll
-    for (int i = 0; i < N; ++i) {
-      const int j = i ^ stride;
-      if (j > i) cx(a[i], a[j]);
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Per-row top-L accumulator, one thread per batch row.
-//
-// Layout (slot-major, row-minor, so the 32 threads of a warp touch 32
-// consecutive 8-byte words):
-//   top[s * kRows + (r ^ (s & 31))], s < L : row r's best L keys, descending
-//                               (0 = empty), shared memory.  The XOR swizzle
-//                               keeps per-thread access conflict-free and lets
-//                               a warp read one row's 32 consecutive slots in
-//                               2 wavefronts instead of 32 (store_partials).
-//   app[s * kRows + r], s < A : row r's unsorted survivors since the last
-//                               merge, in shared memory or (when shared
-//                               memory is short) in an L2-resident workspace
-//                               slice of this CTA, written and read back by
-//                               the same thread only
-// ---------------------------------------------------------------------------
-// Dynamic shared memory of every kernel in this library.  Per-row lists are
-// addressed by byte offset from this symbol so that code outside the kernel
-// body still compiles to shared-memory instructions.
-extern __shared__ __align__(16) uint8_t stk_smem[];
-
-__device__ __forceinline__ uint64_t* smem_keys(uint32_t off) { return reinterpret_cast<uint64_t*>(stk_smem + off); }
-
-// Slot s of row r in a swizzled top list at byte offset `top`.
-__device__ __forceinline__ uint64_t& top_slot(uint32_t top, int s, int r) {
-  return smem_keys(top)[s * kRows + (r ^ (s & 31))];
-}
-
-// Merge row r's n waiting survivors (A append slots, unsorted) into its sorted
-// top list and return the new threshold: the value of the (kth+1)-th best key,
-// never below floor_thr (a lower bound known from elsewhere, -inf if none).
-// The append slots are in shared memory (APP_SMEM, app_off = byte offset from
-// stk_smem) or in global memory (app_g).  Kept out of line: it runs rarely and
-// is large.
-template <int L, int A, bool APP_SMEM>
-__device__ __noinline__ float merge_survivors(uint32_t top_off, uint32_t app_off, const uint64_t* __restrict__ app_g,
-                                              int r, int n, int kth, float floor_thr) {
-  static_assert(A == 16 || A == 32, "append slots");
-#define TOP(s) top_slot(top_off, (s), r)
-  uint64_t a[A];
-#pragma unroll
-  for (int s = 0; s < A; ++s) {
-    if constexpr (APP_SMEM)
-      a[s] = (s < n) ? smem_keys(app_off)[s * kRows + r] : kEmptyKey;
-    else
-      a[s] = (s < n) ? (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(app_g + s * kRows + r))
-                     : kEmptyKey;
-  }
-  sort_desc<A>(a);
-  if constexpr (L == 32) {
-    // top-32 of two sorted lists: c[i] = max(top[i], a'[31 - i]) is bitonic
-    // (a' = a padded with empty keys; only the last A positions change).
-    uint64_t c[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) c[i] = TOP(i);
-#pragma unroll
-    for (int q = 0; q < A; ++q) c[32 - A + q] = kmax(c[32 - A + q], a[A - 1 - q]);
-    merge_desc<32>(c);
-#pragma unroll
-    for (int i = 0; i < 32; ++i) TOP(i) = c[i];
-  } else {
-    // Only the last A positions can change in c[i] = max(top[i], a'[L-1-i]).
-#pragma unroll
-    for (int q = 0; q < A; ++q) TOP(L - A + q) = kmax(TOP(L - A + q), a[A - 1 - q]);
-    // Bitonic merge: strides >= 32 in shared memory, then 32-blocks in registers.
-#pragma unroll
-    for (int stride = L >> 1; stride >= 32; stride >>= 1) {
-#pragma unroll 16
-      for (int i = 0; i < L; ++i) {
-        if ((i & stride) == 0) {
-          uint64_t x = TOP(i), y = TOP(i + stride);
-          cx(x, y);
-          TOP(i) = x;
-          TOP(i + stride) = y;
-        }
-      }
-    }
-#pragma unroll 1
-    for (int blk = 0; blk < L / 32; ++blk) {
-      uint64_t c[32];
-#pragma unroll
-      for (int q = 0; q < 32; ++q) c[q] = TOP(blk * 32 + q);
-      merge_desc<32>(c);
-#pragma unroll
-      for (int q = 0; q < 32; ++q) TOP(blk * 32 + q) = c[q];
-    }
-  }
-  const uint64_t kk = TOP(kth);
-#undef TOP
-  return kk ? fmaxf(key_value(kk), floor_thr) : floor_thr;
-}
-
-// vals[j & 31] for a per-lane (divergent) j, by a 5-level select tree.
-__device__ __forceinline__ float pick32(const float (&vals)[32], int j) {
-  float t16[16], t8[8], t4[4], t2[2];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) t16[i] = (j & 16) ? vals[i + 16] : vals[i];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) t8[i] = (j & 8) ? t16[i + 8] : t16[i];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) t4[i] = (j & 4) ? t8[i + 4] : t8[i];
-#pragma unroll
-  for (int i = 0; i < 2; ++i) t2[i] = (j & 2) ? t4[i + 2] : t4[i];
-  return (j & 1) ? t2[1] : t2[0];
-}
-
-// The n (<= A) unsorted append slots of row r, sorted descending and padded
-// with empty keys to kAppendMax keys, stored at dst (16-byte aligned).  Out of
-// line like merge_survivors: it runs once per unit.
-template <int A, bool APP_SMEM>
-__device__ __noinline__ void store_sorted_tail(uint32_t app_off, const uint64_t* __restrict__ app_g, int r, int n,
-                                               uint64_t* __restrict__ dst) {
-  ulonglong2* d = reinterpret_cast<ulonglong2*>(dst);
-  if (n > 0) {
-    uint64_t a[A];
-#pragma unroll
-    for (int s = 0; s < A; ++s) {
-      if constexpr (APP_SMEM)
-        a[s] = (s < n) ? smem_keys(app_off)[s * kRows + r] : kEmptyKey;
-      else
-        a[s] = (s < n) ? (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(app_g + s * kRows + r))
-                       : kEmptyKey;
-    }
-    sort_desc<A>(a);
-#pragma unroll
-    for (int i = 0; i < A / 2; ++i) d[i] = make_ulonglong2(a[2 * i], a[2 * i + 1]);
-  } else {
-#pragma unroll
-    for (int i = 0; i < A / 2; ++i) d[i] = make_ulonglong2(0ull, 0ull);
-  }
-#pragma unroll
-  for (int i = A / 2; i < kAppendMax / 2; ++i) d[i] = make_ulonglong2(0ull, 0ull);
-}
-
-template <int L, int A, bool APP_SMEM>
-struct RowTopK {
-  uint32_t top;     // byte offset of top[0] from stk_smem
-  uint32_t app_s;   // byte offset of the shared append slots (APP_SMEM)
-  uint64_t* app_g;  // global append slots (!APP_SMEM)
-  int r;            // row within the M tile
-  int cnt;          // survivors waiting in the append slots
-  float thr;        // value of the k-th best key so far (-inf until k are held)
-  float floor_thr;  // known lower bound of the row's k-th score (-inf if none)
-  int kth;          // k - 1
-
-  __device__ __forceinline__ void init(uint32_t top_, uint32_t app_s_, uint64_t* app_g_, int row, int k) {
-    top = top_;
-    app_s = app_s_;
-    app_g = app_g_;
-    r = row;
-    cnt = 0;
-    thr = -__int_as_float(0x7f800000);
-    floor_thr = thr;
-    kth = k - 1;
-#pragma unroll 4
-    for (int s = 0; s < L; ++s) top_slot(top, s, r) = kEmptyKey;
-  }
-
-  __device__ __forceinline__ void flush() {
-    thr = merge_survivors<L, A, APP_SMEM>(top, app_s, app_g, r, cnt, kth, floor_thr);
-    cnt = 0;
-  }
-
-  __device__ __forceinline__ void push(uint64_t key) {
-    if constexpr (APP_SMEM)
-      smem_keys(app_s)[cnt * kRows + r] = key;
-    else
-      __stcg(reinterpret_cast<unsigned long long*>(app_g + cnt * kRows + r), (unsigned long long)key);
-    ++cnt;
-  }
-
-  // Offer one chunk of 32 scores (vals[j] is feature f0 + j).  valid_mask
-  // marks real features (tail of F, rows beyond B).  All 32 lanes of the warp
-  // must call this together: a merge runs for every lane as soon as one lane
-  // would overflow its append slots.  A chunk may bring more survivors than
-  // A, so the chunk is taken in (at most 32 / A) passes of A candidates.
-  // Survivors are rare once a threshold is known, so the warp loops once per
-  // survivor of its busiest lane; each lane takes its lowest pending survivor
-  // (value picked from registers by a select tree, no divergent branches).
-  __device__ __forceinline__ void offer(const float (&vals)[32], uint32_t f0, uint32_t valid_mask) {
-    uint32_t mask = 0;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) mask |= (vals[j] > thr) ? (1u << j) : 0u;
-    mask &= valid_mask;
-#pragma unroll
-    for (int part = 0; part < 32 / A; ++part) {
-      const uint32_t pm = A == 32 ? 0xffffffffu : (0xffffu << (16 * part));
-      if (__any_sync(0xffffffffu, cnt + __popc(mask & pm) > A)) {
-        flush();
-        mask = 0;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) mask |= (vals[j] > thr) ? (1u << j) : 0u;
-        mask &= valid_mask;
-      }
-      uint32_t m = mask & pm;
-      while (__any_sync(0xffffffffu, m != 0u)) {
-        const bool has = m != 0u;
-        const int j = __ffs(m) - 1;  // -1 (ignored) when this lane has none
-        m &= m - 1u;
-        const float v = pick32(vals, j);
-        if (has) push(make_key(v, f0 + uint32_t(j)));
-      }
-    }
-  }
-
-  // Raise the filter to a lower bound of the row's k-th score obtained from a
-  // sample (scores strictly below `lb` can never be in the row's top-k).
-  __device__ __forceinline__ void set_floor(float lb) {
-    const float t = nextafterf(lb, -__int_as_float(0x7f800000));  // keep scores == lb
-    floor_thr = fmaxf(floor_thr, t);
-    thr = fmaxf(thr, floor_thr);
-  }
-
-  __device__ __forceinline__ void finish() {
-    if (__any_sync(0xffffffffu, cnt > 0)) flush();
-  }
-
-  // Instead of a final flush: writes the pending survivors, sorted descending
-  // and padded with empty keys to kAppendMax, at dst (16-byte aligned) -- a
-  // second sorted run beside the row's list, which the finish step reads too.
-  __device__ __forceinline__ void store_tail(uint64_t* dst) {
-    store_sorted_tail<A, APP_SMEM>(app_s, app_g, r, cnt, dst);
-    cnt = 0;
-  }
-};
-
-// ---------------------------------------------------------------------------
-// Warp-cooperative lists: element i = e * 32 + lane, E = L / 32 per lane.
-// ---------------------------------------------------------------------------
-template <int E>
-__device__ __forceinline__ void warp_merge_desc(uint64_t (&a)[E], int lane) {
-#pragma unroll
-  for (int stride = E * 16; stride > 0; stride >>= 1) {
-    if (stride >= 32) {
-      const int s = stride >> 5;
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-        if ((e & s) == 0) {
-          const uint64_t x = a[e], y = a[e | s];
-          a[e] = kmax(x, y);
-          a[e | s] = kmin(x, y);
-        }
-      }
-    } else {
-      const bool lower = (lane & stride) == 0;
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const uint64_t y = __shfl_xor_sync(0xffffffffu, a[e], stride);
-        a[e] = lower ? kmax(a[e], y) : kmin(a[e], y);
-      }
-    }
-  }
-}
-
-// t <- best L of (t u u), both descending lists of L = 32 * E keys.
-template <int E>
-__device__ __forceinline__ void warp_merge_lists(uint64_t (&t)[E], const uint64_t (&u)[E], int lane) {
-#pragma unroll
-  for (int e = 0; e < E; ++e) {
-    const uint64_t y = __shfl_sync(0xffffffffu, u[E - 1 - e], 31 - lane);
-    t[e] = kmax(t[e], y);
-  }
-  warp_merge_desc<E>(t, lane);
-}
-
-// ---------------------------------------------------------------------------
 // PTX wrappers.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -552,6 +250,29 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&v)[32]) {
       : "memory");
 }
 
+// Thread t of the warp stores v[j] to lane (base lane + t), column col + j,
+// j < 32 (the store counterpart of tmem_ld32).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32"
+      " [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16,"
+      " %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+      "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+      "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Two consecutive 32-bit columns of this thread's lane (one 64-bit key).
+__device__ __forceinline__ uint64_t tmem_ld_key(uint32_t taddr) {
+  uint32_t lo, hi;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];" : "=r"(lo), "=r"(hi) : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(lo), "+r"(hi)::"memory");
+  return (uint64_t(hi) << 32) | lo;
+}
+
 // Shared-memory matrix descriptor for a K-major tile written by TMA with
 // 128-byte swizzle: rows of 128 B, 8-row atoms of 1024 B (stride byte offset),
 // version 1 (sm_100), layout type 2 (SWIZZLE_128B).  The tile base must be
@@ -586,5 +307,411 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(uint32_t ab_format, uint32
 
 // Instruction descriptor, kind::tf32 (A and B format 2), fp32 accumulate, K-major.
 __host__ __device__ constexpr uint32_t make_idesc_tf32(uint32_t m, uint32_t n) { return make_idesc_f16(2u, m, n); }
+
+// ---------------------------------------------------------------------------
+// Per-thread networks (N is a compile-time power of two; fully unrolled so the
+// arrays stay in registers).
+// ---------------------------------------------------------------------------
+template <int N>
+__device__ __forceinline__ void sort_desc(uint64_t (&a)[N]) {
+#pragma unroll
+  for (int size = 2; size <= N; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const int j = i ^ stride;
+        if (j > i) {
+          if ((i & size) == 0)
+            cx(a[i], a[j]);  // descending block
+          else
+            cx(a[j], a[i]);  // ascending block
+        }
+      }
+    }
+  }
+}
+
+// Turns a bitonic sequence into a descending one.
+template <int N>
+__device__ __forceinline__ void merge_desc(uint64_t (&a)[N]) {
+#pragma unroll
+  for (int stride = N >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      const int j = i ^ stride;
+      if (j > i) cx(a[i], a[j]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Per-row top-L accumulator, one thread per batch row.
+//
+// Layout (slot-major, row-minor, so the 32 threads of a warp touch 32
+// consecutive 8-byte words):
+//   top[s * kRows + (r ^ (s & 31))], s < L : row r's best L keys, descending
+//                               (0 = empty), shared memory.  The XOR swizzle
+//                               keeps per-thread access conflict-free and lets
+//                               a warp read one row's 32 consecutive slots in
+//                               2 wavefronts instead of 32 (store_partials).
+//   app[s * kRows + r], s < A : row r's unsorted survivors since the last
+//                               merge, in shared memory or (when shared
+//                               memory is short) in an L2-resident workspace
+//                               slice of this CTA, written and read back by
+//                               the same thread only
+// ---------------------------------------------------------------------------
+// Dynamic shared memory of every kernel in this library.  Per-row lists are
+// addressed by byte offset from this symbol so that code outside the kernel
+// body still compiles to shared-memory instructions.
+extern __shared__ __align__(16) uint8_t stk_smem[];
+
+__device__ __forceinline__ uint64_t* smem_keys(uint32_t off) { return reinterpret_cast<uint64_t*>(stk_smem + off); }
+
+// Slot s of row r in a swizzled top list at byte offset `top`.
+__device__ __forceinline__ uint64_t& top_slot(uint32_t top, int s, int r) {
+  return smem_keys(top)[s * kRows + (r ^ (s & 31))];
+}
+
+// Merge row r's n waiting survivors (A append slots, unsorted) into its sorted
+// top list and return the new threshold: the value of the (kth+1)-th best key,
+// never below floor_thr (a lower bound known from elsewhere, -inf if none).
+// The append slots are in shared memory (APP_SMEM, app_off = byte offset from
+// stk_smem) or in global memory (app_g).  Kept out of line: it runs rarely and
+// is large.
+template <int L, int A, bool APP_SMEM>
+__device__ __noinline__ float merge_survivors(uint32_t top_off, uint32_t app_off, const uint64_t* __restrict__ app_g,
+                                              int r, int n, int kth, float floor_thr) {
+  static_assert(A == 16 || A == 32, "append slots");
+#define TOP(s) top_slot(top_off, (s), r)
+  uint64_t a[A];
+#pragma unroll
+  for (int s = 0; s < A; ++s) {
+    if constexpr (APP_SMEM)
+      a[s] = (s < n) ? smem_keys(app_off)[s * kRows + r] : kEmptyKey;
+    else
+      a[s] = (s < n) ? (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(app_g + s * kRows + r))
+                     : kEmptyKey;
+  }
+  sort_desc<A>(a);
+  if constexpr (L == 32) {
+    // top-32 of two sorted lists: c[i] = max(top[i], a'[31 - i]) is bitonic
+    // (a' = a padded with empty keys; only the last A positions change).
+    uint64_t c[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) c[i] = TOP(i);
+#pragma unroll
+    for (int q = 0; q < A; ++q) c[32 - A + q] = kmax(c[32 - A + q], a[A - 1 - q]);
+    merge_desc<32>(c);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) TOP(i) = c[i];
+  } else {
+    // Only the last A positions can change in c[i] = max(top[i], a'[L-1-i]).
+#pragma unroll
+    for (int q = 0; q < A; ++q) TOP(L - A + q) = kmax(TOP(L - A + q), a[A - 1 - q]);
+    // Bitonic merge: strides >= 32 in shared memory, then 32-blocks in registers.
+#pragma unroll
+    for (int stride = L >> 1; stride >= 32; stride >>= 1) {
+#pragma unroll 16
+      for (int i = 0; i < L; ++i) {
+        if ((i & stride) == 0) {
+          uint64_t x = TOP(i), y = TOP(i + stride);
+          cx(x, y);
+          TOP(i) = x;
+          TOP(i + stride) = y;
+        }
+      }
+    }
+#pragma unroll 1
+    for (int blk = 0; blk < L / 32; ++blk) {
+      uint64_t c[32];
+#pragma unroll
+      for (int q = 0; q < 32; ++q) c[q] = TOP(blk * 32 + q);
+      merge_desc<32>(c);
+#pragma unroll
+      for (int q = 0; q < 32; ++q) TOP(blk * 32 + q) = c[q];
+    }
+  }
+  const uint64_t kk = TOP(kth);
+#undef TOP
+  return kk ? fmaxf(key_value(kk), floor_thr) : floor_thr;
+}
+
+// Key i of a list held in tensor memory occupies 32-bit columns 2i (low half)
+// and 2i + 1 (high half) of the owning thread's lane.
+__device__ __forceinline__ uint64_t col_key(const uint32_t (&v)[32], int j) {
+  return (uint64_t(v[2 * j + 1]) << 32) | v[2 * j];
+}
+__device__ __forceinline__ void set_col_key(uint32_t (&v)[32], int j, uint64_t key) {
+  v[2 * j] = uint32_t(key);
+  v[2 * j + 1] = uint32_t(key >> 32);
+}
+
+// merge_survivors for a top list in tensor memory (tlist: the TMEM address of
+// key 0 of this thread's row; L keys at columns [0, 2L)).  Same steps and
+// result: the A sorted survivors enter through the last A positions, then a
+// bitonic merge -- strides >= 32 on pairs of 16-key groups, then 32-key blocks
+// in registers.  Every lane of the warp calls it together (warp-wide TMEM
+// loads and stores).
+template <int L, int A, bool APP_SMEM>
+__device__ __noinline__ float merge_survivors_tmem(uint32_t tlist, uint32_t app_off,
+                                                   const uint64_t* __restrict__ app_g, int r, int n, int kth,
+                                                   float floor_thr) {
+  static_assert(A == 16 || A == 32, "append slots");
+  static_assert(L >= 64 && L % 32 == 0, "list length");
+  uint64_t a[A];
+#pragma unroll
+  for (int s = 0; s < A; ++s) {
+    if constexpr (APP_SMEM)
+      a[s] = (s < n) ? smem_keys(app_off)[s * kRows + r] : kEmptyKey;
+    else
+      a[s] = (s < n) ? (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(app_g + s * kRows + r))
+                     : kEmptyKey;
+  }
+  sort_desc<A>(a);
+#pragma unroll
+  for (int h = 0; h < A / 16; ++h) {
+    uint32_t v[32];
+    const int i0 = L - A + 16 * h;
+    tmem_ld32(tlist + 2 * i0, v);
+    tmem_wait_ld(v);
+#pragma unroll
+    for (int q = 0; q < 16; ++q) set_col_key(v, q, kmax(col_key(v, q), a[A - 1 - (16 * h + q)]));
+    tmem_st32(tlist + 2 * i0, v);
+  }
+  tmem_wait_st();
+#pragma unroll 1
+  for (int stride = L >> 1; stride >= 32; stride >>= 1) {
+#pragma unroll 1
+    for (int i0 = 0; i0 < L; i0 += 16) {
+      if (i0 & stride) continue;
+      uint32_t p[32], q[32];
+      tmem_ld32(tlist + 2 * i0, p);
+      tmem_ld32(tlist + 2 * (i0 + stride), q);
+      tmem_wait_ld(p);
+      tmem_wait_ld(q);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        uint64_t x = col_key(p, j), y = col_key(q, j);
+        cx(x, y);
+        set_col_key(p, j, x);
+        set_col_key(q, j, y);
+      }
+      tmem_st32(tlist + 2 * i0, p);
+      tmem_st32(tlist + 2 * (i0 + stride), q);
+    }
+    tmem_wait_st();
+  }
+#pragma unroll 1
+  for (int blk = 0; blk < L / 32; ++blk) {
+    uint32_t p[32], q[32];
+    tmem_ld32(tlist + 64 * blk, p);
+    tmem_ld32(tlist + 64 * blk + 32, q);
+    tmem_wait_ld(p);
+    tmem_wait_ld(q);
+    uint64_t c[32];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      c[j] = col_key(p, j);
+      c[16 + j] = col_key(q, j);
+    }
+    merge_desc<32>(c);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      set_col_key(p, j, c[j]);
+      set_col_key(q, j, c[16 + j]);
+    }
+    tmem_st32(tlist + 64 * blk, p);
+    tmem_st32(tlist + 64 * blk + 32, q);
+  }
+  tmem_wait_st();
+  const uint64_t kk = tmem_ld_key(tlist + 2 * kth);
+  return kk ? fmaxf(key_value(kk), floor_thr) : floor_thr;
+}
+
+// vals[j & 31] for a per-lane (divergent) j, by a 5-level select tree.
+__device__ __forceinline__ float pick32(const float (&vals)[32], int j) {
+  float t16[16], t8[8], t4[4], t2[2];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) t16[i] = (j & 16) ? vals[i + 16] : vals[i];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) t8[i] = (j & 8) ? t16[i + 8] : t16[i];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) t4[i] = (j & 4) ? t8[i + 4] : t8[i];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) t2[i] = (j & 2) ? t4[i + 2] : t4[i];
+  return (j & 1) ? t2[1] : t2[0];
+}
+
+// The n (<= A) unsorted append slots of row r, sorted descending and padded
+// with empty keys to kAppendMax keys, stored at dst (16-byte aligned).  Out of
+// line like merge_survivors: it runs once per unit.
+template <int A, bool APP_SMEM>
+__device__ __noinline__ void store_sorted_tail(uint32_t app_off, const uint64_t* __restrict__ app_g, int r, int n,
+                                               uint64_t* __restrict__ dst) {
+  ulonglong2* d = reinterpret_cast<ulonglong2*>(dst);
+  if (n > 0) {
+    uint64_t a[A];
+#pragma unroll
+    for (int s = 0; s < A; ++s) {
+      if constexpr (APP_SMEM)
+        a[s] = (s < n) ? smem_keys(app_off)[s * kRows + r] : kEmptyKey;
+      else
+        a[s] = (s < n) ? (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(app_g + s * kRows + r))
+                       : kEmptyKey;
+    }
+    sort_desc<A>(a);
+#pragma unroll
+    for (int i = 0; i < A / 2; ++i) d[i] = make_ulonglong2(a[2 * i], a[2 * i + 1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < A / 2; ++i) d[i] = make_ulonglong2(0ull, 0ull);
+  }
+#pragma unroll
+  for (int i = A / 2; i < kAppendMax / 2; ++i) d[i] = make_ulonglong2(0ull, 0ull);
+}
+
+template <int L, int A, bool APP_SMEM, bool TOPT = false>
+struct RowTopK {
+  uint32_t top;     // byte offset of top[0] from stk_smem, or (TOPT) the TMEM address of this row's list
+  uint32_t app_s;   // byte offset of the shared append slots (APP_SMEM)
+  uint64_t* app_g;  // global append slots (!APP_SMEM)
+  int r;            // row within the M tile
+  int cnt;          // survivors waiting in the append slots
+  float thr;        // value of the k-th best key so far (-inf until k are held)
+  float floor_thr;  // known lower bound of the row's k-th score (-inf if none)
+  int kth;          // k - 1
+
+  __device__ __forceinline__ void init(uint32_t top_, uint32_t app_s_, uint64_t* app_g_, int row, int k) {
+    top = top_;
+    app_s = app_s_;
+    app_g = app_g_;
+    r = row;
+    cnt = 0;
+    thr = -__int_as_float(0x7f800000);
+    floor_thr = thr;
+    kth = k - 1;
+    if constexpr (TOPT) {
+      uint32_t z[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) z[j] = 0u;
+#pragma unroll
+      for (int c = 0; c < 2 * L; c += 32) tmem_st32(top + c, z);
+      tmem_wait_st();
+    } else {
+#pragma unroll 4
+      for (int s = 0; s < L; ++s) top_slot(top, s, r) = kEmptyKey;
+    }
+  }
+
+  __device__ __forceinline__ void flush() {
+    if constexpr (TOPT)
+      thr = merge_survivors_tmem<L, A, APP_SMEM>(top, app_s, app_g, r, cnt, kth, floor_thr);
+    else
+      thr = merge_survivors<L, A, APP_SMEM>(top, app_s, app_g, r, cnt, kth, floor_thr);
+    cnt = 0;
+  }
+
+  __device__ __forceinline__ void push(uint64_t key) {
+    if constexpr (APP_SMEM)
+      smem_keys(app_s)[cnt * kRows + r] = key;
+    else
+      __stcg(reinterpret_cast<unsigned long long*>(app_g + cnt * kRows + r), (unsigned long long)key);
+    ++cnt;
+  }
+
+  // Offer one chunk of 32 scores (vals[j] is feature f0 + j).  valid_mask
+  // marks real features (tail of F, rows beyond B).  All 32 lanes of the warp
+  // must call this together: a merge runs for every lane as soon as one lane
+  // would overflow its append slots.  A chunk may bring more survivors than
+  // A, so the chunk is taken in (at most 32 / A) passes of A candidates.
+  // Survivors are rare once a threshold is known, so the warp loops once per
+  // survivor of its busiest lane; each lane takes its lowest pending survivor
+  // (value picked from registers by a select tree, no divergent branches).
+  __device__ __forceinline__ void offer(const float (&vals)[32], uint32_t f0, uint32_t valid_mask) {
+    uint32_t mask = 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) mask |= (vals[j] > thr) ? (1u << j) : 0u;
+    mask &= valid_mask;
+#pragma unroll
+    for (int part = 0; part < 32 / A; ++part) {
+      const uint32_t pm = A == 32 ? 0xffffffffu : (0xffffu << (16 * part));
+      if (__any_sync(0xffffffffu, cnt + __popc(mask & pm) > A)) {
+        flush();
+        mask = 0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) mask |= (vals[j] > thr) ? (1u << j) : 0u;
+        mask &= valid_mask;
+      }
+      uint32_t m = mask & pm;
+      while (__any_sync(0xffffffffu, m != 0u)) {
+        const bool has = m != 0u;
+        const int j = __ffs(m) - 1;  // -1 (ignored) when this lane has none
+        m &= m - 1u;
+        const float v = pick32(vals, j);
+        if (has) push(make_key(v, f0 + uint32_t(j)));
+      }
+    }
+  }
+
+  // Raise the filter to a lower bound of the row's k-th score obtained from a
+  // sample (scores strictly below `lb` can never be in the row's top-k).
+  __device__ __forceinline__ void set_floor(float lb) {
+    const float t = nextafterf(lb, -__int_as_float(0x7f800000));  // keep scores == lb
+    floor_thr = fmaxf(floor_thr, t);
+    thr = fmaxf(thr, floor_thr);
+  }
+
+  __device__ __forceinline__ void finish() {
+    if (__any_sync(0xffffffffu, cnt > 0)) flush();
+  }
+
+  // Instead of a final flush: writes the pending survivors, sorted descending
+  // and padded with empty keys to kAppendMax, at dst (16-byte aligned) -- a
+  // second sorted run beside the row's list, which the finish step reads too.
+  __device__ __forceinline__ void store_tail(uint64_t* dst) {
+    store_sorted_tail<A, APP_SMEM>(app_s, app_g, r, cnt, dst);
+    cnt = 0;
+  }
+};
+
+// ---------------------------------------------------------------------------
+// Warp-cooperative lists: element i = e * 32 + lane, E = L / 32 per lane.
+// ---------------------------------------------------------------------------
+template <int E>
+__device__ __forceinline__ void warp_merge_desc(uint64_t (&a)[E], int lane) {
+#pragma unroll
+  for (int stride = E * 16; stride > 0; stride >>= 1) {
+    if (stride >= 32) {
+      const int s = stride >> 5;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        if ((e & s) == 0) {
+          const uint64_t x = a[e], y = a[e | s];
+          a[e] = kmax(x, y);
+          a[e | s] = kmin(x, y);
+        }
+      }
+    } else {
+      const bool lower = (lane & stride) == 0;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const uint64_t y = __shfl_xor_sync(0xffffffffu, a[e], stride);
+        a[e] = lower ? kmax(a[e], y) : kmin(a[e], y);
+      }
+    }
+  }
+}
+
+// t <- best L of (t u u), both descending lists of L = 32 * E keys.
+template <int E>
+__device__ __forceinline__ void warp_merge_lists(uint64_t (&t)[E], const uint64_t (&u)[E], int lane) {
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const uint64_t y = __shfl_sync(0xffffffffu, u[E - 1 - e], 31 - lane);
+    t[e] = kmax(t[e], y);
+  }
+  warp_merge_desc<E>(t, lane);
+}
 
 }  // namespace stk

@@ -20,9 +20,10 @@
 //      thread per list, 4 keys at a time until a key below tau (lists are
 //      sorted).  The score kernel's lists are sparse -- each key passed the
 //      row's threshold floor -- so this is ~1.3 k keys per row on Gaussian
-//      data.  Few lists (<= kFinishFewLists, e.g. one per GPU): one thread per
-//      4-key chunk, all chunks at once, so a list costs one memory round trip
-//      whatever its depth.
+//      data.  Few or full lists (at most kFinishFewLists lists, e.g. one per
+//      GPU, or at most 8 chunks per thread, e.g. the full per-unit lists of a
+//      large batch): one thread per 4-key chunk, all chunks at once, so a list
+//      costs one memory round trip whatever its depth.
 //   3. Each candidate's position in the row's sorted result is the number of
 //      larger candidates (keys are distinct): one thread per candidate.
 //   More candidates than kFinishCap (adversarial inputs): the lists are folded
@@ -93,7 +94,9 @@ __device__ void select_row(const uint64_t* __restrict__ lists, int nlists, int64
   uint64_t kth = 0ull;  // largest k-th key of one list among this thread's lists
   // One list per thread (the common case): its first 4 keys of each run come
   // with the head in the same memory round trip and are gathered from registers.
-  const bool one_each = use_heads && nlists <= nthreads && nlists > kFinishFewLists;
+  const bool chunk_parallel =
+      use_heads && (nlists <= kFinishFewLists || (int64_t)nlists * ((L + tail) / 4) <= 8 * (int64_t)nthreads);
+  const bool one_each = use_heads && nlists <= nthreads && !chunk_parallel;
   uint64_t first[4] = {0ull, 0ull, 0ull, 0ull}, tfirst[4] = {0ull, 0ull, 0ull, 0ull};
   if (use_heads)
     for (int s = tid; s < nlists; s += nthreads) {
@@ -150,7 +153,7 @@ __device__ void select_row(const uint64_t* __restrict__ lists, int nlists, int64
     const uint64_t kk[4] = {u0.x, u0.y, u1.x, u1.y};
     return keep4(kk);
   };
-  if (use_heads && nlists <= kFinishFewLists) {
+  if (chunk_parallel) {
     const int chunks = (L + tail) / 4;
     for (int t = tid; t < nlists * chunks; t += nthreads) {
       const int s = t / chunks, q = (t % chunks) * 4;

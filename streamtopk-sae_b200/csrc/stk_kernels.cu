@@ -84,6 +84,21 @@ __device__ __forceinline__ void store_partials(uint32_t top, uint64_t* __restric
   __syncwarp();
 }
 
+// Copies this thread's row list from tensor memory (TOPT) to row_out
+// (16-byte aligned), 16 keys per warp-wide TMEM load.
+template <int L>
+__device__ __forceinline__ void store_list_tmem(uint32_t tlist, uint64_t* __restrict__ row_out) {
+#pragma unroll 1
+  for (int c = 0; c < 2 * L; c += 32) {
+    uint32_t v[32];
+    tmem_ld32(tlist + c, v);
+    tmem_wait_ld(v);
+    ulonglong2* d = reinterpret_cast<ulonglong2*>(row_out + c / 2);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) d[j] = make_ulonglong2(col_key(v, 2 * j), col_key(v, 2 * j + 1));
+  }
+}
+
 // Width of the tile starting at ft in the unit range [fb, fe).  (A schedule
 // that ended long units with a narrow tile, to shorten the exposed epilogue of
 // the last tile, measured slower at cfg3: its extra tile re-reads all of X.)
@@ -235,12 +250,12 @@ __device__ __forceinline__ void load_bias_tile(const float* __restrict__ bias, i
 // that the small terms do not add to the rounding of the large accumulator);
 // the epilogue (warps 4-7) adds the two.  The dropped Xl*Wl term is below
 // 2^-20 of |x||w|.
-template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TF32>
+template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPT, bool TF32>
 __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
     fused_topk_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_xl,
                       const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_w32,
                       const FusedParams p) {
-  using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM>;
+  using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM, TOPT>;
   constexpr int kSplitThreads = 64;                 // warps 2-3 (TF32)
   constexpr int kFirstEpiWarp = TF32 ? 4 : 2;
   constexpr uint32_t kWRowBytes = TF32 ? 64u : 128u;  // bytes of one W row in a stage
@@ -248,8 +263,16 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
   // TMEM: two accumulator buffers (tile parity), each NT columns, or for TF32
   // each 2 x NT (Xh*Wh, then the cross terms).
   constexpr uint32_t kAccCols = TF32 ? 2 * NT : NT;
-  constexpr uint32_t kTmemCols = TF32 ? 512u : (uint32_t)Cfg::kTmemCols;
+  constexpr uint32_t kTmemCols = (TF32 || TOPT) ? 512u : (uint32_t)Cfg::kTmemCols;
   static_assert(!TF32 || NT <= 128, "TF32 needs 4 x NT TMEM columns");
+  static_assert(!TOPT || (!TF32 && NT + 2 * L <= 512), "TMEM lists need 2 x L columns beside the accumulators");
+  // Accumulator buffers: two (the MMA of tile t + 1 overlaps the epilogue of
+  // tile t) unless TMEM-resident lists leave room for one only (NT = 256 with
+  // L = 128); then the TMA ring keeps filling during the epilogue and only the
+  // MMA waits.
+  constexpr int kAccBufs = (TOPT && 2 * kAccCols + 2 * L > 512) ? 1 : 2;
+  static_assert(!TOPT || kAccBufs * kAccCols + 2 * L <= 512, "TMEM columns");
+  constexpr uint32_t kListCol = kAccBufs * kAccCols;  // TOPT: the row lists' first column
   uint8_t* smem = stk_smem + ((1024u - (smem_u32(stk_smem) & 1023u)) & 1023u);
   uint64_t* top = reinterpret_cast<uint64_t*>(smem + Cfg::kTopOff);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOff);
@@ -356,8 +379,8 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
         unit_range(g, u, m, fb, fe);
         for (int64_t ft = fb, w = 0; ft < fe && ok; ft += w, ++tile) {
           w = tile_width<NT>(ft, fb, fe);
-          const int a = tile & 1;
-          if (!mbar_wait(&acc_empty[a], ((tile >> 1) & 1) ^ 1, abort_flag)) {
+          const int a = (int)(tile % kAccBufs);
+          if (!mbar_wait(&acc_empty[a], ((tile / kAccBufs) & 1) ^ 1, abort_flag)) {
             ok = false;
             break;
           }
@@ -459,7 +482,8 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
     const uint32_t top_s = (uint32_t)(reinterpret_cast<uint8_t*>(top) - stk_smem);
     const uint32_t app_s = (uint32_t)(reinterpret_cast<uint8_t*>(smem + Cfg::kAppOff) - stk_smem);
     uint64_t* app_cta = p.app + (size_t)blockIdx.x * (kAppendMax * kRows);
-    RowTopK<L, A, APP_SMEM> acc;
+    RowTopK<L, A, APP_SMEM, TOPT> acc;
+    const uint32_t list_s = TOPT ? t_lane + kListCol : top_s;  // where this thread's row list lives
     uint32_t tile = 0;
     bool ok = true;
     TileWalk<NT> cur;
@@ -470,13 +494,13 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
       TileWalk<NT> nxt = cur;
       nxt.next(g);
       if (nxt.valid(g)) load_bias_tile<NT>(p.bias, nxt.ft, nxt.width(), p.F, lane, bnext);
-      if (cur.first_of_unit()) acc.init(top_s, app_s, app_cta, r, p.k);
+      if (cur.first_of_unit()) acc.init(list_s, app_s, app_cta, r, p.k);
       const bool row_ok = (int64_t)cur.m * kRows + r < p.B;
       const int w = cur.width();
-      const int a = tile & 1;
+      const int a = (int)(tile % kAccBufs);
       // Warp-uniform wait: lane 0 polls, the others follow its verdict.
       int got = 1;
-      if (lane == 0) got = mbar_wait(&acc_full[a], (tile >> 1) & 1, abort_flag) ? 1 : 0;
+      if (lane == 0) got = mbar_wait(&acc_full[a], (tile / kAccBufs) & 1, abort_flag) ? 1 : 0;
       got = __shfl_sync(0xffffffffu, got, 0);
       if (!got) {
         if (p.pilot_hist != nullptr && cur.first_of_unit()) {
@@ -571,7 +595,10 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
           acc.store_tail(out_unit + (int64_t)r * p.list_pitch + L);  // no final merge: a sorted second run
         else
           acc.finish();
-        store_partials<L>(top_s, out_unit, p.list_pitch, q * 32, lane);
+        if constexpr (TOPT)
+          store_list_tmem<L>(list_s, out_unit + (int64_t)r * p.list_pitch);
+        else
+          store_partials<L>(top_s, out_unit, p.list_pitch, q * 32, lane);
         __threadfence();  // the lists are read by other CTAs in the finish step
       }
 #pragma unroll
@@ -725,11 +752,11 @@ __global__ void __launch_bounds__(kFinishThreads, 2) finish_kernel(const FinishA
 // ---------------------------------------------------------------------------
 // Explicit instantiations and launch helpers (host side of this TU).
 // ---------------------------------------------------------------------------
-template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TF32>
+template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPT, bool TF32>
 cudaError_t launch_fused(const CUtensorMap& tx, const CUtensorMap& txl, const CUtensorMap& tw, const CUtensorMap& tw32,
                          const FusedParams& p, int grid, cudaStream_t stream) {
-  using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM>;
-  auto kern = fused_topk_kernel<L, NT, STAGES, A, APP_SMEM, TF32>;
+  using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM, TOPT>;
+  auto kern = fused_topk_kernel<L, NT, STAGES, A, APP_SMEM, TOPT, TF32>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   if (e != cudaSuccess) return e;
   kern<<<grid, TF32 ? kFusedThreads + 64 : kFusedThreads, Cfg::kSmemBytes, stream>>>(tx, txl, tw, tw32, p);
@@ -776,15 +803,15 @@ cudaError_t launch_finish(const FinishArgs& fa, int grid, cudaStream_t stream) {
   return cudaLaunchKernelEx(&cfg, finish_kernel<L>, fa);
 }
 
-#define STK_INST_FUSED(L, NT, S, A, SM)                                                                      \
-  template cudaError_t launch_fused<L, NT, S, A, SM, false>(const CUtensorMap&, const CUtensorMap&,            \
-                                                            const CUtensorMap&, const CUtensorMap&,            \
-                                                            const FusedParams&, int, cudaStream_t);
+#define STK_INST_FUSED(L, NT, S, A, SM, TT)                                                                  \
+  template cudaError_t launch_fused<L, NT, S, A, SM, TT, false>(const CUtensorMap&, const CUtensorMap&,        \
+                                                                const CUtensorMap&, const CUtensorMap&,        \
+                                                                const FusedParams&, int, cudaStream_t);
 STK_FUSED_CONFIGS(STK_INST_FUSED)
-#define STK_INST_FUSED_TF32(L, NT, S, A, SM)                                                                 \
-  template cudaError_t launch_fused<L, NT, S, A, SM, true>(const CUtensorMap&, const CUtensorMap&,             \
-                                                           const CUtensorMap&, const CUtensorMap&,             \
-                                                           const FusedParams&, int, cudaStream_t);
+#define STK_INST_FUSED_TF32(L, NT, S, A, SM, TT)                                                             \
+  template cudaError_t launch_fused<L, NT, S, A, SM, TT, true>(const CUtensorMap&, const CUtensorMap&,         \
+                                                               const CUtensorMap&, const CUtensorMap&,         \
+                                                               const FusedParams&, int, cudaStream_t);
 STK_FUSED_TF32_CONFIGS(STK_INST_FUSED_TF32)
 
 #define STK_INST_SIMT(L)                                                                                         \

@@ -108,15 +108,16 @@ struct SimtParams {
 };
 
 // Shared-memory plan of the fused kernel: STAGES x (X tile 128x64, W tile
-// NTx64, both K-major 128-byte swizzled), the per-row top lists, the per-row
-// append slots when they live in shared memory (APP_SMEM), then the mbarriers.
-template <int L, int NT, int STAGES, int A, bool APP_SMEM>
+// NTx64, both K-major 128-byte swizzled), the per-row top lists unless they
+// live in tensor memory (TOPT), the per-row append slots when they live in
+// shared memory (APP_SMEM), then the mbarriers.
+template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPT>
 struct FusedCfg {
   static constexpr int kXBytes = kRows * 64 * 2;
   static constexpr int kWBytes = NT * 64 * 2;
   static constexpr int kStageBytes = kXBytes + kWBytes;
   static constexpr int kTopOff = STAGES * kStageBytes;
-  static constexpr int kAppOff = kTopOff + L * kRows * 8;
+  static constexpr int kAppOff = kTopOff + (TOPT ? 0 : L * kRows * 8);
   static constexpr int kBarOff = kAppOff + (APP_SMEM ? A * kRows * 8 : 0);
   static constexpr int kSmemBytes = 1024 + kBarOff + 256;
   static constexpr int kTmemCols = (2 * NT <= 32) ? 32 : (2 * NT <= 64) ? 64 : (2 * NT <= 128) ? 128 : (2 * NT <= 256) ? 256 : 512;
@@ -141,28 +142,32 @@ struct SimtCfg {
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
-// (L, NT, STAGES, A, APP_SMEM) instantiated for the fused kernel (the
-// defaults are chosen in stk_capi.cu).
-#define STK_FUSED_CONFIGS(X) \
-  X(32, 256, 3, 32, true)    \
-  X(64, 256, 3, 16, true)    \
-  X(64, 128, 4, 16, true)    \
-  X(32, 128, 5, 32, true)    \
-  X(128, 256, 2, 32, false)  \
-  X(128, 128, 3, 32, false)
+// (L, NT, STAGES, A, APP_SMEM, TOPT) instantiated for the fused kernel (the
+// defaults are chosen in stk_capi.cu).  TOPT: the per-row top lists live in
+// tensor memory beside the accumulators (two NT-column buffers, or one when
+// 2 x NT + 2 x L > 512 columns), which leaves the shared memory to the TMA ring.
+#define STK_FUSED_CONFIGS(X)      \
+  X(32, 256, 3, 32, true, false)  \
+  X(64, 256, 3, 16, true, false)  \
+  X(64, 128, 4, 16, true, false)  \
+  X(32, 128, 5, 32, true, false)  \
+  X(128, 256, 2, 32, false, false) \
+  X(128, 128, 3, 32, false, false) \
+  X(128, 128, 6, 32, true, true)  \
+  X(128, 256, 4, 32, true, true)
 
 // Configurations of the fp32 (3-pass TF32) variant: same shared-memory plan
 // (X and its residual take the bytes of the 16-bit X tile, W and its residual
 // those of the 16-bit W tile, K = 16 per stage with 64-byte swizzle); NT <= 128
 // because each accumulator buffer holds two NT-column accumulators.
-#define STK_FUSED_TF32_CONFIGS(X) \
-  X(32, 128, 5, 32, true)         \
-  X(64, 128, 4, 16, true)         \
-  X(128, 128, 3, 32, false)
+#define STK_FUSED_TF32_CONFIGS(X)   \
+  X(32, 128, 5, 32, true, false)    \
+  X(64, 128, 4, 16, true, false)    \
+  X(128, 128, 3, 32, false, false)
 
 // TF32: X is read through two maps (tx: X itself, txl: its residual
 // X - trunc13(X)); otherwise txl is unused.
-template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TF32>
+template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPT, bool TF32>
 cudaError_t launch_fused(const CUtensorMap& tx, const CUtensorMap& txl, const CUtensorMap& tw, const CUtensorMap& tw32,
                          const FusedParams& p, int grid, cudaStream_t stream);
 

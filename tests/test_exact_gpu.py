@@ -321,11 +321,11 @@ def test_working_memory_is_the_workspace(B, d, F, k):
 
 
 @pytest.mark.parametrize("cfg", ["32,256,3,32,1", "32,128,5,32,1", "64,256,3,16,1", "64,128,4,16,1",
-                                 "128,256,2,32,0", "128,128,3,32,0"])
+                                 "128,256,2,32,0", "128,128,3,32,0", "128,128,6,32,1,1", "128,256,4,32,1,1"])
 def test_tile_configurations_agree(cfg, monkeypatch):
     """Every instantiated tile configuration (128- or 256-feature tiles,
-    pipeline depth, append slots in shared or global memory) gives the default
-    configuration's rows bit for bit."""
+    pipeline depth, append slots in shared or global memory, top lists in
+    shared or tensor memory) gives the default configuration's rows bit for bit."""
     from streamtopk_sae import native
     L = int(cfg.split(",")[0])
     k = {32: 32, 64: 64, 128: 128}[L]
