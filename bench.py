@@ -8,9 +8,13 @@ Default workload (the north-star target):
 exact bf16, B=128, d=2048, F=262144, k=64, X ~ N(0,1), W_enc rows N(0,1)
 scaled to unit L2 norm, b_enc ~ N(0, 0.01) (std 0.1); W_enc is 1 GiB, larger
 than L2, so no L2 flush is needed between steps.  With N > 1 (torchrun, one
-process per GPU, NCCL) W_enc is sharded along F: each rank encodes its shard,
-an NCCL all-gather of the (B, L) key lists and a merge kernel finish the step
-(strong scaling: total work fixed).
+process per GPU) W_enc is sharded along F (streamtopk_sae.shard.ShardedEncoder,
+strong scaling: total work fixed): each rank's score kernel selects its rows'
+best k keys in its own tail and stores them into every rank's receive buffer
+over NVLink (CUDA IPC peer stores, per-row step tags, bounded waits), then
+merges the N lists of its rows: one kernel launch per step, replayed from a
+CUDA graph.  When a rank cannot map its peers the lists travel by an NCCL
+all-gather and a finish kernel instead (--transport nccl forces that).
 
 Printed on rank 0: one JSON line with the contract's keys, plus
   roofline      the fused tcgen05 kernel's algorithmic bytes / its CUDA-event
@@ -21,7 +25,8 @@ Printed on rank 0: one JSON line with the contract's keys, plus
   cpu_baseline  the reference's own CPU op (compiled from its sources into
                 oracle/_ref) on a bounded sample, rank 0 at N=1 only;
   e2e           the same metric through the public API with pinned host X in
-                and host V/I out every step;
+                and host V/I out every step (by default the upload of step
+                i+1 overlaps the kernels of step i on a copy stream);
   clocks        nvidia-smi samples taken during the timed region.
 --impl reference times the reference's CPU implementation (oracle/_ref, all
 host cores through a process pool) on the same metric.
@@ -449,31 +454,27 @@ def run_b200(args, cfg):
     Vh = torch.empty((B, k), dtype=torch.float32).pin_memory()
     Ih = torch.empty((B, k), dtype=torch.int32).pin_memory()
     e2e_steps = max(1, min(args.steps, 2000))
+    overlap = not args.e2e_serial
+    graphs = []
     if world == 1:
-        Xd = torch.empty_like(X)
-
-        def e2e_call(xh):
-            Xd.copy_(xh, non_blocking=True)
-            return step(Xd)
-        e2e = None
+        # The public op called eagerly on a device buffer (two when overlapped).
+        Xd2 = [torch.empty_like(X) for _ in range(2 if overlap else 1)]
+        runs = [(lambda xd: (lambda: step(xd)))(xd) for xd in Xd2]
     else:
-        e2e = CapturedEncode(step, X, steps=1, warmup=1)
-        e2e_call = e2e      # pinned host X -> static device buffer, replay
+        # One CUDA graph of one encode step per input buffer (graph.CapturedEncode:
+        # its static X is the buffer the host copy lands in).
+        graphs = [CapturedEncode(step, X, steps=1, warmup=1 if i == 0 else 0) for i in range(2 if overlap else 1)]
+        Xd2 = [g_.X for g_ in graphs]
+        runs = [g_.replay for g_ in graphs]
 
-    def e2e_step():
-        V, I = e2e_call(Xh)
-        Vh.copy_(V, non_blocking=True)
-        Ih.copy_(I, non_blocking=True)
-
-    overlap = not args.e2e_serial and world == 1
     if overlap:
         # A serving loop: X of step i+1 is uploaded on a copy stream while the
         # kernels of step i run (two device buffers); V/I come back on another.
         h2d = torch.cuda.Stream(device=dev)
         d2h = torch.cuda.Stream(device=dev)
-        Xd2 = [torch.empty_like(X), torch.empty_like(X)]
         copied = [torch.cuda.Event(), torch.cuda.Event()]
         consumed = [torch.cuda.Event(), torch.cuda.Event()]
+        readback = [torch.cuda.Event(), torch.cuda.Event()]
 
         def e2e_run(n):
             h2d.wait_stream(stream)
@@ -489,7 +490,9 @@ def run_b200(args, cfg):
                         Xd2[nxt].copy_(Xh, non_blocking=True)
                         copied[nxt].record(h2d)
                 stream.wait_event(copied[cur])
-                V, I = step(Xd2[cur])         # the public op (topk_sae_cuda_exact / _approx)
+                if world > 1 and i >= 2:
+                    stream.wait_event(readback[cur])  # V/I of this graph's previous replay are read
+                V, I = runs[cur]()            # the public op / the captured ShardedEncoder.encode
                 consumed[cur].record(stream)
                 d2h.wait_event(consumed[cur])
                 with torch.cuda.stream(d2h):
@@ -497,11 +500,15 @@ def run_b200(args, cfg):
                     I.record_stream(d2h)
                     Vh.copy_(V, non_blocking=True)
                     Ih.copy_(I, non_blocking=True)
+                    readback[cur].record(d2h)
             stream.wait_stream(d2h)
     else:
         def e2e_run(n):
             for _ in range(n):
-                e2e_step()
+                Xd2[0].copy_(Xh, non_blocking=True)
+                V, I = runs[0]()
+                Vh.copy_(V, non_blocking=True)
+                Ih.copy_(I, non_blocking=True)
 
     e2e_run(3)
     torch.cuda.synchronize(dev)
@@ -514,9 +521,9 @@ def run_b200(args, cfg):
     if world > 1:
         dist.all_reduce(t2, op=dist.ReduceOp.MAX)
     e2e_value = B * e2e_steps / (float(t2.item()) / 1e3)
-    if e2e is not None:
-        e2e.close()
-    e2e = e2e_call = None
+    for g_ in graphs:
+        g_.close()
+    graphs = runs = Xd2 = None
     torch.cuda.synchronize(dev)
 
     # ---------------- roofline of the dominant kernel (this rank's shard)
@@ -552,7 +559,7 @@ def run_b200(args, cfg):
             "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": Xh.numel() * Xh.element_size() * world,
                     "d2h_bytes_per_step": (Vh.numel() * 4 + Ih.numel() * 4) * world,
                     "path": (("streamtopk_sae.topk_sae_cuda_exact" if world == 1 else
-                              "streamtopk_sae.shard.ShardedEncoder.encode in a CUDA graph (graph.CapturedEncode)") +
+                              "streamtopk_sae.shard.ShardedEncoder.encode in CUDA graphs (graph.CapturedEncode)") +
                              (", X of step i+1 uploaded on a copy stream during step i, V/I read back on another"
                               if overlap else ", copies and kernels serialised on one stream"))},
             "parity": parity,
@@ -657,7 +664,7 @@ def main():
     ap.add_argument("--dtype", default=None, choices=["bf16", "fp16", "fp32"],
                     help="input dtype override (config 2 is a dtype sweep)")
     ap.add_argument("--e2e-serial", action="store_true",
-                    help="N=1 e2e: serialise each step's copies and kernels on one stream (default: the X upload "
+                    help="e2e: serialise each step's copies and kernels on one stream (default: the X upload "
                          "of step i+1 overlaps the kernels of step i on a copy stream)")
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="omit the timed CPU sample (profiling runs)")

@@ -10,12 +10,13 @@
 // bit-identical results: keys are unique, so a row's top-k is unique.
 //
 // Per row:
-//   1. tau = the larger of the k-th largest list head and the largest k-th key
-//      of any one list.  The k largest heads are k distinct keys, and a list
-//      holds k keys >= its own k-th key, so either way the row's k-th key is
-//      >= tau (tau = 1, every key, when neither bound exists).  The heads bound
-//      is the tight one for the score kernel's many sparse lists, the k-th key
-//      bound for the few full lists of the exchange.
+//   1. tau = a lower bound of the row's k-th key from k distinct real keys:
+//      the k-th largest list head (many lists), or, when there are fewer than
+//      2k lists (but more than 2k / L), the k-th largest of the first
+//      ceil(2k / nlists) keys of every list; and at least the largest k-th key
+//      of any one list (a list holds k keys >= its own k-th).  tau = 1 (every key) when no bound exists.  The
+//      heads bound suits the score kernel's many sparse lists, the prefix bound
+//      the few full lists of the exchange (one per GPU) or of a large batch.
 //   2. Every key >= tau is gathered into shared memory.  Many lists: one
 //      thread per list, 4 keys at a time until a key below tau (lists are
 //      sorted).  The score kernel's lists are sparse -- each key passed the
@@ -124,8 +125,31 @@ __device__ void select_row(const uint64_t* __restrict__ lists, int nlists, int64
       }
       sm.heads[s] = h;
     }
+  // Few lists for this k (nlists < 2k): the bound comes from the first
+  // m = ceil(2k / nlists) keys of every list instead of the heads alone -- the
+  // k-th largest of these nlists * m >= 2k real keys (k distinct keys >= it).
+  // Not when m would cover whole lists (one or two lists): the largest k-th
+  // key of one list is then as good, and the gather reads the lists anyway.
+  const int m2k = (use_heads && nlists > 0) ? max(1, (2 * k + nlists - 1) / nlists) : 0;
+  const int m = m2k < L ? m2k : 0;
+  const int P = nlists * m;  // <= 2k + nlists <= kFinishCap when m > 1
+  if (m > 1)
+    for (int t = tid; t < P; t += nthreads) {
+      const int s = t / m, j = t - (t / m) * m;
+      sm.cand[t] = list_on(list_mask, s) ? (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(
+                                               lists + ((int64_t)s * stride + b) * pitch + j))
+                                         : 0ull;
+    }
   __syncthreads();
-  if (use_heads) {
+  if (m > 1) {
+    for (int t = tid; t < P; t += nthreads) {
+      const uint64_t key = sm.cand[t];
+      if (key == 0ull) continue;
+      int r = 0;
+      for (int j = 0; j < P; ++j) r += sm.cand[j] > key ? 1 : 0;
+      if (r == k - 1) atomicMax(reinterpret_cast<unsigned long long*>(&sm.tau), (unsigned long long)key);
+    }
+  } else if (use_heads) {
     for (int s = tid; s < nlists; s += nthreads) {
       const uint64_t h = sm.heads[s];
       if (h == 0ull) continue;
@@ -133,8 +157,8 @@ __device__ void select_row(const uint64_t* __restrict__ lists, int nlists, int64
       for (int j = 0; j < nlists; ++j) r += sm.heads[j] > h ? 1 : 0;
       if (r == k - 1) atomicMax(reinterpret_cast<unsigned long long*>(&sm.tau), (unsigned long long)h);
     }
-    if (kth != 0ull) atomicMax(reinterpret_cast<unsigned long long*>(&sm.tau), (unsigned long long)kth);
   }
+  if (kth != 0ull) atomicMax(reinterpret_cast<unsigned long long*>(&sm.tau), (unsigned long long)kth);
   __syncthreads();
   const uint64_t tau = sm.tau;
   auto keep4 = [&](const uint64_t (&kk)[4]) {
