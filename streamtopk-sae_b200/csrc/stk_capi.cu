@@ -211,6 +211,7 @@ struct Plan {
   int ctas;
   bool pilot;
   bool fin_fused;  // the fused kernel finishes the rows itself (all units resident at once)
+  bool shared_floor;  // units publish their thresholds per row (several units per CTA, no pilot)
   int pitch;       // keys per row list in the partials: L, or L + kAppendMax (sorted tail run, fused finish)
   size_t ws_partials;
   size_t ws_app;
@@ -257,8 +258,17 @@ int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t 
   // second run (no final merge in the score kernel).
   pl->pitch = (pl->fin_fused && !std::getenv("STK_FULL_FLUSH")) ? pl->L + stk::kAppendMax : pl->L;
   pl->ws_partials = (partial_bytes(pl->grid, pl->pitch) + 255) & ~size_t(255);
+  // Without the pilot (several units per CTA, e.g. B > 256), the units of an
+  // M tile share their rising thresholds as a floor instead.  Not for the
+  // approximate path's per-tile candidate units (fixed_chunks), whose lists
+  // must hold each tile's own top c.
+  pl->shared_floor = pl->tc && !pl->pilot && pl->grid.units > pl->ctas && pl->grid.fixed_chunks == 0 &&
+                     !(flags & STK_FLAG_NO_PILOT);
   const size_t pilot_bytes = pl->pilot ? (size_t)pl->grid.m_tiles * stk::kRows * (stk::kPilotBins + 1) * 4 : 0;
-  pl->ws_sync = (pl->pilot || pl->fin_fused) ? ((kSyncBytes + pilot_bytes + 255) & ~size_t(255)) : 0;
+  const size_t floor_bytes = pl->shared_floor ? (size_t)pl->grid.m_tiles * stk::kRows * 4 : 0;
+  pl->ws_sync = (pl->pilot || pl->fin_fused || pl->shared_floor)
+                    ? ((kSyncBytes + pilot_bytes + floor_bytes + 255) & ~size_t(255))
+                    : 0;
   pl->ws_split = pl->tf32 ? (((size_t)B * d * 4 + 255) & ~size_t(255)) : 0;
   pl->ws = pl->ws_partials + pl->ws_app + pl->ws_sync + pl->ws_split;
   return STK_OK;
@@ -301,10 +311,11 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   int topt = 0;
   if (pl.L == 128 && !pl.tf32) {
     // k > 64: the per-row top-128 lists (128 KB) go to tensor memory beside
-    // 128-column accumulators, and the shared memory holds a six-stage TMA
-    // ring (two stages fit beside the lists in shared memory).
+    // 128-column accumulators, and the shared memory holds a three-stage TMA
+    // ring of 64 KB stages (K = 128 each; two 48 KB stages fit beside the
+    // lists in shared memory).
     nt = 128;
-    stages = 6;
+    stages = 3;
     app_smem = 1;
     topt = 1;
   }
@@ -351,6 +362,7 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   p.pilot_rowmax = nullptr;
   p.pilot_count = nullptr;
   p.tail_count = nullptr;
+  p.row_floor = nullptr;
   p.finish = 0;
   p.list_pitch = pl.pitch;
   std::memset(&p.fin, 0, sizeof p.fin);
@@ -362,6 +374,7 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
       p.pilot_hist = reinterpret_cast<uint32_t*>(base + kSyncBytes);
       p.pilot_rowmax = p.pilot_hist + (size_t)pl.grid.m_tiles * stk::kRows * stk::kPilotBins;
     }
+    if (pl.shared_floor) p.row_floor = reinterpret_cast<uint32_t*>(base + kSyncBytes);
     cudaError_t me = cudaMemsetAsync(base, 0, pl.ws_sync, stream);
     if (me != cudaSuccess) return cuda_fail(me, "cudaMemsetAsync(sync)");
   }
@@ -600,6 +613,7 @@ int candidates_plan(const void* X, const void* W, int64_t B, int64_t d, int64_t 
   if (pl->grid.units > 0x7fffffff / 2) return fail(STK_EINVAL, "too many candidate tiles");
   pl->ctas = pl->grid.units < sms ? pl->grid.units : sms;
   pl->pilot = false;
+  pl->shared_floor = false;  // each tile's own top c, not the row's top k
   pl->pitch = pl->L;
   pl->ws_partials = (partial_bytes(pl->grid, pl->pitch) + 255) & ~size_t(255);
   pl->ws_app = ((size_t)pl->ctas * stk::kAppendBytesPerCta + 255) & ~size_t(255);

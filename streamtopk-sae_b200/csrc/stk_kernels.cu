@@ -321,6 +321,8 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const UnitGrid& g = p.grid;
+  // Pipeline stages per tile: K blocks of kKPerStage elements, kSub per stage.
+  const int num_kb = TF32 ? p.num_kb : (p.num_kb + Cfg::kSub - 1) / Cfg::kSub;
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
@@ -334,24 +336,28 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
         unit_range(g, u, m, fb, fe);
         for (int64_t ft = fb, w = 0; ft < fe && ok; ft += w) {
           w = tile_width<NT>(ft, fb, fe);
-          const uint32_t bytes = Cfg::kXBytes + (uint32_t)w * kWRowBytes;
-          for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+          const uint32_t bytes = Cfg::kSub * (Cfg::kXBytes + (uint32_t)w * kWRowBytes);
+          for (int kb = 0; kb < num_kb; ++kb, ++it) {
             const int s = it % STAGES;
             if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag)) {
               ok = false;
               break;
             }
-            uint8_t* sx = smem + s * Cfg::kStageBytes;
-            uint8_t* sw = sx + Cfg::kXBytes;
             mbar_arrive_expect_tx(&full[s], bytes);
-            const int kx = kb * kKPerStage;
-            tma_load_2d(&tmap_x, &full[s], sx, kx, m * kRows, pol_x);
-            if constexpr (TF32) tma_load_2d(&tmap_xl, &full[s], sx + Cfg::kXBytes / 2, kx, m * kRows, pol_x);
-            if (w == NT) {
-              tma_load_2d(&tmap_w, &full[s], sw, kx, (int)ft, pol_w);
-            } else {
-              for (int q = 0; q < w / 32; ++q)
-                tma_load_2d(&tmap_w32, &full[s], sw + q * 32 * kWRowBytes, kx, (int)ft + 32 * q, pol_w);
+            // kSub K boxes: X boxes first, then the W boxes (a box past d
+            // reads zeros and adds nothing).
+            for (int h = 0; h < Cfg::kSub; ++h) {
+              uint8_t* sx = smem + s * Cfg::kStageBytes + h * Cfg::kXBytes;
+              uint8_t* sw = smem + s * Cfg::kStageBytes + Cfg::kSub * Cfg::kXBytes + h * Cfg::kWBytes;
+              const int kx = (kb * Cfg::kSub + h) * kKPerStage;
+              tma_load_2d(&tmap_x, &full[s], sx, kx, m * kRows, pol_x);
+              if constexpr (TF32) tma_load_2d(&tmap_xl, &full[s], sx + Cfg::kXBytes / 2, kx, m * kRows, pol_x);
+              if (w == NT) {
+                tma_load_2d(&tmap_w, &full[s], sw, kx, (int)ft, pol_w);
+              } else {
+                for (int q = 0; q < w / 32; ++q)
+                  tma_load_2d(&tmap_w32, &full[s], sw + q * 32 * kWRowBytes, kx, (int)ft + 32 * q, pol_w);
+              }
             }
           }
         }
@@ -388,7 +394,7 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
           const uint32_t d_tmem = tmem_base + (uint32_t)a * kAccCols;
           const uint32_t idesc = TF32 ? make_idesc_tf32(128u, (uint32_t)w)
                                       : make_idesc_f16((uint32_t)p.ab_format, 128u, (uint32_t)w);
-          for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+          for (int kb = 0; kb < num_kb; ++kb, ++it) {
             const int s = it % STAGES;
             // TF32: the W tile must also have been split by warps 2-3.
             if (!mbar_wait(TF32 ? &split_done[s] : &full[s], (it / STAGES) & 1, abort_flag)) {
@@ -410,11 +416,14 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
                 umma_tf32(d_tmem + NT, dxl + 2 * kk, dwh + 2 * kk, idesc, 1u);
               }
             } else {
-              const uint64_t dx = smem_desc_sw128(sx);
-              const uint64_t dw = smem_desc_sw128(sx + Cfg::kXBytes);
 #pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                umma_f16(d_tmem, dx + 2 * kk, dw + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+              for (int h = 0; h < Cfg::kSub; ++h) {
+                const uint64_t dx = smem_desc_sw128(sx + h * Cfg::kXBytes);
+                const uint64_t dw = smem_desc_sw128(sx + Cfg::kSub * Cfg::kXBytes + h * Cfg::kWBytes);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                  umma_f16(d_tmem, dx + 2 * kk, dw + 2 * kk, idesc, (kb | h | kk) != 0 ? 1u : 0u);
+              }
             }
             umma_commit(&empty[s]);
           }
@@ -446,7 +455,7 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
       unit_range(g, u, m, fb, fe);
       for (int64_t ft = fb, w = 0; ft < fe && ok; ft += w) {
         w = tile_width<NT>(ft, fb, fe);
-        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
           const int s = it % STAGES;
           const bool got = mbar_wait(&full[s], (it / STAGES) & 1, abort_flag);
           if (!__all_sync(0xffffffffu, got)) {
@@ -488,13 +497,17 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
     bool ok = true;
     TileWalk<NT> cur;
     cur.start(g);
+    float published = -__int_as_float(0x7f800000);  // this unit's last published threshold
     float bcur[NT / 32], bnext[NT / 32];
     if (cur.valid(g)) load_bias_tile<NT>(p.bias, cur.ft, cur.width(), p.F, lane, bcur);
     while (cur.valid(g)) {
       TileWalk<NT> nxt = cur;
       nxt.next(g);
       if (nxt.valid(g)) load_bias_tile<NT>(p.bias, nxt.ft, nxt.width(), p.F, lane, bnext);
-      if (cur.first_of_unit()) acc.init(list_s, app_s, app_cta, r, p.k);
+      if (cur.first_of_unit()) {
+        acc.init(list_s, app_s, app_cta, r, p.k);
+        published = -__int_as_float(0x7f800000);
+      }
       const bool row_ok = (int64_t)cur.m * kRows + r < p.B;
       const int w = cur.width();
       const int a = (int)(tile % kAccBufs);
@@ -516,6 +529,11 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
       tc_fence_after();
       const int nchunk = w / 32;
       const uint32_t tcol = t_lane + (uint32_t)a * kAccCols;
+      // Shared floor: the best lower bound of this row's k-th score that the
+      // other units of this M tile published so far (read now, applied after
+      // the tile, so the load's latency hides behind the chunks).
+      uint32_t shared_floor = 0u;
+      if (p.row_floor != nullptr && row_ok) shared_floor = __ldcg(p.row_floor + (size_t)cur.m * kRows + r);
       if (p.pilot_hist != nullptr && cur.first_of_unit()) {
         // Sample: histogram the first chunks of this tile (they stay in TMEM
         // and are offered below), meet the other CTAs, read back a floor.
@@ -588,6 +606,16 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
         for (int j = 0; j < 32; ++j) vals[j] = __uint_as_float(v[j]) + __shfl_sync(0xffffffffu, bl, j);
         const uint32_t valid = row_ok ? feature_mask(f, p.F) : 0u;
         acc.offer(vals, p.index_offset + (uint32_t)f, valid);
+      }
+      if (p.row_floor != nullptr && row_ok) {
+        // A unit's threshold is the k-th best of k real scores of the row (or
+        // a floor already known), so it bounds the row's k-th score from
+        // below for every unit: publish it, and take the others' bound.
+        if (shared_floor != 0u) acc.set_floor(order_float(shared_floor));
+        if (acc.thr > published) {
+          atomicMax(p.row_floor + (size_t)cur.m * kRows + r, float_order(acc.thr));
+          published = acc.thr;
+        }
       }
       if (cur.last_of_unit()) {
         uint64_t* out_unit = p.partials + (int64_t)cur.u * kRows * p.list_pitch;

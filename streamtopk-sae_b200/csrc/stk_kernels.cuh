@@ -85,12 +85,14 @@ struct FusedParams {
   uint32_t* pilot_rowmax;  // [m_tiles][128] highest bin seen per row
   uint32_t* pilot_count;   // CTAs that finished their sample
   uint32_t* tail_count;    // CTAs whose lists are stored (finish barrier); zeroed by the host
+  uint32_t* row_floor;     // [m_tiles][128] shared lower bound of each row's k-th score (float_order; 0 =
+                           // none), raised by every unit as its threshold rises; zeroed by the host; null = off
   int finish;              // 1: the kernel finishes the rows itself (fin), after a grid barrier
   int list_pitch;          // keys per row list in partials: L, or L + kAppendMax with a sorted tail run
   FinishArgs fin;
   int64_t B, F;
   int k;
-  int num_kb;          // ceil(d / 64)
+  int num_kb;          // ceil(d / 64) (16-bit inputs; the kernel groups kSub per stage), ceil(d / 16) for TF32
   int ab_format;       // 0 fp16, 1 bf16
   int w_evict_first;   // W is read once (single M tile): stream it past L2
   uint32_t index_offset;
@@ -115,7 +117,12 @@ template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPT>
 struct FusedCfg {
   static constexpr int kXBytes = kRows * 64 * 2;
   static constexpr int kWBytes = NT * 64 * 2;
-  static constexpr int kStageBytes = kXBytes + kWBytes;
+  // 64-element K boxes per pipeline stage.  Two (K = 128 per stage: the X
+  // boxes, then the W boxes) for the TMEM-list configurations with 128-feature
+  // tiles: each stage's handoff (TMA barrier, MMA issue, commit) then carries
+  // eight MMAs, which keeps the tensor pipe busier (cfg5: 10.9 -> 10.3 ms).
+  static constexpr int kSub = (TOPT && NT == 128) ? 2 : 1;
+  static constexpr int kStageBytes = kSub * (kXBytes + kWBytes);
   static constexpr int kTopOff = STAGES * kStageBytes;
   static constexpr int kAppOff = kTopOff + (TOPT ? 0 : L * kRows * 8);
   static constexpr int kBarOff = kAppOff + (APP_SMEM ? A * kRows * 8 : 0);
@@ -153,7 +160,7 @@ struct SimtCfg {
   X(32, 128, 5, 32, true, false)  \
   X(128, 256, 2, 32, false, false) \
   X(128, 128, 3, 32, false, false) \
-  X(128, 128, 6, 32, true, true)  \
+  X(128, 128, 3, 32, true, true)  \
   X(128, 256, 4, 32, true, true)
 
 // Configurations of the fp32 (3-pass TF32) variant: same shared-memory plan

@@ -202,10 +202,12 @@ def test_bias_cast_and_noncontiguous_inputs():
 
 
 @pytest.mark.parametrize("B,d,F,k", [(128, 256, 65536, 64), (96, 512, 40000, 32), (200, 128, 30000, 128),
-                                     (128, 64, 300000, 16)])
+                                     (128, 64, 300000, 16), (384, 256, 60000, 32), (640, 128, 40000, 128)])
 def test_sampled_floor_changes_nothing(B, d, F, k):
-    """The sampled threshold floor only skips work: results are bitwise equal
-    with and without it (keys are unique, so the top-k is unique)."""
+    """The sampled threshold floor (B <= 256) and the floor the units of an M
+    tile share (B > 256, several units per CTA) only skip work: results are
+    bitwise equal with and without them (keys are unique, so the top-k is
+    unique)."""
     from streamtopk_sae import _capi, native
     X, W, b = oracle.gaussian_inputs(B, d, F, seed=F % 1000)
     Xt, Wt, bt, Xr, Wr, br = device_inputs(X, W, b, "bf16")
@@ -321,7 +323,7 @@ def test_working_memory_is_the_workspace(B, d, F, k):
 
 
 @pytest.mark.parametrize("cfg", ["32,256,3,32,1", "32,128,5,32,1", "64,256,3,16,1", "64,128,4,16,1",
-                                 "128,256,2,32,0", "128,128,3,32,0", "128,128,6,32,1,1", "128,256,4,32,1,1"])
+                                 "128,256,2,32,0", "128,128,3,32,0", "128,128,3,32,1,1", "128,256,4,32,1,1"])
 def test_tile_configurations_agree(cfg, monkeypatch):
     """Every instantiated tile configuration (128- or 256-feature tiles,
     pipeline depth, append slots in shared or global memory, top lists in
