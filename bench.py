@@ -62,6 +62,8 @@ def esize(dtype):
 
 
 def alg_bytes(B, d, F, k, dtype):
+    if dtype == "fp8":   # bf16 X in, E4M3 W_enc, fp32 bias and per-feature scale, (B, k) out
+        return B * d * 2 + F * d + 8 * F + 8 * B * k
     """Algorithmic bytes per encode (reference bench/run_bandwidth.py:73-78)."""
     return B * d * esize(dtype) + F * d * esize(dtype) + 4 * F + 8 * B * k
 
@@ -88,14 +90,18 @@ def profiled_traffic(config_id, n_gpus):
     return None
 
 
-def float64_row_scores(X, W, b, rows, chunk=32768):
-    """float64 scores of the sampled rows over all features (on X's device)."""
+def float64_row_scores(X, W, b, rows, chunk=32768, w_scale=None):
+    """float64 scores of the sampled rows over all features (on X's device);
+    W's rows times w_scale when given (the fp8 path's dequantized W_enc)."""
     import torch
     Xs = X[rows].double()
     out = torch.empty((len(rows), W.shape[0]), dtype=torch.float64, device=X.device)
     for f0 in range(0, W.shape[0], chunk):
         f1 = min(W.shape[0], f0 + chunk)
-        out[:, f0:f1] = Xs @ W[f0:f1].double().T + b[f0:f1].double()
+        Wc = W[f0:f1].double()
+        if w_scale is not None:
+            Wc = Wc * w_scale[f0:f1, None].double()
+        out[:, f0:f1] = Xs @ Wc.T + b[f0:f1].double()
     return out
 
 
@@ -305,6 +311,9 @@ def config_dict(args, cfg):
          "B": cfg["B"], "d": cfg["d"], "F": cfg["F"], "k": cfg["k"], "global_batch": cfg["B"],
          "parallelism": f"F-shard{args.gpus}" if args.gpus > 1 else "single-gpu",
          "l2": "inputs larger than L2: each rank streams >= 128 MiB of W_enc per step"}
+    if cfg["dtype"] == "fp8":
+        d["fp8"] = ("E4M3 W_enc with one fp32 scale per feature (quantized once); X bf16, quantized per row to E4M3 "
+                    "on every call; kind::f8f6f4 with fp32 accumulation (an extension: lossy, reported as recall)")
     return d
 
 
@@ -331,14 +340,32 @@ def run_b200(args, cfg):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
     B, d, F, k = cfg["B"], cfg["d"], cfg["F"], cfg["k"]
-    dtype = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}[cfg["dtype"]]
+    fp8 = cfg["dtype"] == "fp8"
+    if fp8 and (world > 1 or cfg["mode"] != "exact"):
+        raise SystemExit("--dtype fp8: the exact encode on one GPU")
+    dtype = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32, "fp8": torch.bfloat16}[cfg["dtype"]]
     X, W, b = stk.make_inputs(B, d, F, dtype=dtype, seed=0, device=dev, w_init=cfg["w_init"])
     f0, f1 = stk_shard.shard_bounds(F, world, rank)
     # Correctness of what is timed (outside the timed region): float64 scores of
     # a few rows over all F, and at N > 1 the single-GPU encode of the full
     # W_enc on rank 0 (every rank holds the full W_enc before slicing).
     check_rows = sorted({0, B // 3, (2 * B) // 3, B - 1})
-    S_rows = float64_row_scores(X, W, b, check_rows) if rank == 0 else None
+    bf16_exact = None
+    if fp8:
+        # E4M3 W_enc (one scale per feature) and X quantized per row on every
+        # call: parity is against float64 scores of the quantized operands,
+        # and recall against the bf16 exact encode measures the quantization.
+        from streamtopk_sae import fp8 as stk_fp8
+        W8, w_scale = stk_fp8.quantize_weights(W)
+        Q, sx = stk_fp8.quantize_rows(X)
+        S_rows = float64_row_scores(Q.float() * sx[:, None], W8, b, check_rows, w_scale=w_scale)
+        bf16_exact = stk.topk_sae_cuda_exact(X, W, b, k)
+        torch.cuda.synchronize(dev)
+        del W, Q, sx
+        W = None
+        torch.cuda.empty_cache()
+    else:
+        S_rows = float64_row_scores(X, W, b, check_rows) if rank == 0 else None
     single_gpu = None
     if world > 1 and rank == 0:
         single_gpu = stk.topk_sae_cuda_exact(X, W, b, k)
@@ -350,6 +377,8 @@ def run_b200(args, cfg):
         enc = stk_shard.ShardedEncoder(W, b, F, f0, k, mode=cfg["mode"], c=cfg.get("c"),
                                        transport=args.transport, max_rows=B)
         step = enc.encode
+    elif fp8:
+        step = lambda x: stk_fp8.topk_sae_cuda_exact_fp8(x, W8, w_scale, b, k)  # noqa: E731
     elif cfg["mode"] == "approx":
         step = lambda x: stk.topk_sae_cuda_approx(x, W, b, k, cfg["c"])  # noqa: E731
     else:
@@ -445,6 +474,9 @@ def run_b200(args, cfg):
                   "rows_checked": len(check_rows), "rtol": rtol}
         if single_gpu is not None:
             parity["bitwise_vs_single_gpu"] = bool(torch.equal(Vp, single_gpu[0]) and torch.equal(Ip, single_gpu[1]))
+        if bf16_exact is not None:
+            parity["float64_of"] = "the quantized operands (x_scale * X8, w_scale * W8)"
+            parity["recall_vs_bf16_exact"] = stk.recall_at_k(Ip.long(), bf16_exact[1].long())
         parity["ok"] = all(v for kk, v in parity.items() if kk in ("rows_vs_float64", "bitwise_vs_single_gpu"))
         S_rows = single_gpu = None
     del Vp, Ip
@@ -534,7 +566,7 @@ def run_b200(args, cfg):
         per_launch = alg_bytes(B, d, Fs, k, cfg["dtype"])
         achieved = per_launch / (fused_avg_ms / 1e3) / 1e9
         roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                "traffic": (None if args.shape else profiled_traffic(args.config, world)),
+                "traffic": (None if args.shape or cfg["dtype"] == "fp8" else profiled_traffic(args.config, world)),
                 "kernel": "fused_topk_kernel", "kernel_ms": fused_avg_ms,
                 "algorithmic_bytes_per_launch": per_launch,
                 "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else "fallback"}
@@ -543,7 +575,7 @@ def run_b200(args, cfg):
         achieved = flops / (fused_avg_ms / 1e3) / 1e12
         peak = tf_sus
         roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                "traffic": (None if args.shape else profiled_traffic(args.config, world)), "kernel": "fused_topk_kernel",
+                "traffic": (None if args.shape or cfg["dtype"] == "fp8" else profiled_traffic(args.config, world)), "kernel": "fused_topk_kernel",
                 "kernel_ms": fused_avg_ms, "algorithmic_flops_per_launch": flops,
                 "peak_source": f"{src} bf16_tflops_sustained (fp16 assumed equal)"}
 
@@ -661,8 +693,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS))
-    ap.add_argument("--dtype", default=None, choices=["bf16", "fp16", "fp32"],
-                    help="input dtype override (config 2 is a dtype sweep)")
+    ap.add_argument("--dtype", default=None, choices=["bf16", "fp16", "fp32", "fp8"],
+                    help="input dtype override (config 2 is a dtype sweep); fp8: E4M3 W_enc with per-feature "
+                         "scales and X quantized per row on every call (streamtopk_sae.fp8; N=1, exact)")
     ap.add_argument("--e2e-serial", action="store_true",
                     help="e2e: serialise each step's copies and kernels on one stream (default: the X upload "
                          "of step i+1 overlaps the kernels of step i on a copy stream)")

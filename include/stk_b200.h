@@ -42,7 +42,9 @@ enum stk_status {
   STK_ENOSPACE = 4  /* workspace too small */
 };
 
-enum stk_dtype { STK_F32 = 0, STK_F16 = 1, STK_BF16 = 2 };
+/* Element types.  STK_E4M3 (one byte: FP8 E4M3, bias 7, max 448) is only
+ * W_enc's type in the stk_*_fp8 calls; X is then fp32, fp16 or bf16. */
+enum stk_dtype { STK_F32 = 0, STK_F16 = 1, STK_BF16 = 2, STK_E4M3 = 3 };
 
 /* Flags for the *_forward calls. */
 enum stk_flags {
@@ -156,6 +158,31 @@ STK_API int stk_device_error(void* stream, unsigned* code);
  */
 STK_API int stk_exact_forward_noalloc(const void* X, const void* W, const float* b, float* V, int32_t* I, int64_t B,
                                       int64_t d, int64_t F, int64_t k, int dtype, int flags, void* stream);
+
+/*
+ * FP8 W_enc streaming (no counterpart in the reference, whose dtype set is
+ * fp32 / fp16 / bf16, streamtopk_exact.cu:803-804): W_enc is (F, d) E4M3 with
+ * one fp32 dequantization scale per feature (w[f][j] ~= w_scale[f] * W8[f][j],
+ * e.g. from stk_quantize_rows_fp8), half the HBM bytes of bf16.  X (B, d) in
+ * x_dtype (fp32 / fp16 / bf16) is quantized per row to E4M3 by the library
+ * into the workspace (x_scale[r] = max_j |x[r][j]| / 448), and the tensor cores
+ * run kind::f8f6f4 with fp32 accumulation:
+ *     score[r][f] = x_scale[r] * w_scale[f] * sum_j X8[r][j] * W8[f][j] + b[f]
+ * and V / I are the exact top-k of these scores (keys as in stk_exact_forward).
+ * Lossy against the unquantized scores: a different operator, not a drop-in
+ * for the reference's.  Needs d % 16 == 0 and 16-byte aligned X and W8; k as
+ * in stk_exact_forward up to 128.
+ */
+STK_API int stk_workspace_bytes_fp8(int64_t B, int64_t d, int64_t F, int64_t k, size_t* bytes);
+STK_API int stk_exact_forward_fp8(const void* X, int x_dtype, const void* W8, const float* w_scale, const float* b,
+                                  float* V, int32_t* I, int64_t B, int64_t d, int64_t F, int64_t k, int flags,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+/* Per-row E4M3 quantization of a (rows, d) matrix in x_dtype (d % 16 == 0):
+ * scale[r] = max_j |x[r][j]| / 448 (1 for an all-zero row), Q[r][j] =
+ * E4M3(x[r][j] * 448 / max_j |x[r][j]|), round to nearest even, saturating.
+ * The quantization the fp8 encode applies to X; also makes W8 / w_scale. */
+STK_API int stk_quantize_rows_fp8(const void* X, int x_dtype, void* Q, float* scale, int64_t rows, int64_t d,
+                                  void* stream);
 
 /*
  * Direct GPU-to-GPU exchange for the F-sharded encode (no counterpart in the

@@ -167,6 +167,26 @@ int make_map_f32(CUtensorMap* map, const void* base, int64_t rows, int64_t d, in
   return STK_OK;
 }
 
+// 2-D K-major tensor map over a (rows, d) row-major byte matrix (E4M3) with a
+// (128 x box_rows) box (128 bytes of K per row) and 128-byte swizzle.
+int make_map_u8(CUtensorMap* map, const void* base, int64_t rows, int64_t d, int box_rows) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return fail(STK_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {(cuuint64_t)d, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)d};
+  const cuuint32_t box[2] = {128, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[96];
+    std::snprintf(buf, sizeof buf, "cuTensorMapEncodeTiled (e4m3) failed (CUresult %d)", (int)r);
+    return fail(STK_ECUDA, buf);
+  }
+  return STK_OK;
+}
+
 int list_len(int64_t k) { return k <= 32 ? 32 : k <= 64 ? 64 : k <= 128 ? 128 : 0; }
 
 bool ref_k(int64_t k) {
@@ -206,6 +226,9 @@ size_t partial_bytes(const stk::UnitGrid& g, int pitch) {
 struct Plan {
   bool tc;    // tcgen05 path
   bool tf32;  // tcgen05 path for fp32 inputs (3-pass TF32), opt-in
+  bool fp8;   // E4M3 W_enc, X quantized per row into the workspace (kind::f8f6f4)
+  int x_dtype;              // fp8: X's element type
+  const float* w_scale;     // fp8: per-feature scale of W_enc (call data)
   int L;
   stk::UnitGrid grid;
   int ctas;
@@ -217,6 +240,7 @@ struct Plan {
   size_t ws_app;
   size_t ws_sync;   // zeroed per call: barrier counters, then the pilot histogram and row maxima
   size_t ws_split;  // TF32: X's residual X - trunc13(X), 256-byte aligned
+  size_t ws_q;      // fp8: X quantized (B x d bytes, 256-aligned), then its row scales
   size_t ws;
 };
 
@@ -240,8 +264,11 @@ int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t 
   // forces fp32 FMA.
   pl->tf32 = dtype == STK_F32 && ((flags & STK_FLAG_TF32) || d <= kTf32DefaultMaxD) && (d % 4 == 0) &&
              !(flags & STK_FLAG_SIMT) && aligned;
+  pl->fp8 = dtype == STK_E4M3;
+  pl->x_dtype = dtype;
+  pl->w_scale = nullptr;
   pl->tc = ((dtype == STK_BF16 || dtype == STK_F16) && (d % 8 == 0) && !(flags & STK_FLAG_SIMT) && aligned) ||
-           pl->tf32;
+           pl->tf32 || (pl->fp8 && d % 16 == 0 && aligned);
   pl->grid = make_grid(B, F, sms);
   pl->ctas = pl->grid.units < sms ? pl->grid.units : sms;
   // partial lists, then one append buffer per CTA, then (optionally) the
@@ -270,7 +297,8 @@ int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t 
                     ? ((kSyncBytes + pilot_bytes + floor_bytes + 255) & ~size_t(255))
                     : 0;
   pl->ws_split = pl->tf32 ? (((size_t)B * d * 4 + 255) & ~size_t(255)) : 0;
-  pl->ws = pl->ws_partials + pl->ws_app + pl->ws_sync + pl->ws_split;
+  pl->ws_q = pl->fp8 ? (((size_t)B * d + 255) & ~size_t(255)) + (((size_t)B * 4 + 255) & ~size_t(255)) : 0;
+  pl->ws = pl->ws_partials + pl->ws_app + pl->ws_sync + pl->ws_split + pl->ws_q;
   return STK_OK;
 }
 
@@ -323,7 +351,24 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   CUtensorMap tx, txl, tw, tw32;
   const bool bf16 = dtype == STK_BF16;
   int rc = STK_OK;
-  if (pl.tf32) {
+  const float* x_scale = nullptr;
+  if (pl.fp8) {
+    // X is quantized per row (E4M3 + one scale per row) into the workspace;
+    // W_enc is E4M3 already.  Both through byte maps, 128 K elements per box.
+    uint8_t* xq = reinterpret_cast<uint8_t*>(partials) + pl.ws_partials + pl.ws_app + pl.ws_sync + pl.ws_split;
+    float* xs = reinterpret_cast<float*>(xq + (((size_t)B * d + 255) & ~size_t(255)));
+    cudaError_t qe = cudaErrorInvalidValue;
+    if (pl.x_dtype == STK_F32) qe = stk::launch_quantize_rows_e4m3(static_cast<const float*>(X), xq, xs, B, d, stream);
+    if (pl.x_dtype == STK_F16) qe = stk::launch_quantize_rows_e4m3(static_cast<const __half*>(X), xq, xs, B, d, stream);
+    if (pl.x_dtype == STK_BF16)
+      qe = stk::launch_quantize_rows_e4m3(static_cast<const __nv_bfloat16*>(X), xq, xs, B, d, stream);
+    if (qe != cudaSuccess) return cuda_fail(qe, "quantize_rows_e4m3_kernel launch");
+    x_scale = xs;
+    rc = make_map_u8(&tx, xq, B, d, stk::kRows);
+    if (!rc) rc = make_map_u8(&tw, W, F, d, nt);
+    if (!rc) rc = make_map_u8(&tw32, W, F, d, 32);
+    txl = tx;
+  } else if (pl.tf32) {
     // X's residual X - trunc13(X) is computed once per call (L2-resident,
     // re-read by every tile); W's residual tile by tile inside the kernel.  The
     // raw X and W are the hi operands (the tensor core reads them as TF32).
@@ -349,7 +394,9 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   p.B = B;
   p.F = F;
   p.k = (int)k;
-  p.num_kb = pl.tf32 ? (int)((d + 15) / 16) : (int)((d + 63) / 64);
+  p.num_kb = pl.tf32 ? (int)((d + 15) / 16) : pl.fp8 ? (int)((d + 127) / 128) : (int)((d + 63) / 64);
+  p.x_scale = x_scale;
+  p.w_scale = pl.w_scale;
   p.ab_format = bf16 ? 1 : 0;
   p.w_evict_first = pl.grid.m_tiles == 1 ? 1 : 0;
   p.index_offset = index_offset;
@@ -385,17 +432,23 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   cudaError_t e = cudaErrorInvalidValue;
   ProfScope prof(kProfFused, stream);
 #define STK_TRY_FUSED(Lc, NTc, Sc, Ac, SMc, TTc)                                                      \
-  if (!pl.tf32 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc &&  \
+  if (!pl.tf32 && !pl.fp8 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc &&  \
       (topt != 0) == TTc)                                                                               \
-    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, TTc, false>(tx, txl, tw, tw32, p, pl.ctas, stream);
+    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, TTc, stk::kModeF16>(tx, txl, tw, tw32, p, pl.ctas, stream);
   STK_FUSED_CONFIGS(STK_TRY_FUSED)
 #undef STK_TRY_FUSED
 #define STK_TRY_FUSED_TF32(Lc, NTc, Sc, Ac, SMc, TTc)                                                 \
   if (pl.tf32 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc &&   \
       (topt != 0) == TTc)                                                                               \
-    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, TTc, true>(tx, txl, tw, tw32, p, pl.ctas, stream);
+    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, TTc, stk::kModeTF32>(tx, txl, tw, tw32, p, pl.ctas, stream);
   STK_FUSED_TF32_CONFIGS(STK_TRY_FUSED_TF32)
 #undef STK_TRY_FUSED_TF32
+#define STK_TRY_FUSED_FP8(Lc, NTc, Sc, Ac, SMc, TTc)                                                  \
+  if (pl.fp8 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc &&    \
+      (topt != 0) == TTc)                                                                               \
+    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, TTc, stk::kModeFP8>(tx, txl, tw, tw32, p, pl.ctas, stream);
+  STK_FUSED_FP8_CONFIGS(STK_TRY_FUSED_FP8)
+#undef STK_TRY_FUSED_FP8
   if (e != cudaSuccess) return cuda_fail(e, "fused_topk_kernel launch");
   return STK_OK;
 }
@@ -561,6 +614,63 @@ int stk_exact_forward(const void* X, const void* W, const float* b, float* V, in
                 static_cast<cudaStream_t>(stream));
 }
 
+int stk_quantize_rows_fp8(const void* X, int x_dtype, void* Q, float* scale, int64_t rows, int64_t d, void* stream) {
+  if (x_dtype != STK_F32 && x_dtype != STK_F16 && x_dtype != STK_BF16)
+    return fail(STK_EINVAL, "stk_quantize_rows_fp8: X dtype must be fp32, fp16, or bf16");
+  if (rows < 0 || d < 1) return fail(STK_EINVAL, "stk_quantize_rows_fp8: empty or negative shape");
+  if (d % 16 != 0) return fail(STK_EINVAL, "stk_quantize_rows_fp8: d must be a multiple of 16");
+  if (rows == 0) return STK_OK;
+  if (!X || !Q || !scale || !aligned16(Q)) return fail(STK_EINVAL, "stk_quantize_rows_fp8: null or unaligned pointer");
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaErrorInvalidValue;
+  uint8_t* q = static_cast<uint8_t*>(Q);
+  if (x_dtype == STK_F32) e = stk::launch_quantize_rows_e4m3(static_cast<const float*>(X), q, scale, rows, d, s);
+  if (x_dtype == STK_F16) e = stk::launch_quantize_rows_e4m3(static_cast<const __half*>(X), q, scale, rows, d, s);
+  if (x_dtype == STK_BF16)
+    e = stk::launch_quantize_rows_e4m3(static_cast<const __nv_bfloat16*>(X), q, scale, rows, d, s);
+  if (e != cudaSuccess) return cuda_fail(e, "quantize_rows_e4m3_kernel launch");
+  return STK_OK;
+}
+
+int stk_workspace_bytes_fp8(int64_t B, int64_t d, int64_t F, int64_t k, size_t* bytes) {
+  if (!bytes) return fail(STK_EINVAL, "bytes is NULL");
+  int rc = check_common("stk_workspace_bytes_fp8", B, d, F, STK_BF16);
+  if (rc) return rc;
+  if (k < 1 || list_len(k) == 0) return fail(STK_EINVAL, "k out of range");
+  Plan pl;
+  rc = plan(nullptr, nullptr, B, d, F, k, STK_E4M3, 0, &pl);
+  if (rc) return rc;
+  *bytes = pl.ws;
+  return STK_OK;
+}
+
+int stk_exact_forward_fp8(const void* X, int x_dtype, const void* W8, const float* w_scale, const float* b, float* V,
+                          int32_t* I, int64_t B, int64_t d, int64_t F, int64_t k, int flags, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  int rc = check_common("streamtopk_cuda_exact_fp8", B, d, F, x_dtype);
+  if (rc) return rc;
+  if (!(k >= 1 && k <= F)) return fail(STK_EINVAL, "k out of range");
+  if (d > 4096 && !(flags & STK_FLAG_ANY_D)) return fail(STK_EINVAL, "d exceeds D_MAX=4096");
+  if (!(flags & STK_FLAG_ANY_K) && !ref_k(k))
+    return fail(STK_EINVAL, "streamtopk_cuda_exact_fp8: unsupported k=" + std::to_string(k) +
+                                ". Supported: 1,2,4,8,16,32,64,128.");
+  if (k > 128) return fail(STK_EINVAL, "streamtopk_cuda_exact_fp8: k must be <= 128");
+  if (d % 16 != 0) return fail(STK_EINVAL, "streamtopk_cuda_exact_fp8: d must be a multiple of 16");
+  if (B > 0 && (!X || !W8 || !w_scale || !b || !aligned16(X) || !aligned16(W8)))
+    return fail(STK_EINVAL, "streamtopk_cuda_exact_fp8: null or unaligned (16-byte) input");
+  if (flags & STK_FLAG_SIMT) return fail(STK_EINVAL, "streamtopk_cuda_exact_fp8: no SIMT path for FP8");
+  Plan pl;
+  rc = plan(X, W8, B, d, F, k, STK_E4M3, flags, &pl);
+  if (rc) return rc;
+  pl.x_dtype = x_dtype;
+  pl.w_scale = w_scale;
+  if (B == 0) return STK_OK;
+  if (workspace_bytes < pl.ws || (pl.ws && workspace == nullptr))
+    return fail(STK_ENOSPACE, "workspace too small (need " + std::to_string(pl.ws) + " bytes)");
+  return score_and_finish(pl, X, W8, b, V, I, nullptr, B, d, F, k, STK_E4M3, 0u, nullptr, workspace,
+                          static_cast<cudaStream_t>(stream));
+}
+
 int stk_approx_forward(const void* X, const void* W, const float* b, float* V, int32_t* I, int64_t B, int64_t d,
                        int64_t F, int64_t k, int64_t c, int dtype, int flags, void* workspace,
                        size_t workspace_bytes, void* stream) {
@@ -614,6 +724,10 @@ int candidates_plan(const void* X, const void* W, int64_t B, int64_t d, int64_t 
   pl->ctas = pl->grid.units < sms ? pl->grid.units : sms;
   pl->pilot = false;
   pl->shared_floor = false;  // each tile's own top c, not the row's top k
+  pl->fp8 = false;
+  pl->x_dtype = dtype;
+  pl->w_scale = nullptr;
+  pl->ws_q = 0;
   pl->pitch = pl->L;
   pl->ws_partials = (partial_bytes(pl->grid, pl->pitch) + 255) & ~size_t(255);
   pl->ws_app = ((size_t)pl->ctas * stk::kAppendBytesPerCta + 255) & ~size_t(255);

@@ -205,6 +205,19 @@ __device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t adesc, uint6
       : "memory");
 }
 
+// Same with FP8 operands, kind::f8f6f4 (the instruction descriptor's A/B
+// format code 0 = E4M3), K = 32 per instruction: 32 bytes of a 128-byte row,
+// so the descriptor advances exactly as for 16-bit operands.
+__device__ __forceinline__ void umma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Makes this thread's generic-proxy writes to shared memory visible to the
 // async proxy (tensor-core operand reads) after the next synchronisation.
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -223,6 +223,18 @@ __device__ __forceinline__ float pick(const float (&b)[N], int i) {
   return v;
 }
 
+// Score of column j of a chunk (lane j's bias bl and, for FP8, scale sl):
+// the accumulator plus the bias, or for FP8 the dequantized product
+// x_scale * w_scale * acc plus the bias.
+template <bool FP8>
+__device__ __forceinline__ float chunk_score(uint32_t acc_bits, float bl, float sl, float sxr, int j) {
+  const float b = __shfl_sync(0xffffffffu, bl, j);
+  if constexpr (FP8)
+    return fmaf(__uint_as_float(acc_bits), sxr * __shfl_sync(0xffffffffu, sl, j), b);
+  else
+    return __uint_as_float(acc_bits) + b;
+}
+
 // Bias of one tile: lane l holds bias[ft + 32 c + l] for chunk c (0 past F).
 template <int NT>
 __device__ __forceinline__ void load_bias_tile(const float* __restrict__ bias, int64_t ft, int w, int64_t F, int lane,
@@ -250,16 +262,22 @@ __device__ __forceinline__ void load_bias_tile(const float* __restrict__ bias, i
 // that the small terms do not add to the rounding of the large accumulator);
 // the epilogue (warps 4-7) adds the two.  The dropped Xl*Wl term is below
 // 2^-20 of |x||w|.
-template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPT, bool TF32>
-__global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
+//
+// MODE = kModeFP8: E4M3 X and W, kind::f8f6f4, K = 128 per 128-byte box (the
+// 16-bit plan with one byte per element); the epilogue scales each score by
+// its row's and feature's dequantization factors before the bias.
+template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPT, int MODE>
+__global__ void __launch_bounds__(MODE == kModeTF32 ? kFusedThreads + 64 : kFusedThreads, 1)
     fused_topk_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_xl,
                       const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_w32,
                       const FusedParams p) {
   using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM, TOPT>;
+  constexpr bool TF32 = MODE == kModeTF32;
+  constexpr bool FP8 = MODE == kModeFP8;
   constexpr int kSplitThreads = 64;                 // warps 2-3 (TF32)
   constexpr int kFirstEpiWarp = TF32 ? 4 : 2;
   constexpr uint32_t kWRowBytes = TF32 ? 64u : 128u;  // bytes of one W row in a stage
-  constexpr int kKPerStage = TF32 ? 16 : 64;        // elements of K per stage
+  constexpr int kKPerStage = TF32 ? 16 : FP8 ? 128 : 64;  // elements of K per 128-byte box
   // TMEM: two accumulator buffers (tile parity), each NT columns, or for TF32
   // each 2 x NT (Xh*Wh, then the cross terms).
   constexpr uint32_t kAccCols = TF32 ? 2 * NT : NT;
@@ -393,7 +411,8 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + (uint32_t)a * kAccCols;
           const uint32_t idesc = TF32 ? make_idesc_tf32(128u, (uint32_t)w)
-                                      : make_idesc_f16((uint32_t)p.ab_format, 128u, (uint32_t)w);
+                                 : FP8  ? make_idesc_f16(0u, 128u, (uint32_t)w)  // E4M3 x E4M3
+                                        : make_idesc_f16((uint32_t)p.ab_format, 128u, (uint32_t)w);
           for (int kb = 0; kb < num_kb; ++kb, ++it) {
             const int s = it % STAGES;
             // TF32: the W tile must also have been split by warps 2-3.
@@ -421,8 +440,12 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
                 const uint64_t dx = smem_desc_sw128(sx + h * Cfg::kXBytes);
                 const uint64_t dw = smem_desc_sw128(sx + Cfg::kSub * Cfg::kXBytes + h * Cfg::kWBytes);
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                  umma_f16(d_tmem, dx + 2 * kk, dw + 2 * kk, idesc, (kb | h | kk) != 0 ? 1u : 0u);
+                for (int kk = 0; kk < 4; ++kk) {
+                  if constexpr (FP8)
+                    umma_f8(d_tmem, dx + 2 * kk, dw + 2 * kk, idesc, (kb | h | kk) != 0 ? 1u : 0u);
+                  else
+                    umma_f16(d_tmem, dx + 2 * kk, dw + 2 * kk, idesc, (kb | h | kk) != 0 ? 1u : 0u);
+                }
               }
             }
             umma_commit(&empty[s]);
@@ -499,16 +522,25 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
     cur.start(g);
     float published = -__int_as_float(0x7f800000);  // this unit's last published threshold
     float bcur[NT / 32], bnext[NT / 32];
-    if (cur.valid(g)) load_bias_tile<NT>(p.bias, cur.ft, cur.width(), p.F, lane, bcur);
+    float scur[NT / 32], snext[NT / 32];  // FP8: per-feature scales, like the bias
+    if (cur.valid(g)) {
+      load_bias_tile<NT>(p.bias, cur.ft, cur.width(), p.F, lane, bcur);
+      if constexpr (FP8) load_bias_tile<NT>(p.w_scale, cur.ft, cur.width(), p.F, lane, scur);
+    }
     while (cur.valid(g)) {
       TileWalk<NT> nxt = cur;
       nxt.next(g);
-      if (nxt.valid(g)) load_bias_tile<NT>(p.bias, nxt.ft, nxt.width(), p.F, lane, bnext);
+      if (nxt.valid(g)) {
+        load_bias_tile<NT>(p.bias, nxt.ft, nxt.width(), p.F, lane, bnext);
+        if constexpr (FP8) load_bias_tile<NT>(p.w_scale, nxt.ft, nxt.width(), p.F, lane, snext);
+      }
       if (cur.first_of_unit()) {
         acc.init(list_s, app_s, app_cta, r, p.k);
         published = -__int_as_float(0x7f800000);
       }
       const bool row_ok = (int64_t)cur.m * kRows + r < p.B;
+      float sxr = 1.f;  // FP8: this row's dequantization scale
+      if constexpr (FP8) sxr = row_ok ? __ldg(p.x_scale + (size_t)cur.m * kRows + r) : 0.f;
       const int w = cur.width();
       const int a = (int)(tile % kAccBufs);
       // Warp-uniform wait: lane 0 polls, the others follow its verdict.
@@ -546,6 +578,7 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
           load_chunk<TF32, NT>(tcol, c, v);
           const int64_t f = cur.ft + 32 * c;
           const float bl = pick<NT / 32>(bcur, c);
+          const float sl = FP8 ? pick<NT / 32>(scur, c) : 0.f;
           const uint32_t valid = row_ok ? feature_mask(f, p.F) : 0u;
           // Histogram the maximum of each group of kPilotGroup scores: they
           // are real scores of distinct features, so the k-th largest of them
@@ -556,7 +589,7 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
             float gm = -__int_as_float(0x7f800000);
 #pragma unroll
             for (int j = g0; j < g0 + kPilotGroup; ++j) {
-              const float vj = __uint_as_float(v[j]) + __shfl_sync(0xffffffffu, bl, j);
+              const float vj = chunk_score<FP8>(v[j], bl, sl, sxr, j);
               if (valid & (1u << j)) gm = fmaxf(gm, vj);
             }
             if ((valid >> g0) & ((1u << kPilotGroup) - 1u)) {
@@ -601,9 +634,10 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
         }
         const int64_t f = cur.ft + 32 * c;
         const float bl = pick<NT / 32>(bcur, c);
+        const float sl = FP8 ? pick<NT / 32>(scur, c) : 0.f;
         float vals[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) vals[j] = __uint_as_float(v[j]) + __shfl_sync(0xffffffffu, bl, j);
+        for (int j = 0; j < 32; ++j) vals[j] = chunk_score<FP8>(v[j], bl, sl, sxr, j);
         const uint32_t valid = row_ok ? feature_mask(f, p.F) : 0u;
         acc.offer(vals, p.index_offset + (uint32_t)f, valid);
       }
@@ -630,7 +664,10 @@ __global__ void __launch_bounds__(TF32 ? kFusedThreads + 64 : kFusedThreads, 1)
         __threadfence();  // the lists are read by other CTAs in the finish step
       }
 #pragma unroll
-      for (int c = 0; c < NT / 32; ++c) bcur[c] = bnext[c];
+      for (int c = 0; c < NT / 32; ++c) {
+        bcur[c] = bnext[c];
+        if constexpr (FP8) scur[c] = snext[c];
+      }
       cur = nxt;
       ++tile;
     }
@@ -780,14 +817,15 @@ __global__ void __launch_bounds__(kFinishThreads, 2) finish_kernel(const FinishA
 // ---------------------------------------------------------------------------
 // Explicit instantiations and launch helpers (host side of this TU).
 // ---------------------------------------------------------------------------
-template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPT, bool TF32>
+template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPT, int MODE>
 cudaError_t launch_fused(const CUtensorMap& tx, const CUtensorMap& txl, const CUtensorMap& tw, const CUtensorMap& tw32,
                          const FusedParams& p, int grid, cudaStream_t stream) {
   using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM, TOPT>;
-  auto kern = fused_topk_kernel<L, NT, STAGES, A, APP_SMEM, TOPT, TF32>;
+  auto kern = fused_topk_kernel<L, NT, STAGES, A, APP_SMEM, TOPT, MODE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   if (e != cudaSuccess) return e;
-  kern<<<grid, TF32 ? kFusedThreads + 64 : kFusedThreads, Cfg::kSmemBytes, stream>>>(tx, txl, tw, tw32, p);
+  kern<<<grid, MODE == kModeTF32 ? kFusedThreads + 64 : kFusedThreads, Cfg::kSmemBytes, stream>>>(tx, txl, tw, tw32,
+                                                                                                  p);
   return cudaGetLastError();
 }
 
@@ -832,15 +870,20 @@ cudaError_t launch_finish(const FinishArgs& fa, int grid, cudaStream_t stream) {
 }
 
 #define STK_INST_FUSED(L, NT, S, A, SM, TT)                                                                  \
-  template cudaError_t launch_fused<L, NT, S, A, SM, TT, false>(const CUtensorMap&, const CUtensorMap&,        \
-                                                                const CUtensorMap&, const CUtensorMap&,        \
-                                                                const FusedParams&, int, cudaStream_t);
+  template cudaError_t launch_fused<L, NT, S, A, SM, TT, kModeF16>(const CUtensorMap&, const CUtensorMap&,     \
+                                                                   const CUtensorMap&, const CUtensorMap&,     \
+                                                                   const FusedParams&, int, cudaStream_t);
 STK_FUSED_CONFIGS(STK_INST_FUSED)
 #define STK_INST_FUSED_TF32(L, NT, S, A, SM, TT)                                                             \
-  template cudaError_t launch_fused<L, NT, S, A, SM, TT, true>(const CUtensorMap&, const CUtensorMap&,         \
-                                                               const CUtensorMap&, const CUtensorMap&,         \
-                                                               const FusedParams&, int, cudaStream_t);
+  template cudaError_t launch_fused<L, NT, S, A, SM, TT, kModeTF32>(const CUtensorMap&, const CUtensorMap&,    \
+                                                                    const CUtensorMap&, const CUtensorMap&,    \
+                                                                    const FusedParams&, int, cudaStream_t);
 STK_FUSED_TF32_CONFIGS(STK_INST_FUSED_TF32)
+#define STK_INST_FUSED_FP8(L, NT, S, A, SM, TT)                                                              \
+  template cudaError_t launch_fused<L, NT, S, A, SM, TT, kModeFP8>(const CUtensorMap&, const CUtensorMap&,     \
+                                                                   const CUtensorMap&, const CUtensorMap&,     \
+                                                                   const FusedParams&, int, cudaStream_t);
+STK_FUSED_FP8_CONFIGS(STK_INST_FUSED_FP8)
 
 #define STK_INST_SIMT(L)                                                                                         \
   template cudaError_t launch_simt<float, L>(const void*, const void*, const SimtParams&, int, cudaStream_t);   \
@@ -851,6 +894,52 @@ STK_FUSED_TF32_CONFIGS(STK_INST_FUSED_TF32)
 STK_INST_SIMT(32)
 STK_INST_SIMT(64)
 STK_INST_SIMT(128)
+
+// ---------------------------------------------------------------------------
+// Per-row E4M3 quantization (the FP8 path's X, or W_enc once ahead of use):
+// one warp per row, the row's absolute maximum by a warp reduction, then 4
+// elements per lane and step converted with the hardware's round-to-nearest-
+// even, saturating E4M3 conversion and stored as one 32-bit word.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void quantize_rows_e4m3_kernel(const T* __restrict__ X, uint8_t* __restrict__ Q,
+                                          float* __restrict__ scale, int64_t rows, int64_t d) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const T* x = X + row * d;
+  float m = 0.f;
+  for (int64_t j = lane; j < d; j += 32) m = fmaxf(m, fabsf(to_f32(x[j])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float inv = m > 0.f ? 448.f / m : 1.f;
+  if (lane == 0) scale[row] = m > 0.f ? m / 448.f : 1.f;
+  uint32_t* q = reinterpret_cast<uint32_t*>(Q + row * d);  // d % 16 == 0: 16-byte aligned rows
+  for (int64_t j = 4 * lane; j < d; j += 128) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const __nv_fp8_storage_t b = __nv_cvt_float_to_fp8(to_f32(x[j + e]) * inv, __NV_SATFINITE, __NV_E4M3);
+      word |= (uint32_t)b << (8 * e);
+    }
+    q[j / 4] = word;
+  }
+}
+
+template <typename T>
+cudaError_t launch_quantize_rows_e4m3(const T* X, uint8_t* Q, float* scale, int64_t rows, int64_t d,
+                                      cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  constexpr int kWarps = 8;
+  const int64_t blocks = (rows + kWarps - 1) / kWarps;
+  quantize_rows_e4m3_kernel<T><<<(unsigned)blocks, 32 * kWarps, 0, stream>>>(X, Q, scale, rows, d);
+  return cudaGetLastError();
+}
+template cudaError_t launch_quantize_rows_e4m3<float>(const float*, uint8_t*, float*, int64_t, int64_t, cudaStream_t);
+template cudaError_t launch_quantize_rows_e4m3<__half>(const __half*, uint8_t*, float*, int64_t, int64_t,
+                                                       cudaStream_t);
+template cudaError_t launch_quantize_rows_e4m3<__nv_bfloat16>(const __nv_bfloat16*, uint8_t*, float*, int64_t,
+                                                              int64_t, cudaStream_t);
 
 // ---------------------------------------------------------------------------
 // Whole-row sort for small F (k up to F <= kFullSortMaxF, beyond the list

@@ -4,6 +4,7 @@
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 
 #include "stk_device.cuh"
 
@@ -97,6 +98,8 @@ struct FusedParams {
   int w_evict_first;   // W is read once (single M tile): stream it past L2
   uint32_t index_offset;
   int pilot_chunks;    // sampled 32-feature chunks per CTA (<= the first tile's chunks)
+  const float* x_scale;  // FP8: [B] per-row dequantization scale of X
+  const float* w_scale;  // FP8: [F] per-feature dequantization scale of W (scores = x_s * w_s * acc + b)
 };
 
 struct SimtParams {
@@ -172,14 +175,36 @@ struct SimtCfg {
   X(64, 128, 4, 16, true, false)    \
   X(128, 128, 3, 32, false, false)
 
+// Configurations of the FP8 variant (E4M3 X and W_enc, K = 128 per 128-byte
+// box): the 16-bit shared-memory plan, half the bytes per K element.
+#define STK_FUSED_FP8_CONFIGS(X)      \
+  X(32, 256, 3, 32, true, false)     \
+  X(64, 256, 3, 16, true, false)     \
+  X(64, 128, 4, 16, true, false)     \
+  X(32, 128, 5, 32, true, false)     \
+  X(128, 128, 3, 32, true, true)
+
+// Operand modes of the fused kernel.
+constexpr int kModeF16 = 0;   // fp16 / bf16 X and W, kind::f16
+constexpr int kModeTF32 = 1;  // fp32 X and W, 3-pass kind::tf32
+constexpr int kModeFP8 = 2;   // E4M3 X (quantized per row by the library) and W (per-feature scale), kind::f8f6f4
+
 // TF32: X is read through two maps (tx: X itself, txl: its residual
 // X - trunc13(X)); otherwise txl is unused.
-template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPT, bool TF32>
+template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPT, int MODE>
 cudaError_t launch_fused(const CUtensorMap& tx, const CUtensorMap& txl, const CUtensorMap& tw, const CUtensorMap& tw32,
                          const FusedParams& p, int grid, cudaStream_t stream);
 
 // Xl = X - trunc13(X) (exact in fp32), n elements.
 cudaError_t launch_residual_tf32(const float* X, float* Xl, int64_t n, cudaStream_t stream);
+
+// Per-row E4M3 quantization of a (rows, d) matrix of T (float, __half or
+// __nv_bfloat16): scale[r] = max_j |x[r][j]| / 448 (1 for an all-zero row),
+// Q[r][j] = E4M3(x[r][j] * (448 / max_j |x[r][j]|)), round to nearest even,
+// saturating.  x[r][j] ~= scale[r] * Q[r][j].
+template <typename T>
+cudaError_t launch_quantize_rows_e4m3(const T* X, uint8_t* Q, float* scale, int64_t rows, int64_t d,
+                                      cudaStream_t stream);
 
 template <typename T, int L>
 cudaError_t launch_simt(const void* X, const void* W, const SimtParams& p, int grid, cudaStream_t stream);

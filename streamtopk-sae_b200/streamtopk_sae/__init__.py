@@ -7,7 +7,9 @@ materialising the (B, F) score matrix, on tcgen05 tensor cores with the top-k
 selection fused into the GEMM epilogue.  ``shard`` adds the multi-GPU
 F-sharded encoder (one process per GPU; the per-rank key lists are exchanged
 by direct peer stores between the GPUs, or by an NCCL all-gather, then merged).
+``fp8`` adds an E4M3 W_enc path (half the HBM bytes; lossy, an extension).
 """
+from streamtopk_sae.fp8 import quantize_weights, topk_sae_cuda_exact_fp8
 from streamtopk_sae.ops import check_device_errors, topk_sae_cpu, topk_sae_cuda_approx, topk_sae_cuda_exact
 from streamtopk_sae.utils import make_inputs, recall_at_k
 
@@ -18,4 +20,6 @@ __all__ = [
     "check_device_errors",
     "recall_at_k",
     "make_inputs",
+    "quantize_weights",
+    "topk_sae_cuda_exact_fp8",
 ]

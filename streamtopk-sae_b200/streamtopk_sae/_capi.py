@@ -13,7 +13,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libstk_b200.so")
 
 STK_OK, STK_EINVAL, STK_ECUDA, STK_EDEVICE, STK_ENOSPACE = 0, 1, 2, 3, 4
-STK_F32, STK_F16, STK_BF16 = 0, 1, 2
+STK_F32, STK_F16, STK_BF16, STK_E4M3 = 0, 1, 2, 3
 STK_FLAG_ANY_K, STK_FLAG_ANY_D, STK_FLAG_SIMT, STK_FLAG_NO_PILOT, STK_FLAG_TF32 = 1, 2, 4, 8, 16
 STK_FLAG_SEPARATE_FINISH = 32
 
@@ -24,6 +24,7 @@ EXPORTS = (
     "stk_profile_begin", "stk_profile_end", "stk_exact_forward_noalloc", "stk_candidates_workspace_bytes",
     "stk_exchange_bytes", "stk_exchange_create", "stk_exchange_ipc_handle", "stk_exchange_connect",
     "stk_exchange_forward", "stk_exchange_destroy",
+    "stk_workspace_bytes_fp8", "stk_exact_forward_fp8", "stk_quantize_rows_fp8",
 )
 IPC_HANDLE_BYTES = 64
 
@@ -89,6 +90,12 @@ def load():
         L.stk_exchange_forward.argtypes = [vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32, vp, sz, vp]
         L.stk_exchange_destroy.restype = i32
         L.stk_exchange_destroy.argtypes = [vp]
+        L.stk_workspace_bytes_fp8.restype = i32
+        L.stk_workspace_bytes_fp8.argtypes = [i64, i64, i64, i64, ctypes.POINTER(sz)]
+        L.stk_exact_forward_fp8.restype = i32
+        L.stk_exact_forward_fp8.argtypes = [vp, i32, vp, vp, vp, vp, vp, i64, i64, i64, i64, i32, vp, sz, vp]
+        L.stk_quantize_rows_fp8.restype = i32
+        L.stk_quantize_rows_fp8.argtypes = [vp, i32, vp, vp, i64, i64, vp]
         _lib = L
     return _lib
 
@@ -103,6 +110,12 @@ def check(rc: int) -> None:
 def workspace_bytes(B: int, d: int, F: int, k: int, dtype_code: int) -> int:
     out = ctypes.c_size_t(0)
     check(load().stk_workspace_bytes(B, d, F, k, dtype_code, ctypes.byref(out)))
+    return int(out.value)
+
+
+def workspace_bytes_fp8(B: int, d: int, F: int, k: int) -> int:
+    out = ctypes.c_size_t(0)
+    check(load().stk_workspace_bytes_fp8(B, d, F, k, ctypes.byref(out)))
     return int(out.value)
 
 
