@@ -55,8 +55,10 @@ enum stk_flags {
   STK_FLAG_NO_PILOT = 8, /* skip the sampled threshold floor (testing / comparison) */
   STK_FLAG_TF32 = 16,    /* fp32 inputs on tensor cores (3-pass TF32) also for d > 2048 (the default up to
                             d = 2048, d % 4 == 0); otherwise fp32 uses the SIMT kernel */
-  STK_FLAG_SEPARATE_FINISH = 32 /* finish the rows in a second kernel even where the score kernel
-                                   could do it in its tail (testing / comparison) */
+  STK_FLAG_SEPARATE_FINISH = 32, /* finish the rows in a second kernel even where the score kernel
+                                    could do it in its tail (testing / comparison) */
+  STK_FLAG_NO_PAIR = 64 /* no CTA pairs (tcgen05 cta_group::2, used for k > 64 with several 128-row
+                           M tiles per call) (testing / comparison) */
 };
 
 /* Library version (major * 10000 + minor * 100 + patch). */

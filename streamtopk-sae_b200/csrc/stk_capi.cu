@@ -35,9 +35,42 @@ int cuda_fail(cudaError_t e, const char* where) {
 constexpr int kMaxDevices = 64;
 struct DeviceInfo {
   int sms = 0;
+  int pair_grid = -1;  // CTAs of the CTA-pair kernel (even; 0: unavailable); -1 not queried yet
 };
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_dev_mu;
+
+int device_sms(int* sms);
+
+// CTAs to launch the CTA-pair kernel with: two per 2-CTA cluster, as many
+// clusters as fit on the device at once (at most one CTA per SM).
+int pair_grid(int* grid) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(STK_EINVAL, "device ordinal out of range");
+  {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (g_dev[dev].pair_grid >= 0) {
+      *grid = g_dev[dev].pair_grid;
+      return STK_OK;
+    }
+  }
+  int sms = 0;
+  int rc = device_sms(&sms);
+  if (rc) return rc;
+  int clusters = 0;
+#define STK_PAIR_MAX(Lc, NTc, Sc, Ac, SMc, TTc) \
+  clusters = stk::pair_clusters_max<Lc, NTc, Sc, Ac, SMc, TTc, stk::kModeF16 | stk::kModePair>();
+  STK_FUSED_PAIR_CONFIGS(STK_PAIR_MAX)
+#undef STK_PAIR_MAX
+  cudaGetLastError();  // an occupancy query that failed leaves no sticky error
+  if (clusters > sms / 2) clusters = sms / 2;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  g_dev[dev].pair_grid = clusters > 0 ? 2 * clusters : 0;
+  *grid = g_dev[dev].pair_grid;
+  return STK_OK;
+}
 
 int device_sms(int* sms) {
   int dev = 0;
@@ -235,6 +268,7 @@ struct Plan {
   bool pilot;
   bool fin_fused;  // the fused kernel finishes the rows itself (all units resident at once)
   bool shared_floor;  // units publish their thresholds per row (several units per CTA, no pilot)
+  bool pair;          // CTA pairs (tcgen05 cta_group::2, M = 256): k > 64, an even number of M tiles
   int pitch;       // keys per row list in the partials: L, or L + kAppendMax (sorted tail run, fused finish)
   size_t ws_partials;
   size_t ws_app;
@@ -271,6 +305,21 @@ int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t 
            pl->tf32 || (pl->fp8 && d % 16 == 0 && aligned);
   pl->grid = make_grid(B, F, sms);
   pl->ctas = pl->grid.units < sms ? pl->grid.units : sms;
+  // CTA pairs for k > 64 with several rounds of units per CTA and an even
+  // number of M tiles: the pair's MMA covers two M tiles (M = 256) and each
+  // CTA loads half the W tile, which cuts the L2-to-SM bytes per MMA by a
+  // quarter (the TMEM-list kernel at B = 4096 is bound by them).
+  pl->pair = false;
+  if (pl->tc && !pl->tf32 && pl->L == 128 && pl->grid.m_tiles >= 2 && pl->grid.m_tiles % 2 == 0 &&
+      !(flags & STK_FLAG_NO_PAIR)) {
+    int pg = 0;
+    rc = pair_grid(&pg);
+    if (rc) return rc;
+    if (pg >= 2 && pl->grid.units > pg) {
+      pl->pair = true;
+      pl->ctas = pg;
+    }
+  }
   // partial lists, then one append buffer per CTA, then (optionally) the
   // pilot histogram, row maxima and arrival counter (256-byte aligned parts)
   pl->ws_app = ((size_t)pl->ctas * stk::kAppendBytesPerCta + 255) & ~size_t(255);
@@ -347,7 +396,18 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
     app_smem = 1;
     topt = 1;
   }
-  fused_override(pl.L, &nt, &stages, &nslots, &app_smem, &topt);
+  if (pl.pair) {
+    // The pair configuration: 128-feature tiles, four 48 KB stages (each CTA's
+    // X boxes and half the W rows, K = 128), lists in TMEM.
+    nt = 128;
+    stages = 4;
+    nslots = 32;
+    app_smem = 1;
+    topt = 1;
+  } else {
+    fused_override(pl.L, &nt, &stages, &nslots, &app_smem, &topt);
+  }
+  const int w_box = pl.pair ? nt / 2 : nt;  // pairs: each CTA loads half the tile's W rows
   CUtensorMap tx, txl, tw, tw32;
   const bool bf16 = dtype == STK_BF16;
   int rc = STK_OK;
@@ -365,7 +425,7 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
     if (qe != cudaSuccess) return cuda_fail(qe, "quantize_rows_e4m3_kernel launch");
     x_scale = xs;
     rc = make_map_u8(&tx, xq, B, d, stk::kRows);
-    if (!rc) rc = make_map_u8(&tw, W, F, d, nt);
+    if (!rc) rc = make_map_u8(&tw, W, F, d, w_box);
     if (!rc) rc = make_map_u8(&tw32, W, F, d, 32);
     txl = tx;
   } else if (pl.tf32) {
@@ -381,7 +441,7 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
     if (!rc) rc = make_map_f32(&tw32, W, F, d, 32);
   } else {
     rc = make_map(&tx, X, B, d, stk::kRows, bf16);
-    if (!rc) rc = make_map(&tw, W, F, d, nt, bf16);
+    if (!rc) rc = make_map(&tw, W, F, d, w_box, bf16);
     if (!rc) rc = make_map(&tw32, W, F, d, 32, bf16);
     txl = tx;
   }
@@ -431,8 +491,20 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   }
   cudaError_t e = cudaErrorInvalidValue;
   ProfScope prof(kProfFused, stream);
+#define STK_TRY_FUSED_PAIR(Lc, NTc, Sc, Ac, SMc, TTc)                                                      \
+  if (pl.pair && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc &&           \
+      (topt != 0) == TTc) {                                                                                    \
+    if (pl.fp8)                                                                                                \
+      e = stk::launch_fused_pair<Lc, NTc, Sc, Ac, SMc, TTc, stk::kModeFP8 | stk::kModePair>(tx, tw, p, pl.ctas, \
+                                                                                             stream);          \
+    else                                                                                                       \
+      e = stk::launch_fused_pair<Lc, NTc, Sc, Ac, SMc, TTc, stk::kModeF16 | stk::kModePair>(tx, tw, p, pl.ctas, \
+                                                                                             stream);          \
+  }
+  STK_FUSED_PAIR_CONFIGS(STK_TRY_FUSED_PAIR)
+#undef STK_TRY_FUSED_PAIR
 #define STK_TRY_FUSED(Lc, NTc, Sc, Ac, SMc, TTc)                                                      \
-  if (!pl.tf32 && !pl.fp8 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc &&  \
+  if (!pl.pair && !pl.tf32 && !pl.fp8 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc &&  \
       (topt != 0) == TTc)                                                                               \
     e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, TTc, stk::kModeF16>(tx, txl, tw, tw32, p, pl.ctas, stream);
   STK_FUSED_CONFIGS(STK_TRY_FUSED)
@@ -444,7 +516,7 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   STK_FUSED_TF32_CONFIGS(STK_TRY_FUSED_TF32)
 #undef STK_TRY_FUSED_TF32
 #define STK_TRY_FUSED_FP8(Lc, NTc, Sc, Ac, SMc, TTc)                                                  \
-  if (pl.fp8 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc &&    \
+  if (!pl.pair && pl.fp8 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc &&    \
       (topt != 0) == TTc)                                                                               \
     e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, TTc, stk::kModeFP8>(tx, txl, tw, tw32, p, pl.ctas, stream);
   STK_FUSED_FP8_CONFIGS(STK_TRY_FUSED_FP8)
@@ -724,6 +796,7 @@ int candidates_plan(const void* X, const void* W, int64_t B, int64_t d, int64_t 
   pl->ctas = pl->grid.units < sms ? pl->grid.units : sms;
   pl->pilot = false;
   pl->shared_floor = false;  // each tile's own top c, not the row's top k
+  pl->pair = false;
   pl->fp8 = false;
   pl->x_dtype = dtype;
   pl->w_scale = nullptr;

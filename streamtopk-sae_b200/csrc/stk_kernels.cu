@@ -108,31 +108,49 @@ __device__ __forceinline__ int tile_width(int64_t ft, int64_t fb, int64_t fe) {
   return (int)min((int64_t)NT, fe - ft);
 }
 
-// Walks the tiles of this CTA: units u = blockIdx.x, +gridDim.x, ...; tiles
-// of tile_width<NT> features within each unit's range.
-template <int NT>
-struct TileWalk {
-  int u, m;
-  int64_t fb, fe, ft;
-  __device__ __forceinline__ void start(const UnitGrid& g) {
-    u = blockIdx.x;
-    if (u < g.units) {
-      unit_range(g, u, m, fb, fe);
-      ft = fb;
-    }
+// The j-th unit of this CTA.  One CTA per unit: u = blockIdx.x + j * gridDim.x.
+// CTA pairs (PAIR, a 2-CTA cluster sharing the MMA): pair-unit pu = cluster +
+// j * clusters covers one feature range of two adjacent M tiles, the CTA of
+// rank r taking M tile 2 * (pu % (m_tiles / 2)) + r (m_tiles is even), so a
+// CTA's units are still units u = range * m_tiles + m of the plain grid.
+template <bool PAIR>
+__device__ __forceinline__ bool unit_at(const UnitGrid& g, int j, uint32_t rank, int& u, int& m, int64_t& fb,
+                                        int64_t& fe) {
+  if constexpr (PAIR) {
+    const int mp_tiles = g.m_tiles / 2;
+    const int pu = (int)(blockIdx.x / 2) + j * (int)(gridDim.x / 2);
+    if (pu >= g.segs * mp_tiles) return false;
+    u = (pu / mp_tiles) * g.m_tiles + 2 * (pu % mp_tiles) + (int)rank;
+  } else {
+    u = (int)blockIdx.x + j * (int)gridDim.x;
+    if (u >= g.units) return false;
   }
-  __device__ __forceinline__ bool valid(const UnitGrid& g) const { return u < g.units; }
+  unit_range(g, u, m, fb, fe);
+  return true;
+}
+
+// Walks the tiles of this CTA: its units (unit_at), tiles of tile_width<NT>
+// features within each unit's range.
+template <int NT, bool PAIR>
+struct TileWalk {
+  int j, u, m;
+  int64_t fb, fe, ft;
+  bool ok;
+  __device__ __forceinline__ void start(const UnitGrid& g, uint32_t rank) {
+    j = 0;
+    ok = unit_at<PAIR>(g, 0, rank, u, m, fb, fe);
+    ft = fb;
+  }
+  __device__ __forceinline__ bool valid(const UnitGrid&) const { return ok; }
   __device__ __forceinline__ bool first_of_unit() const { return ft == fb; }
   __device__ __forceinline__ int width() const { return tile_width<NT>(ft, fb, fe); }
   __device__ __forceinline__ bool last_of_unit() const { return ft + width() >= fe; }
-  __device__ __forceinline__ void next(const UnitGrid& g) {
+  __device__ __forceinline__ void next(const UnitGrid& g, uint32_t rank) {
     ft += width();
     if (ft >= fe) {
-      u += gridDim.x;
-      if (u < g.units) {
-        unit_range(g, u, m, fb, fe);
-        ft = fb;
-      }
+      ++j;
+      ok = unit_at<PAIR>(g, j, rank, u, m, fb, fe);
+      ft = fb;
     }
   }
 };
@@ -266,14 +284,26 @@ __device__ __forceinline__ void load_bias_tile(const float* __restrict__ bias, i
 // MODE = kModeFP8: E4M3 X and W, kind::f8f6f4, K = 128 per 128-byte box (the
 // 16-bit plan with one byte per element); the epilogue scales each score by
 // its row's and feature's dequantization factors before the bias.
+//
+// MODE | kModePair: CTA pairs (2-CTA clusters).  The pair's first CTA issues
+// tcgen05.mma.cta_group::2 with M = 256 (each CTA's 128 X rows, its own M
+// tile) and N = NT (each CTA holds NT / 2 of the W tile's rows): every CTA
+// loads half the W bytes per tile, and the accumulator of each CTA's rows
+// lands in its own TMEM, read by its own epilogue as in the one-CTA kernel.
+// Both CTAs' TMA loads count on the first CTA's full barrier (it alone waits
+// on it and expects both CTAs' bytes); its commits arrive on both CTAs' empty
+// and acc_full barriers; the second CTA's epilogue arrives remotely on the
+// first CTA's acc_empty barrier (8 arrivals per phase).
 template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPT, int MODE>
-__global__ void __launch_bounds__(MODE == kModeTF32 ? kFusedThreads + 64 : kFusedThreads, 1)
+__global__ void __launch_bounds__((MODE & 3) == kModeTF32 ? kFusedThreads + 64 : kFusedThreads, 1)
     fused_topk_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_xl,
                       const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_w32,
                       const FusedParams p) {
-  using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM, TOPT>;
-  constexpr bool TF32 = MODE == kModeTF32;
-  constexpr bool FP8 = MODE == kModeFP8;
+  constexpr bool PAIR = (MODE & kModePair) != 0;
+  using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM, TOPT, PAIR>;
+  constexpr bool TF32 = (MODE & 3) == kModeTF32;
+  constexpr bool FP8 = (MODE & 3) == kModeFP8;
+  static_assert(!PAIR || (!TF32 && NT % 32 == 0), "CTA pairs: 16-bit or FP8 operands");
   constexpr int kSplitThreads = 64;                 // warps 2-3 (TF32)
   constexpr int kFirstEpiWarp = TF32 ? 4 : 2;
   constexpr uint32_t kWRowBytes = TF32 ? 64u : 128u;  // bytes of one W row in a stage
@@ -317,7 +347,7 @@ __global__ void __launch_bounds__(MODE == kModeTF32 ? kFusedThreads + 64 : kFuse
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], kEpilogueWarps);
+      mbar_init(&acc_empty[a], PAIR ? 2 * kEpilogueWarps : kEpilogueWarps);
     }
     mbar_init(mma_done, 1);
     if constexpr (TF32)
@@ -329,12 +359,21 @@ __global__ void __launch_bounds__(MODE == kModeTF32 ? kFusedThreads + 64 : kFuse
     tma_prefetch_desc(&tmap_w);
     tma_prefetch_desc(&tmap_w32);
   }
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;  // 0: the pair's MMA-issuing CTA
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync();  // both CTAs' barriers are initialised before any remote arrival
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -348,59 +387,78 @@ __global__ void __launch_bounds__(MODE == kModeTF32 ? kFusedThreads + 64 : kFuse
       const uint64_t pol_w = p.w_evict_first ? l2_policy_evict_first() : l2_policy_evict_normal();
       uint32_t it = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < g.units && ok; u += gridDim.x) {
-        int m;
-        int64_t fb, fe;
-        unit_range(g, u, m, fb, fe);
+      int u, m;
+      int64_t fb, fe;
+      for (int j = 0; ok && unit_at<PAIR>(g, j, rank, u, m, fb, fe); ++j) {
         for (int64_t ft = fb, w = 0; ft < fe && ok; ft += w) {
           w = tile_width<NT>(ft, fb, fe);
-          const uint32_t bytes = Cfg::kSub * (Cfg::kXBytes + (uint32_t)w * kWRowBytes);
+          // Pairs: each CTA loads its X tile and NT / 2 W rows (the whole half
+          // even for a narrow tile: columns past w are never read).
+          const uint32_t bytes = PAIR ? 2u * Cfg::kStageBytes
+                                      : Cfg::kSub * (Cfg::kXBytes + (uint32_t)w * kWRowBytes);
           for (int kb = 0; kb < num_kb; ++kb, ++it) {
             const int s = it % STAGES;
             if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag)) {
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&full[s], bytes);
+            if (!PAIR || rank == 0) mbar_arrive_expect_tx(&full[s], bytes);
             // kSub K boxes: X boxes first, then the W boxes (a box past d
             // reads zeros and adds nothing).
             for (int h = 0; h < Cfg::kSub; ++h) {
               uint8_t* sx = smem + s * Cfg::kStageBytes + h * Cfg::kXBytes;
               uint8_t* sw = smem + s * Cfg::kStageBytes + Cfg::kSub * Cfg::kXBytes + h * Cfg::kWBytes;
               const int kx = (kb * Cfg::kSub + h) * kKPerStage;
-              tma_load_2d(&tmap_x, &full[s], sx, kx, m * kRows, pol_x);
-              if constexpr (TF32) tma_load_2d(&tmap_xl, &full[s], sx + Cfg::kXBytes / 2, kx, m * kRows, pol_x);
-              if (w == NT) {
-                tma_load_2d(&tmap_w, &full[s], sw, kx, (int)ft, pol_w);
+              if constexpr (PAIR) {
+                const uint32_t full0 = mapa_shared(smem_u32(&full[s]), 0u);
+                tma_load_2d_pair(&tmap_x, full0, sx, kx, m * kRows, pol_x);
+                tma_load_2d_pair(&tmap_w, full0, sw, kx, (int)ft + (int)rank * (NT / 2), pol_w);
               } else {
-                for (int q = 0; q < w / 32; ++q)
-                  tma_load_2d(&tmap_w32, &full[s], sw + q * 32 * kWRowBytes, kx, (int)ft + 32 * q, pol_w);
+                tma_load_2d(&tmap_x, &full[s], sx, kx, m * kRows, pol_x);
+                if constexpr (TF32) tma_load_2d(&tmap_xl, &full[s], sx + Cfg::kXBytes / 2, kx, m * kRows, pol_x);
+                if (w == NT) {
+                  tma_load_2d(&tmap_w, &full[s], sw, kx, (int)ft, pol_w);
+                } else {
+                  for (int q = 0; q < w / 32; ++q)
+                    tma_load_2d(&tmap_w32, &full[s], sw + q * 32 * kWRowBytes, kx, (int)ft + 32 * q, pol_w);
+                }
               }
             }
           }
         }
       }
+      const uint32_t n = it < (uint32_t)STAGES ? it : (uint32_t)STAGES;
       if (!ok) {
         raise_device_error(kErrWaitTimeout);
         *abort_flag = 1;
-        // Let the copies already issued land before the CTA can exit.
-        const uint32_t n = it < (uint32_t)STAGES ? it : (uint32_t)STAGES;
-        for (uint32_t j = 0; j < n; ++j) {
-          const uint32_t i = it - 1 - j;
-          mbar_wait(&full[i % STAGES], (i / STAGES) & 1, nullptr);
+        // Let the copies already issued land before the CTA can exit.  (A
+        // pair's copies count on the first CTA's barrier: its MMA issuer
+        // waits for them, or gives up too, and the pair meets at the final
+        // cluster barrier.)
+        if (!PAIR)
+          for (uint32_t i0 = 0; i0 < n; ++i0) {
+            const uint32_t i = it - 1 - i0;
+            mbar_wait(&full[i % STAGES], (i / STAGES) & 1, nullptr);
+          }
+      }
+      if constexpr (PAIR) {
+        // The first CTA's last commits arrive on this CTA's empty barriers:
+        // wait for them (bounded) so that none is still in flight at exit.
+        for (uint32_t i0 = 0; i0 < n; ++i0) {
+          const uint32_t i = it - 1 - i0;
+          mbar_wait(&empty[i % STAGES], (i / STAGES) & 1, nullptr);
         }
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && (!PAIR || rank == 0)) {
       uint32_t it = 0, tile = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < g.units && ok; u += gridDim.x) {
-        int m;
-        int64_t fb, fe;
-        unit_range(g, u, m, fb, fe);
+      int u, m;
+      int64_t fb, fe;
+      for (int j = 0; ok && unit_at<PAIR>(g, j, rank, u, m, fb, fe); ++j) {
         for (int64_t ft = fb, w = 0; ft < fe && ok; ft += w, ++tile) {
           w = tile_width<NT>(ft, fb, fe);
           const int a = (int)(tile % kAccBufs);
@@ -410,9 +468,11 @@ __global__ void __launch_bounds__(MODE == kModeTF32 ? kFusedThreads + 64 : kFuse
           }
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + (uint32_t)a * kAccCols;
+          const uint32_t mma_m = PAIR ? 256u : 128u;
+          const uint32_t mma_n = PAIR ? (uint32_t)NT : (uint32_t)w;
           const uint32_t idesc = TF32 ? make_idesc_tf32(128u, (uint32_t)w)
-                                 : FP8  ? make_idesc_f16(0u, 128u, (uint32_t)w)  // E4M3 x E4M3
-                                        : make_idesc_f16((uint32_t)p.ab_format, 128u, (uint32_t)w);
+                                 : FP8  ? make_idesc_f16(0u, mma_m, mma_n)  // E4M3 x E4M3
+                                        : make_idesc_f16((uint32_t)p.ab_format, mma_m, mma_n);
           for (int kb = 0; kb < num_kb; ++kb, ++it) {
             const int s = it % STAGES;
             // TF32: the W tile must also have been split by warps 2-3.
@@ -441,16 +501,33 @@ __global__ void __launch_bounds__(MODE == kModeTF32 ? kFusedThreads + 64 : kFuse
                 const uint64_t dw = smem_desc_sw128(sx + Cfg::kSub * Cfg::kXBytes + h * Cfg::kWBytes);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
-                  if constexpr (FP8)
-                    umma_f8(d_tmem, dx + 2 * kk, dw + 2 * kk, idesc, (kb | h | kk) != 0 ? 1u : 0u);
+                  const uint32_t acc = (kb | h | kk) != 0 ? 1u : 0u;
+                  if constexpr (PAIR && FP8)
+                    umma_f8_pair(d_tmem, dx + 2 * kk, dw + 2 * kk, idesc, acc);
+                  else if constexpr (PAIR)
+                    umma_f16_pair(d_tmem, dx + 2 * kk, dw + 2 * kk, idesc, acc);
+                  else if constexpr (FP8)
+                    umma_f8(d_tmem, dx + 2 * kk, dw + 2 * kk, idesc, acc);
                   else
-                    umma_f16(d_tmem, dx + 2 * kk, dw + 2 * kk, idesc, (kb | h | kk) != 0 ? 1u : 0u);
+                    umma_f16(d_tmem, dx + 2 * kk, dw + 2 * kk, idesc, acc);
                 }
               }
             }
-            umma_commit(&empty[s]);
+            if constexpr (PAIR) {
+              umma_commit_pair(smem_u32(&empty[s]));
+              umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 1u));
+            } else {
+              umma_commit(&empty[s]);
+            }
           }
-          if (ok) umma_commit(&acc_full[a]);
+          if (ok) {
+            if constexpr (PAIR) {
+              umma_commit_pair(smem_u32(&acc_full[a]));
+              umma_commit_pair(mapa_shared(smem_u32(&acc_full[a]), 1u));
+            } else {
+              umma_commit(&acc_full[a]);
+            }
+          }
         }
       }
       if (!ok) {
@@ -458,7 +535,10 @@ __global__ void __launch_bounds__(MODE == kModeTF32 ? kFusedThreads + 64 : kFuse
         *abort_flag = 1;
       }
       // Every MMA issued above has completed once this barrier flips.
-      umma_commit(mma_done);
+      if constexpr (PAIR)
+        umma_commit_pair(smem_u32(mma_done));
+      else
+        umma_commit(mma_done);
       mbar_wait(mma_done, 0, nullptr);
     }
     __syncwarp();
@@ -518,8 +598,8 @@ __global__ void __launch_bounds__(MODE == kModeTF32 ? kFusedThreads + 64 : kFuse
     const uint32_t list_s = TOPT ? t_lane + kListCol : top_s;  // where this thread's row list lives
     uint32_t tile = 0;
     bool ok = true;
-    TileWalk<NT> cur;
-    cur.start(g);
+    TileWalk<NT, PAIR> cur;
+    cur.start(g, rank);
     float published = -__int_as_float(0x7f800000);  // this unit's last published threshold
     float bcur[NT / 32], bnext[NT / 32];
     float scur[NT / 32], snext[NT / 32];  // FP8: per-feature scales, like the bias
@@ -528,8 +608,8 @@ __global__ void __launch_bounds__(MODE == kModeTF32 ? kFusedThreads + 64 : kFuse
       if constexpr (FP8) load_bias_tile<NT>(p.w_scale, cur.ft, cur.width(), p.F, lane, scur);
     }
     while (cur.valid(g)) {
-      TileWalk<NT> nxt = cur;
-      nxt.next(g);
+      TileWalk<NT, PAIR> nxt = cur;
+      nxt.next(g, rank);
       if (nxt.valid(g)) {
         load_bias_tile<NT>(p.bias, nxt.ft, nxt.width(), p.F, lane, bnext);
         if constexpr (FP8) load_bias_tile<NT>(p.w_scale, nxt.ft, nxt.width(), p.F, lane, snext);
@@ -630,7 +710,12 @@ __global__ void __launch_bounds__(MODE == kModeTF32 ? kFusedThreads + 64 : kFuse
         if (c == nchunk - 1) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[a]);
+          if (lane == 0) {
+            if (PAIR && rank != 0)
+              mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[a]), 0u));  // the pair's MMA issuer waits on it
+            else
+              mbar_arrive(&acc_empty[a]);
+          }
         }
         const int64_t f = cur.ft + 32 * c;
         const float bl = pick<NT / 32>(bcur, c);
@@ -679,6 +764,16 @@ __global__ void __launch_bounds__(MODE == kModeTF32 ? kFusedThreads + 64 : kFuse
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) {
+    // Neither CTA of a pair frees its TMEM or exits while the other may still
+    // touch its barriers (remote arrivals) or the pair's tensor memory.
+    cluster_sync();
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc_pair(tmem_base, kTmemCols);
+    }
+    return;  // (the host never asks a pair kernel for the in-kernel finish)
+  }
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
@@ -829,6 +924,51 @@ cudaError_t launch_fused(const CUtensorMap& tx, const CUtensorMap& txl, const CU
   return cudaGetLastError();
 }
 
+template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPT, int MODE>
+cudaError_t launch_fused_pair(const CUtensorMap& tx, const CUtensorMap& tw, const FusedParams& p, int grid,
+                              cudaStream_t stream) {
+  static_assert((MODE & kModePair) != 0, "pair variant");
+  using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM, TOPT, true>;
+  auto kern = fused_topk_kernel<L, NT, STAGES, A, APP_SMEM, TOPT, MODE>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kFusedThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, tx, tx, tw, tw, p);
+}
+
+template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPT, int MODE>
+int pair_clusters_max() {
+  using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM, TOPT, true>;
+  auto kern = fused_topk_kernel<L, NT, STAGES, A, APP_SMEM, TOPT, MODE>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) != cudaSuccess)
+    return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2);
+  cfg.blockDim = dim3(kFusedThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) return 0;
+  return n;
+}
+
 __global__ void residual_tf32_kernel(const float* __restrict__ X, float* __restrict__ Xl, int64_t n) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const float x = X[i];
@@ -884,6 +1024,14 @@ STK_FUSED_TF32_CONFIGS(STK_INST_FUSED_TF32)
                                                                    const CUtensorMap&, const CUtensorMap&,     \
                                                                    const FusedParams&, int, cudaStream_t);
 STK_FUSED_FP8_CONFIGS(STK_INST_FUSED_FP8)
+#define STK_INST_FUSED_PAIR(L, NT, S, A, SM, TT)                                                             \
+  template cudaError_t launch_fused_pair<L, NT, S, A, SM, TT, kModeF16 | kModePair>(                          \
+      const CUtensorMap&, const CUtensorMap&, const FusedParams&, int, cudaStream_t);                         \
+  template cudaError_t launch_fused_pair<L, NT, S, A, SM, TT, kModeFP8 | kModePair>(                          \
+      const CUtensorMap&, const CUtensorMap&, const FusedParams&, int, cudaStream_t);                         \
+  template int pair_clusters_max<L, NT, S, A, SM, TT, kModeF16 | kModePair>();                                \
+  template int pair_clusters_max<L, NT, S, A, SM, TT, kModeFP8 | kModePair>();
+STK_FUSED_PAIR_CONFIGS(STK_INST_FUSED_PAIR)
 
 #define STK_INST_SIMT(L)                                                                                         \
   template cudaError_t launch_simt<float, L>(const void*, const void*, const SimtParams&, int, cudaStream_t);   \

@@ -116,10 +116,10 @@ struct SimtParams {
 // NTx64, both K-major 128-byte swizzled), the per-row top lists unless they
 // live in tensor memory (TOPT), the per-row append slots when they live in
 // shared memory (APP_SMEM), then the mbarriers.
-template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPT>
+template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPT, bool PAIR = false>
 struct FusedCfg {
   static constexpr int kXBytes = kRows * 64 * 2;
-  static constexpr int kWBytes = NT * 64 * 2;
+  static constexpr int kWBytes = (PAIR ? NT / 2 : NT) * 64 * 2;  // CTA pairs: each CTA holds half the W tile
   // 64-element K boxes per pipeline stage.  Two (K = 128 per stage: the X
   // boxes, then the W boxes) for the TMEM-list configurations with 128-feature
   // tiles: each stage's handoff (TMA barrier, MMA issue, commit) then carries
@@ -188,6 +188,23 @@ struct SimtCfg {
 constexpr int kModeF16 = 0;   // fp16 / bf16 X and W, kind::f16
 constexpr int kModeTF32 = 1;  // fp32 X and W, 3-pass kind::tf32
 constexpr int kModeFP8 = 2;   // E4M3 X (quantized per row by the library) and W (per-feature scale), kind::f8f6f4
+constexpr int kModePair = 4;  // flag: 2-CTA clusters, tcgen05.mma.cta_group::2 with M = 256 (16-bit or FP8)
+
+// Configurations of the CTA-pair variant (B >= 256 with an even number of
+// 128-row M tiles, several units per CTA): each CTA's stage holds its X boxes
+// and half the W rows, so four 48 KB stages (K = 128) fit beside the append slots.
+#define STK_FUSED_PAIR_CONFIGS(X) \
+  X(128, 128, 4, 32, true, true)
+
+// Launches a pair-variant kernel (MODE includes kModePair) as 2-CTA clusters;
+// grid is even.
+template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPT, int MODE>
+cudaError_t launch_fused_pair(const CUtensorMap& tx, const CUtensorMap& tw, const FusedParams& p, int grid,
+                              cudaStream_t stream);
+// Largest number of 2-CTA clusters of a pair-variant kernel that fit on the
+// device at once (0 if none).
+template <int L, int NT, int STAGES, int A, bool APP_SMEM, bool TOPT, int MODE>
+int pair_clusters_max();
 
 // TF32: X is read through two maps (tx: X itself, txl: its residual
 // X - trunc13(X)); otherwise txl is unused.

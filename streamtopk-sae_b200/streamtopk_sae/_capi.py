@@ -15,7 +15,7 @@ LIB_PATH = os.path.join(_HERE, "libstk_b200.so")
 STK_OK, STK_EINVAL, STK_ECUDA, STK_EDEVICE, STK_ENOSPACE = 0, 1, 2, 3, 4
 STK_F32, STK_F16, STK_BF16, STK_E4M3 = 0, 1, 2, 3
 STK_FLAG_ANY_K, STK_FLAG_ANY_D, STK_FLAG_SIMT, STK_FLAG_NO_PILOT, STK_FLAG_TF32 = 1, 2, 4, 8, 16
-STK_FLAG_SEPARATE_FINISH = 32
+STK_FLAG_SEPARATE_FINISH, STK_FLAG_NO_PAIR = 32, 64
 
 EXPORTS = (
     "stk_version", "stk_last_error", "stk_list_len", "stk_workspace_bytes",

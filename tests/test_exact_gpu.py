@@ -220,6 +220,26 @@ def test_sampled_floor_changes_nothing(B, d, F, k):
         check(V1, I1, Xr, Wr, br, k, RTOL["bf16"])
 
 
+@pytest.mark.parametrize("B,d,F,k,dt", [(1024, 256, 30000, 128, "bf16"), (2048, 512, 20000, 128, "fp16"),
+                                        (1024, 128, 50000, 100, "bf16"), (768, 64, 9000, 128, "bf16")])
+def test_cta_pairs_equal_single_cta(B, d, F, k, dt):
+    """k > 64 with an even number of 128-row M tiles and several units per CTA
+    runs as CTA pairs (tcgen05 cta_group::2, M = 256, each CTA loading half of
+    the W tile): bit-identical to the one-CTA kernel, and right against float64."""
+    from streamtopk_sae import _capi, native
+    X, W, b = oracle.gaussian_inputs(B, d, F, seed=B + d)
+    Xt, Wt, bt, Xr, Wr, br = device_inputs(X, W, b, dt)
+    flags = _capi.STK_FLAG_ANY_K
+    V1, I1 = native.streamtopk_cuda_exact_forward(Xt, Wt, bt, k, flags=flags)
+    V2, I2 = native.streamtopk_cuda_exact_forward(Xt, Wt, bt, k, flags=flags | _capi.STK_FLAG_NO_PAIR)
+    torch.cuda.synchronize()
+    no_device_error()
+    assert torch.equal(V1, V2) and torch.equal(I1, I2)
+    rows = np.array(sorted({0, 1, B // 2, B - 2, B - 1}))
+    rt = torch.from_numpy(rows).cuda()
+    check(V1[rt], I1[rt], Xr[rows], Wr, br, k, RTOL[dt])
+
+
 @pytest.mark.parametrize("B,d,F,k", [(128, 512, 60000, 64), (256, 256, 40000, 32), (200, 128, 30000, 128),
                                      (7, 64, 300, 16), (128, 64, 6000, 128), (1, 64, 100000, 1)])
 def test_fused_finish_equals_separate_finish(B, d, F, k):

@@ -46,7 +46,7 @@ def test_quantize_rows_matches_torch(dtype):
 
 
 @pytest.mark.parametrize("B,d,F,k", [(128, 768, 65536, 32), (128, 2048, 100000, 64), (300, 256, 30000, 128),
-                                     (7, 64, 1000, 16), (128, 512, 20000, 1)])
+                                     (7, 64, 1000, 16), (128, 512, 20000, 1), (1024, 256, 30000, 128)])
 def test_fp8_encode_exact_on_quantized_operands(B, d, F, k):
     import streamtopk_sae as stk
     from streamtopk_sae import fp8
