@@ -117,6 +117,23 @@ STK_API int stk_approx_candidates(const void* X, const void* W, const float* b, 
 STK_API int stk_candidates_workspace_bytes(int64_t B, int64_t d, int64_t F, int64_t c, int dtype, size_t* bytes);
 
 /*
+ * The approximate op with its candidate buffer (reference: ops.py:60-83 with
+ * candidate_buffer, streamtopk_approx.cu:234-291): the final (B, k) result V/I
+ * and each 128-feature tile's top c per row, cand_vals / cand_idxs (B,
+ * ceil(F/128), c) descending, (-FLT_MAX, -1) past a tile's last feature.  For
+ * fp16 / bf16 inputs with c <= 32 one W_enc pass computes both (the fused
+ * kernel's candidate variant); otherwise the candidates pass and the exact
+ * top-k run one after the other.  Buffers 16-byte aligned; workspace from
+ * stk_approx_cand_workspace_bytes (enough for either way).
+ */
+STK_API int stk_approx_cand_workspace_bytes(int64_t B, int64_t d, int64_t F, int64_t k, int64_t c, int dtype,
+                                            size_t* bytes);
+STK_API int stk_approx_forward_cand(const void* X, const void* W, const float* b, float* V, int32_t* I,
+                                    float* cand_vals, int32_t* cand_idxs, int64_t B, int64_t d, int64_t F, int64_t k,
+                                    int64_t c, int dtype, int flags, void* workspace, size_t workspace_bytes,
+                                    void* stream);
+
+/*
  * One F-shard of a multi-GPU encode: per row of this shard, with feature
  * indices offset by `index_offset`, sorted 64-bit keys in keys_out (B, L),
  * L = stk_list_len(k): the shard's exact top k, then further keys of the

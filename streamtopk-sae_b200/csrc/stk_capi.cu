@@ -238,6 +238,7 @@ stk::UnitGrid make_grid(int64_t B, int64_t F, int sms) {
   g.segs = segs;
   g.units = g.m_tiles * segs;
   g.fixed_chunks = 0;
+  g.quantum = 1;
   return g;
 }
 
@@ -249,6 +250,7 @@ stk::UnitGrid make_tile_grid(int64_t B, int64_t F) {
   g.fixed_chunks = 4;
   g.segs = (int)((F + 127) / 128);
   g.units = g.m_tiles * g.segs;
+  g.quantum = 1;
   return g;
 }
 
@@ -269,6 +271,10 @@ struct Plan {
   bool fin_fused;  // the fused kernel finishes the rows itself (all units resident at once)
   bool shared_floor;  // units publish their thresholds per row (several units per CTA, no pilot)
   bool pair;          // CTA pairs (tcgen05 cta_group::2, M = 256): k > 64, an even number of M tiles
+  bool cand;          // approximate op with candidates in one pass (each 128-feature tile's top c)
+  float* cand_vals;   // cand: (B, ceil(F / 128), cand_c) outputs (call data)
+  int32_t* cand_idxs;
+  int cand_c;
   int pitch;       // keys per row list in the partials: L, or L + kAppendMax (sorted tail run, fused finish)
   size_t ws_partials;
   size_t ws_app;
@@ -301,6 +307,10 @@ int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t 
   pl->fp8 = dtype == STK_E4M3;
   pl->x_dtype = dtype;
   pl->w_scale = nullptr;
+  pl->cand = false;
+  pl->cand_vals = nullptr;
+  pl->cand_idxs = nullptr;
+  pl->cand_c = 0;
   pl->tc = ((dtype == STK_BF16 || dtype == STK_F16) && (d % 8 == 0) && !(flags & STK_FLAG_SIMT) && aligned) ||
            pl->tf32 || (pl->fp8 && d % 16 == 0 && aligned);
   pl->grid = make_grid(B, F, sms);
@@ -404,7 +414,7 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
     nslots = 32;
     app_smem = 1;
     topt = 1;
-  } else {
+  } else if (!pl.cand) {
     fused_override(pl.L, &nt, &stages, &nslots, &app_smem, &topt);
   }
   const int w_box = pl.pair ? nt / 2 : nt;  // pairs: each CTA loads half the tile's W rows
@@ -457,6 +467,10 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   p.num_kb = pl.tf32 ? (int)((d + 15) / 16) : pl.fp8 ? (int)((d + 127) / 128) : (int)((d + 63) / 64);
   p.x_scale = x_scale;
   p.w_scale = pl.w_scale;
+  p.cand_vals = pl.cand_vals;
+  p.cand_idxs = pl.cand_idxs;
+  p.cand_tiles = (F + 127) / 128;
+  p.cand_c = pl.cand_c;
   p.ab_format = bf16 ? 1 : 0;
   p.w_evict_first = pl.grid.m_tiles == 1 ? 1 : 0;
   p.index_offset = index_offset;
@@ -503,8 +517,15 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
   }
   STK_FUSED_PAIR_CONFIGS(STK_TRY_FUSED_PAIR)
 #undef STK_TRY_FUSED_PAIR
+#define STK_TRY_FUSED_CAND(Lc, NTc, Sc, Ac, SMc, TTc)                                                 \
+  if (pl.cand && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc &&   \
+      (topt != 0) == TTc)                                                                               \
+    e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, TTc, stk::kModeF16 | stk::kModeCand>(tx, txl, tw, tw32, p, pl.ctas, \
+                                                                                     stream);
+  STK_FUSED_CAND_CONFIGS(STK_TRY_FUSED_CAND)
+#undef STK_TRY_FUSED_CAND
 #define STK_TRY_FUSED(Lc, NTc, Sc, Ac, SMc, TTc)                                                      \
-  if (!pl.pair && !pl.tf32 && !pl.fp8 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc &&  \
+  if (!pl.cand && !pl.pair && !pl.tf32 && !pl.fp8 && pl.L == Lc && nt == NTc && stages == Sc && nslots == Ac && (app_smem != 0) == SMc &&  \
       (topt != 0) == TTc)                                                                               \
     e = stk::launch_fused<Lc, NTc, Sc, Ac, SMc, TTc, stk::kModeF16>(tx, txl, tw, tw32, p, pl.ctas, stream);
   STK_FUSED_CONFIGS(STK_TRY_FUSED)
@@ -757,6 +778,88 @@ int stk_approx_forward(const void* X, const void* W, const float* b, float* V, i
                 static_cast<cudaStream_t>(stream));
 }
 
+}  // extern "C"
+
+extern "C" int candidates_plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t c, int dtype,
+                               Plan* pl);
+
+namespace {
+// Plan of the approximate op with candidates: the exact encode's plan with
+// feature ranges aligned to the reference's 128-feature tiles, and the fused
+// kernel's candidate variant when it applies (16-bit inputs, c <= 32);
+// *single = false means the two-pass fallback (candidates pass, then the
+// exact top-k).
+int cand_plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t k, int64_t c, int dtype,
+              int flags, Plan* pl, bool* single) {
+  int rc = plan(X, W, B, d, F, k, dtype, flags | STK_FLAG_ANY_D, pl);
+  if (rc) return rc;
+  const int64_t nq = (pl->grid.nchunks + 3) / 4;
+  *single = pl->tc && !pl->tf32 && !pl->fp8 && !pl->pair && (dtype == STK_BF16 || dtype == STK_F16) && c <= 32 &&
+            pl->L == 32 && pl->grid.fixed_chunks == 0 && nq >= pl->grid.segs;
+  if (*single) {
+    pl->grid.quantum = 4;
+    pl->cand = true;
+    pl->cand_c = (int)c;
+  }
+  return STK_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int stk_approx_cand_workspace_bytes(int64_t B, int64_t d, int64_t F, int64_t k, int64_t c, int dtype, size_t* bytes) {
+  if (!bytes) return fail(STK_EINVAL, "bytes is NULL");
+  int rc = check_common("stk_approx_cand_workspace_bytes", B, d, F, dtype);
+  if (rc) return rc;
+  if (!(k >= 1 && k <= c) || !(c == 16 || c == 32 || c == 64 || c == 128))
+    return fail(STK_EINVAL, "streamtopk_cuda_approx: need 1 <= k <= c, c in {16,32,64,128}");
+  // Enough for either path (one pass, or candidates then the exact top-k).
+  Plan pl;
+  bool single = false;
+  rc = cand_plan(nullptr, nullptr, B, d, F, k, c, dtype, 0, &pl, &single);
+  if (rc) return rc;
+  Plan pc;
+  rc = candidates_plan(nullptr, nullptr, B, d, F, c, dtype, &pc);
+  if (rc) return rc;
+  Plan pe;
+  rc = plan(nullptr, nullptr, B, d, F, k, dtype, dtype == STK_F32 ? STK_FLAG_TF32 : 0, &pe);
+  if (rc) return rc;
+  *bytes = pl.ws > pc.ws ? pl.ws : pc.ws;
+  if (pe.ws > *bytes) *bytes = pe.ws;
+  return STK_OK;
+}
+
+int stk_approx_forward_cand(const void* X, const void* W, const float* b, float* V, int32_t* I, float* cand_vals,
+                            int32_t* cand_idxs, int64_t B, int64_t d, int64_t F, int64_t k, int64_t c, int dtype,
+                            int flags, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_common("streamtopk_cuda_approx", B, d, F, dtype);
+  if (rc) return rc;
+  if (!(k >= 1 && k <= c)) return fail(STK_EINVAL, "k must be <= c");
+  if (!(c == 16 || c == 32 || c == 64 || c == 128))
+    return fail(STK_EINVAL,
+                "streamtopk_cuda_approx: unsupported c=" + std::to_string(c) + ". Supported: 16,32,64,128.");
+  if (B == 0) return STK_OK;
+  if (!cand_vals || !cand_idxs || !aligned16(cand_vals) || !aligned16(cand_idxs))
+    return fail(STK_EINVAL, "candidate buffers must be non-null and 16-byte aligned");
+  Plan pl;
+  bool single = false;
+  rc = cand_plan(X, W, B, d, F, k, c, dtype, flags, &pl, &single);
+  if (rc) return rc;
+  if (!single) {
+    // Two passes: the per-tile candidates, then the exact top-k (equal to the
+    // approximate result for k <= c).
+    rc = stk_approx_candidates(X, W, b, cand_vals, cand_idxs, B, d, F, c, dtype, workspace, workspace_bytes, stream);
+    if (rc) return rc;
+    return stk_approx_forward(X, W, b, V, I, B, d, F, k, c, dtype, flags, workspace, workspace_bytes, stream);
+  }
+  pl.cand_vals = cand_vals;
+  pl.cand_idxs = cand_idxs;
+  if (workspace_bytes < pl.ws || (pl.ws && workspace == nullptr))
+    return fail(STK_ENOSPACE, "workspace too small (need " + std::to_string(pl.ws) + " bytes)");
+  return score_and_finish(pl, X, W, b, V, I, nullptr, B, d, F, k, dtype, 0u, nullptr, workspace,
+                          static_cast<cudaStream_t>(stream));
+}
+
 int stk_shard_forward(const void* X, const void* W_shard, const float* b_shard, uint64_t* keys_out, int64_t B,
                       int64_t d, int64_t F_shard, int64_t k, int64_t index_offset, int dtype, int flags,
                       void* workspace, size_t workspace_bytes, void* stream) {
@@ -797,6 +900,10 @@ int candidates_plan(const void* X, const void* W, int64_t B, int64_t d, int64_t 
   pl->pilot = false;
   pl->shared_floor = false;  // each tile's own top c, not the row's top k
   pl->pair = false;
+  pl->cand = false;
+  pl->cand_vals = nullptr;
+  pl->cand_idxs = nullptr;
+  pl->cand_c = 0;
   pl->fp8 = false;
   pl->x_dtype = dtype;
   pl->w_scale = nullptr;

@@ -745,6 +745,26 @@ struct RowTopK {
     }
   }
 
+  // Offer keys[0..n) of a descending array (n <= N, n <= A): the ones above
+  // the threshold form a prefix.  Warp-wide like offer().
+  template <int N>
+  __device__ __forceinline__ void offer_sorted(const uint64_t (&keys)[N], int n) {
+    int s = 0;
+#pragma unroll
+    for (int j = 0; j < N; ++j) s += (j < n && keys[j] != kEmptyKey && key_value(keys[j]) > thr) ? 1 : 0;
+    if (__any_sync(0xffffffffu, cnt + s > A)) {
+      flush();
+      s = 0;
+#pragma unroll
+      for (int j = 0; j < N; ++j) s += (j < n && keys[j] != kEmptyKey && key_value(keys[j]) > thr) ? 1 : 0;
+    }
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      if (!__any_sync(0xffffffffu, j < s)) break;
+      if (j < s) push(keys[j]);
+    }
+  }
+
   // Raise the filter to a lower bound of the row's k-th score obtained from a
   // sample (scores strictly below `lb` can never be in the row's top-k).
   __device__ __forceinline__ void set_floor(float lb) {

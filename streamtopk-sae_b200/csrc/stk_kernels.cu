@@ -37,9 +37,11 @@ namespace stk {
 __device__ __forceinline__ void unit_range(const UnitGrid& g, int u, int& m, int64_t& f_begin, int64_t& f_end) {
   const int seg = u / g.m_tiles;
   m = u - seg * g.m_tiles;
-  const int64_t c0 = g.fixed_chunks > 0 ? (int64_t)seg * g.fixed_chunks : (int64_t)seg * g.nchunks / g.segs;
+  const int64_t q = g.quantum > 1 ? g.quantum : 1;  // balanced bounds in multiples of q chunks
+  const int64_t nq = (g.nchunks + q - 1) / q;
+  const int64_t c0 = g.fixed_chunks > 0 ? (int64_t)seg * g.fixed_chunks : q * ((int64_t)seg * nq / g.segs);
   const int64_t c1 = g.fixed_chunks > 0 ? min(c0 + g.fixed_chunks, g.nchunks)
-                                        : (int64_t)(seg + 1) * g.nchunks / g.segs;
+                                        : min(q * ((int64_t)(seg + 1) * nq / g.segs), g.nchunks);
   f_begin = c0 * 32;
   f_end = c1 * 32;  // may pass F by < 32 on the last range; masked in the epilogue
 }
@@ -303,6 +305,8 @@ __global__ void __launch_bounds__((MODE & 3) == kModeTF32 ? kFusedThreads + 64 :
   using Cfg = FusedCfg<L, NT, STAGES, A, APP_SMEM, TOPT, PAIR>;
   constexpr bool TF32 = (MODE & 3) == kModeTF32;
   constexpr bool FP8 = (MODE & 3) == kModeFP8;
+  constexpr bool CAND = (MODE & kModeCand) != 0;
+  static_assert(!CAND || (!PAIR && !TF32 && !FP8 && !TOPT && L == 32), "candidate variant: 16-bit, k <= c <= 32");
   static_assert(!PAIR || (!TF32 && NT % 32 == 0), "CTA pairs: 16-bit or FP8 operands");
   constexpr int kSplitThreads = 64;                 // warps 2-3 (TF32)
   constexpr int kFirstEpiWarp = TF32 ? 4 : 2;
@@ -641,6 +645,8 @@ __global__ void __launch_bounds__((MODE & 3) == kModeTF32 ? kFusedThreads + 64 :
       tc_fence_after();
       const int nchunk = w / 32;
       const uint32_t tcol = t_lane + (uint32_t)a * kAccCols;
+      uint64_t run[CAND ? 32 : 1];  // kModeCand: the current 128-feature tile's best 32 keys
+      (void)run;
       // Shared floor: the best lower bound of this row's k-th score that the
       // other units of this M tile published so far (read now, applied after
       // the tile, so the load's latency hides behind the chunks).
@@ -724,7 +730,52 @@ __global__ void __launch_bounds__((MODE & 3) == kModeTF32 ? kFusedThreads + 64 :
 #pragma unroll
         for (int j = 0; j < 32; ++j) vals[j] = chunk_score<FP8>(v[j], bl, sl, sxr, j);
         const uint32_t valid = row_ok ? feature_mask(f, p.F) : 0u;
-        acc.offer(vals, p.index_offset + (uint32_t)f, valid);
+        if constexpr (CAND) {
+          // The 128-feature tile's top c (the reference's per-tile candidates,
+          // streamtopk_approx.cu:42-167): this chunk's 32 keys sorted, merged
+          // into the tile's running best 32 (bitonic merge of two descending
+          // runs); at the tile's end written out, and its best min(c, k)
+          // offered to the row's top-k (which only they can enter: k <= c).
+          uint64_t kc[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            kc[j] = ((valid >> j) & 1u) ? make_key(vals[j], p.index_offset + (uint32_t)f + (uint32_t)j) : kEmptyKey;
+          sort_desc<32>(kc);
+          if ((c & 3) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) run[j] = kc[j];
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) run[j] = kmax(run[j], kc[31 - j]);
+            merge_desc<32>(run);
+          }
+          if ((c & 3) == 3 || c == nchunk - 1) {
+            if (row_ok) {
+              const int64_t t = (cur.ft + 32 * (c & ~3)) / 128;
+              const int64_t o = (((int64_t)cur.m * kRows + r) * p.cand_tiles + t) * p.cand_c;
+              float4* vo = reinterpret_cast<float4*>(p.cand_vals + o);
+              int4* io = reinterpret_cast<int4*>(p.cand_idxs + o);
+#pragma unroll
+              for (int q4 = 0; q4 < 8; ++q4) {
+                if (4 * q4 < p.cand_c) {
+                  float vv[4];
+                  int ii[4];
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    const uint64_t kk = run[4 * q4 + e];
+                    vv[e] = kk ? key_value(kk) : -3.402823466e+38f;
+                    ii[e] = kk ? key_index(kk) : -1;
+                  }
+                  vo[q4] = make_float4(vv[0], vv[1], vv[2], vv[3]);
+                  io[q4] = make_int4(ii[0], ii[1], ii[2], ii[3]);
+                }
+              }
+            }
+            acc.offer_sorted(run, min(p.cand_c, p.k));
+          }
+        } else {
+          acc.offer(vals, p.index_offset + (uint32_t)f, valid);
+        }
       }
       if (p.row_floor != nullptr && row_ok) {
         // A unit's threshold is the k-th best of k real scores of the row (or
@@ -1024,6 +1075,11 @@ STK_FUSED_TF32_CONFIGS(STK_INST_FUSED_TF32)
                                                                    const CUtensorMap&, const CUtensorMap&,     \
                                                                    const FusedParams&, int, cudaStream_t);
 STK_FUSED_FP8_CONFIGS(STK_INST_FUSED_FP8)
+#define STK_INST_FUSED_CAND(L, NT, S, A, SM, TT)                                                             \
+  template cudaError_t launch_fused<L, NT, S, A, SM, TT, kModeF16 | kModeCand>(                               \
+      const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const FusedParams&, int,  \
+      cudaStream_t);
+STK_FUSED_CAND_CONFIGS(STK_INST_FUSED_CAND)
 #define STK_INST_FUSED_PAIR(L, NT, S, A, SM, TT)                                                             \
   template cudaError_t launch_fused_pair<L, NT, S, A, SM, TT, kModeF16 | kModePair>(                          \
       const CUtensorMap&, const CUtensorMap&, const FusedParams&, int, cudaStream_t);                         \

@@ -21,6 +21,7 @@ struct UnitGrid {
   int units;        // m_tiles * segs
   int64_t nchunks;  // ceil(F / 32)
   int fixed_chunks; // > 0: range s is chunks [s*fixed_chunks, (s+1)*fixed_chunks); 0: balanced split
+  int quantum;      // balanced split: range bounds are multiples of quantum chunks (1, or 4 = 128 features)
 };
 
 // Per-CTA global append buffers (configurations whose append slots do not fit
@@ -98,6 +99,10 @@ struct FusedParams {
   int w_evict_first;   // W is read once (single M tile): stream it past L2
   uint32_t index_offset;
   int pilot_chunks;    // sampled 32-feature chunks per CTA (<= the first tile's chunks)
+  float* cand_vals;      // kModeCand: (B, cand_tiles, cand_c) per-tile top-c values (-FLT_MAX padding)
+  int32_t* cand_idxs;    // kModeCand: their feature indices (-1 padding)
+  int64_t cand_tiles;    // ceil(F / 128)
+  int cand_c;            // 16 or 32
   const float* x_scale;  // FP8: [B] per-row dequantization scale of X
   const float* w_scale;  // FP8: [F] per-feature dequantization scale of W (scores = x_s * w_s * acc + b)
 };
@@ -189,6 +194,12 @@ constexpr int kModeF16 = 0;   // fp16 / bf16 X and W, kind::f16
 constexpr int kModeTF32 = 1;  // fp32 X and W, 3-pass kind::tf32
 constexpr int kModeFP8 = 2;   // E4M3 X (quantized per row by the library) and W (per-feature scale), kind::f8f6f4
 constexpr int kModePair = 4;  // flag: 2-CTA clusters, tcgen05.mma.cta_group::2 with M = 256 (16-bit or FP8)
+constexpr int kModeCand = 8;  // flag: also write each 128-feature tile's top c (c <= 32) per row (approx op)
+
+// Configurations of the candidate variant (16-bit inputs, k <= c <= 32).
+#define STK_FUSED_CAND_CONFIGS(X)    \
+  X(32, 256, 3, 32, true, false)    \
+  X(32, 128, 5, 32, true, false)
 
 // Configurations of the CTA-pair variant (B >= 256 with an even number of
 // 128-row M tiles, several units per CTA): each CTA's stage holds its X boxes

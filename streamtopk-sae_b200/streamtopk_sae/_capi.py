@@ -25,6 +25,7 @@ EXPORTS = (
     "stk_exchange_bytes", "stk_exchange_create", "stk_exchange_ipc_handle", "stk_exchange_connect",
     "stk_exchange_forward", "stk_exchange_destroy",
     "stk_workspace_bytes_fp8", "stk_exact_forward_fp8", "stk_quantize_rows_fp8",
+    "stk_approx_cand_workspace_bytes", "stk_approx_forward_cand",
 )
 IPC_HANDLE_BYTES = 64
 
@@ -96,6 +97,11 @@ def load():
         L.stk_exact_forward_fp8.argtypes = [vp, i32, vp, vp, vp, vp, vp, i64, i64, i64, i64, i32, vp, sz, vp]
         L.stk_quantize_rows_fp8.restype = i32
         L.stk_quantize_rows_fp8.argtypes = [vp, i32, vp, vp, i64, i64, vp]
+        L.stk_approx_cand_workspace_bytes.restype = i32
+        L.stk_approx_cand_workspace_bytes.argtypes = [i64, i64, i64, i64, i64, i32, ctypes.POINTER(sz)]
+        L.stk_approx_forward_cand.restype = i32
+        L.stk_approx_forward_cand.argtypes = [vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32, vp, sz,
+                                              vp]
         _lib = L
     return _lib
 
@@ -116,6 +122,12 @@ def workspace_bytes(B: int, d: int, F: int, k: int, dtype_code: int) -> int:
 def workspace_bytes_fp8(B: int, d: int, F: int, k: int) -> int:
     out = ctypes.c_size_t(0)
     check(load().stk_workspace_bytes_fp8(B, d, F, k, ctypes.byref(out)))
+    return int(out.value)
+
+
+def approx_cand_workspace_bytes(B: int, d: int, F: int, k: int, c: int, dtype_code: int) -> int:
+    out = ctypes.c_size_t(0)
+    check(load().stk_approx_cand_workspace_bytes(B, d, F, k, c, dtype_code, ctypes.byref(out)))
     return int(out.value)
 
 

@@ -87,6 +87,28 @@ def approx_topk_forward(X, W_enc, b_enc, k, c, flags=0):
     return V, I
 
 
+def approx_forward_with_candidates(X, W_enc, b_enc, k, c, cand_vals, cand_idxs, flags=0):
+    """Final (B, k) result of the approximate path and, into cand_vals /
+    cand_idxs (B, ceil(F/128), c), each 128-feature tile's top c
+    (stk_approx_forward_cand: one W_enc pass for fp16 / bf16 with c <= 32)."""
+    B, d, F = _common_checks(X, W_enc, b_enc, check_w_b_cuda=False)
+    k, c = int(k), int(c)
+    _require(1 <= k <= c, "k must be <= c")
+    _require(c in (16, 32, 64, 128), f"streamtopk_cuda_approx: unsupported c={c}. Supported: 16,32,64,128.")
+    _require(W_enc.is_cuda and b_enc.is_cuda, "W_enc and b_enc must be on CUDA")
+    V = torch.empty((B, k), dtype=torch.float32, device=X.device)
+    I = torch.empty((B, k), dtype=torch.int32, device=X.device)
+    lib = _capi.load()
+    with torch.cuda.device(X.device):
+        nbytes = _capi.approx_cand_workspace_bytes(B, d, F, k, c, _DTYPE_CODE[X.dtype])
+        ws = torch.empty(max(nbytes, 8), dtype=torch.uint8, device=X.device)
+        stream = torch.cuda.current_stream(X.device).cuda_stream
+        _capi.check(lib.stk_approx_forward_cand(X.data_ptr(), W_enc.data_ptr(), b_enc.data_ptr(), V.data_ptr(),
+                                                I.data_ptr(), cand_vals.data_ptr(), cand_idxs.data_ptr(), B, d, F, k,
+                                                c, _DTYPE_CODE[X.dtype], flags, ws.data_ptr(), nbytes, stream))
+    return V, I
+
+
 def streamtopk_cuda_approx_forward(X, W_enc, b_enc, k, c, candidate_buffer=None):
     """Reference: streamtopk_sae/csrc/cuda/streamtopk_approx.cu:234-291.
 

@@ -62,13 +62,23 @@ def topk_sae_cuda_approx(X, W_enc, b_enc, k, c, candidate_buffer=None, *, allow_
     final top-k runs on the GPU inside the library instead of a torch.topk over
     (B, ceil(F/128)*c) candidates.  If ``candidate_buffer`` (B, ceil(F/128), c)
     fp32 is given, it is filled with the per-tile candidate values, as the
-    reference does.
+    reference does -- for fp16 / bf16 with c <= 32 in the same W_enc pass as
+    the top-k (one kernel), otherwise by a candidates pass first.
     Returns: values (B, k) fp32 (descending), indices (B, k) int32.
     """
     _check_native()
     X, W_enc, b_enc = _prepare(X, W_enc, b_enc)
     if candidate_buffer is not None:
-        native.streamtopk_cuda_approx_forward(X, W_enc, b_enc, k, c, candidate_buffer)
+        B, F = X.shape[0], W_enc.shape[0]
+        tiles = (F + native.T_APPROX - 1) // native.T_APPROX
+        cb = candidate_buffer
+        if not (cb.dim() == 3 and tuple(cb.shape) == (B, tiles, int(c))):
+            raise RuntimeError("candidate_buffer shape mismatch")
+        if not (cb.dtype == torch.float32 and cb.is_contiguous() and cb.device == X.device):
+            raise RuntimeError("candidate_buffer must be a contiguous fp32 tensor on X's device")
+        idxs = torch.empty(cb.shape, dtype=torch.int32, device=X.device)
+        return native.approx_forward_with_candidates(X, W_enc, b_enc, k, c, cb, idxs,
+                                                     flags=_flags(allow_any_k, True))
     return native.approx_topk_forward(X, W_enc, b_enc, k, c, flags=_flags(allow_any_k, True))
 
 

@@ -127,3 +127,26 @@ def test_approx_argument_errors():
         stk.topk_sae_cuda_approx(X, W, b, 32, 16)
     with pytest.raises(RuntimeError, match="unsupported c=24"):
         stk.topk_sae_cuda_approx(X, W, b, 8, 24)
+
+
+@pytest.mark.parametrize("B,d,F,k,c", [(128, 512, 100000, 32, 32), (128, 256, 60037, 16, 16),
+                                       (300, 256, 40000, 8, 32), (64, 128, 20000, 32, 32)])
+def test_candidates_single_pass_equals_two_pass(B, d, F, k, c):
+    """With fp16 / bf16 and c <= 32 the approximate op with a candidate buffer
+    is one W_enc pass (the fused kernel also writes each tile's top c): its
+    candidates equal the separate candidates pass bit for bit, and its top-k
+    the exact op's (k <= c)."""
+    import streamtopk_sae as stk
+    from streamtopk_sae import native
+    X, W, b = oracle.gaussian_inputs(B, d, F, seed=F + c)
+    Xt, Wt, bt, *_ = device_inputs(X, W, b, "bf16")
+    T = (F + 127) // 128
+    cv = torch.empty(B, T, c, device="cuda")
+    ci = torch.empty(B, T, c, dtype=torch.int32, device="cuda")
+    V1, I1 = native.approx_forward_with_candidates(Xt, Wt, bt, k, c, cv, ci)
+    _, _, cv2, ci2 = native.streamtopk_cuda_approx_forward(Xt, Wt, bt, k, c)
+    Ve, Ie = stk.topk_sae_cuda_exact(Xt, Wt, bt, k)
+    torch.cuda.synchronize()
+    no_device_error()
+    assert torch.equal(cv, cv2) and torch.equal(ci, ci2)
+    assert torch.equal(V1, Ve) and torch.equal(I1, Ie)
