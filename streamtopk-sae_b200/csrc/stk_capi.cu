@@ -278,7 +278,7 @@ struct Plan {
   int pitch;       // keys per row list in the partials: L, or L + kAppendMax (sorted tail run, fused finish)
   size_t ws_partials;
   size_t ws_app;
-  size_t ws_sync;   // zeroed per call: barrier counters, then the pilot histogram and row maxima
+  size_t ws_sync;   // zeroed per call: barrier counters, then the pilot histogram or the shared row floor
   size_t ws_split;  // TF32: X's residual X - trunc13(X), 256-byte aligned
   size_t ws_q;      // fp8: X quantized (B x d bytes, 256-aligned), then its row scales
   size_t ws;
@@ -331,7 +331,7 @@ int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t 
     }
   }
   // partial lists, then one append buffer per CTA, then (optionally) the
-  // pilot histogram, row maxima and arrival counter (256-byte aligned parts)
+  // pilot histogram and arrival counters (256-byte aligned parts)
   pl->ws_app = ((size_t)pl->ctas * stk::kAppendBytesPerCta + 255) & ~size_t(255);
   // The sample step needs one unit per CTA (all CTAs resident together) and
   // pays off when each CTA streams several chunks after its sample.
@@ -350,7 +350,7 @@ int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t 
   // must hold each tile's own top c.
   pl->shared_floor = pl->tc && !pl->pilot && pl->grid.units > pl->ctas && pl->grid.fixed_chunks == 0 &&
                      !(flags & STK_FLAG_NO_PILOT);
-  const size_t pilot_bytes = pl->pilot ? (size_t)pl->grid.m_tiles * stk::kRows * (stk::kPilotBins + 1) * 4 : 0;
+  const size_t pilot_bytes = pl->pilot ? (size_t)pl->grid.m_tiles * stk::kRows * stk::kPilotBins * 4 : 0;
   const size_t floor_bytes = pl->shared_floor ? (size_t)pl->grid.m_tiles * stk::kRows * 4 : 0;
   pl->ws_sync = (pl->pilot || pl->fin_fused || pl->shared_floor)
                     ? ((kSyncBytes + pilot_bytes + floor_bytes + 255) & ~size_t(255))
@@ -480,7 +480,6 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
     if (v >= 1 && v <= 8) p.pilot_chunks = v;
   }
   p.pilot_hist = nullptr;
-  p.pilot_rowmax = nullptr;
   p.pilot_count = nullptr;
   p.tail_count = nullptr;
   p.row_floor = nullptr;
@@ -493,7 +492,6 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
     p.tail_count = p.pilot_count + 1;
     if (pl.pilot) {
       p.pilot_hist = reinterpret_cast<uint32_t*>(base + kSyncBytes);
-      p.pilot_rowmax = p.pilot_hist + (size_t)pl.grid.m_tiles * stk::kRows * stk::kPilotBins;
     }
     if (pl.shared_floor) p.row_floor = reinterpret_cast<uint32_t*>(base + kSyncBytes);
     cudaError_t me = cudaMemsetAsync(base, 0, pl.ws_sync, stream);

@@ -686,7 +686,6 @@ __global__ void __launch_bounds__((MODE & 3) == kModeTF32 ? kFusedThreads + 64 :
           }
           any |= valid != 0u;
         }
-        if (any) atomicMax(p.pilot_rowmax + (size_t)cur.m * kRows + r, bmax);
         __threadfence();
         epilogue_bar();
         if (warp == kFirstEpiWarp && lane == 0) {
@@ -703,8 +702,13 @@ __global__ void __launch_bounds__((MODE & 3) == kModeTF32 ? kFusedThreads + 64 :
           *pilot_flag = ok_all;
         }
         epilogue_bar();
-        if (*pilot_flag && row_ok) {
-          const uint32_t tb = __ldcg(p.pilot_rowmax + (size_t)cur.m * kRows + r);
+        if (*pilot_flag && row_ok && any) {
+          // The histogram window is anchored kPilotTopSlack bins (one octave)
+          // above this CTA's own highest sampled bin instead of at the row's
+          // global one (which would cost another memory round trip after the
+          // barrier).  Counts above the window, if any, are only left out of
+          // the count from the top, which makes the bound lower: still valid.
+          const uint32_t tb = min(bmax + kPilotTopSlack, (uint32_t)(kPilotBins - 1));
           float lb;
           if (pilot_bound(h, tb, p.k, lb)) acc.set_floor(lb);
         }

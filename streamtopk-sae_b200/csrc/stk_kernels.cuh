@@ -37,6 +37,7 @@ constexpr int kPilotBits = 12;
 constexpr int kPilotChunks = 2;  // default sampled 32-feature chunks per CTA
 constexpr int kPilotGroup = 8;   // scores per histogrammed group maximum
 constexpr int kPilotBins = 1 << kPilotBits;
+constexpr uint32_t kPilotTopSlack = 8;  // bins (one octave) the bound's window reaches above a CTA's own top
 constexpr unsigned long long kPilotWaitNs = 200000;  // give up (no floor) after 200 us
 
 // Direct GPU-to-GPU exchange of per-rank key lists (F-sharded encode, one
@@ -84,7 +85,6 @@ struct FusedParams {
   uint64_t* partials;  // [units][128][L] keys
   uint64_t* app;       // [gridDim.x][kAppendMax][128] keys (global append slots)
   uint32_t* pilot_hist;    // [m_tiles][128][kPilotBins] counts, zeroed by the host; null = no pilot
-  uint32_t* pilot_rowmax;  // [m_tiles][128] highest bin seen per row
   uint32_t* pilot_count;   // CTAs that finished their sample
   uint32_t* tail_count;    // CTAs whose lists are stored (finish barrier); zeroed by the host
   uint32_t* row_floor;     // [m_tiles][128] shared lower bound of each row's k-th score (float_order; 0 =
