@@ -637,29 +637,43 @@ __device__ __forceinline__ float pick32(const float (&vals)[32], int j) {
 // The n (<= A) unsorted append slots of row r, sorted descending and padded
 // with empty keys to kAppendMax keys, stored at dst (16-byte aligned).  Out of
 // line like merge_survivors: it runs once per unit.
+// The first S slots sorted (S >= n), the rest of the run empty.
+template <int S, int A, bool APP_SMEM>
+__device__ __forceinline__ void sort_tail_run(uint32_t app_off, const uint64_t* __restrict__ app_g, int r, int n,
+                                              ulonglong2* __restrict__ d) {
+  uint64_t a[S];
+#pragma unroll
+  for (int s = 0; s < S; ++s) {
+    if constexpr (APP_SMEM)
+      a[s] = (s < n) ? smem_keys(app_off)[s * kRows + r] : kEmptyKey;
+    else
+      a[s] = (s < n) ? (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(app_g + s * kRows + r))
+                     : kEmptyKey;
+  }
+  sort_desc<S>(a);
+#pragma unroll
+  for (int i = 0; i < S / 2; ++i) d[i] = make_ulonglong2(a[2 * i], a[2 * i + 1]);
+#pragma unroll
+  for (int i = S / 2; i < kAppendMax / 2; ++i) d[i] = make_ulonglong2(0ull, 0ull);
+}
+
 template <int A, bool APP_SMEM>
 __device__ __noinline__ void store_sorted_tail(uint32_t app_off, const uint64_t* __restrict__ app_g, int r, int n,
                                                uint64_t* __restrict__ dst) {
   ulonglong2* d = reinterpret_cast<ulonglong2*>(dst);
-  if (n > 0) {
-    uint64_t a[A];
+  // The network's size follows the warp's largest count (usually a few keys
+  // are pending at a unit's end): 8 keys cost 24 compare-exchanges, A = 32
+  // cost 240.  Warp-uniform, so no lane diverges.
+  int nmax = n;
 #pragma unroll
-    for (int s = 0; s < A; ++s) {
-      if constexpr (APP_SMEM)
-        a[s] = (s < n) ? smem_keys(app_off)[s * kRows + r] : kEmptyKey;
-      else
-        a[s] = (s < n) ? (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(app_g + s * kRows + r))
-                       : kEmptyKey;
-    }
-    sort_desc<A>(a);
-#pragma unroll
-    for (int i = 0; i < A / 2; ++i) d[i] = make_ulonglong2(a[2 * i], a[2 * i + 1]);
+  for (int o = 16; o > 0; o >>= 1) nmax = max(nmax, __shfl_xor_sync(0xffffffffu, nmax, o));
+  if (nmax <= 8) {
+    sort_tail_run<8, A, APP_SMEM>(app_off, app_g, r, n, d);
+  } else if (A > 16 && nmax > 16) {
+    sort_tail_run<(A > 16 ? A : 16), A, APP_SMEM>(app_off, app_g, r, n, d);
   } else {
-#pragma unroll
-    for (int i = 0; i < A / 2; ++i) d[i] = make_ulonglong2(0ull, 0ull);
+    sort_tail_run<16, A, APP_SMEM>(app_off, app_g, r, n, d);
   }
-#pragma unroll
-  for (int i = A / 2; i < kAppendMax / 2; ++i) d[i] = make_ulonglong2(0ull, 0ull);
 }
 
 template <int L, int A, bool APP_SMEM, bool TOPT = false>
