@@ -204,6 +204,19 @@ STK_API int stk_quantize_rows_fp8(const void* X, int x_dtype, void* Q, float* sc
                                   void* stream);
 
 /*
+ * SAE decoder over the encoder's output (no counterpart in the reference,
+ * which stops at the encoder, README.md:9-14; the next step of an SAE forward):
+ *     out[b][:] = b_dec[:] + sum_j V[b][j] * W_dec[I[b][j]][:]
+ * V (B, k) fp32 and I (B, k) int32 as stk_exact_forward returns them (entries
+ * with I < 0 or I >= F are skipped), W_dec (F, d) in dtype, b_dec (d,) fp32 or
+ * NULL, out (B, d) fp32.  A gather-GEMM: B * k rows of W_dec read once each
+ * (fp32 accumulation), never the dense (B, F) codes.  1 <= k <= 1024; d % 8 == 0
+ * for fp16 / bf16 W_dec (d % 4 for fp32); W_dec, b_dec, out 16-byte aligned.
+ */
+STK_API int stk_decode_forward(const float* V, const int32_t* I, const void* W_dec, const float* b_dec, float* out,
+                               int64_t B, int64_t k, int64_t F, int64_t d, int dtype, void* stream);
+
+/*
  * Direct GPU-to-GPU exchange for the F-sharded encode (no counterpart in the
  * reference, which is single-GPU; the F-sharding follows the multi-GPU scheme
  * of the hot path: shard W_enc / b_enc along F, exchange each rank's per-row

@@ -956,6 +956,28 @@ int stk_approx_candidates(const void* X, const void* W, const float* b, float* c
   return STK_OK;
 }
 
+int stk_decode_forward(const float* V, const int32_t* I, const void* W_dec, const float* b_dec, float* out, int64_t B,
+                       int64_t k, int64_t F, int64_t d, int dtype, void* stream) {
+  if (dtype != STK_F32 && dtype != STK_F16 && dtype != STK_BF16)
+    return fail(STK_EINVAL, "stk_decode_forward: W_dec dtype must be fp32, fp16, or bf16");
+  if (B < 0 || d < 1 || F < 1 || k < 1 || k > 1024)
+    return fail(STK_EINVAL, "stk_decode_forward: need B >= 0, d >= 1, F >= 1 and 1 <= k <= 1024");
+  if (F > 0x7fffffffLL) return fail(STK_EINVAL, "stk_decode_forward: F must fit int32 indices");
+  if (d % (dtype == STK_F32 ? 4 : 8) != 0)
+    return fail(STK_EINVAL, "stk_decode_forward: d must be a multiple of 8 (fp16/bf16) or 4 (fp32)");
+  if (B == 0) return STK_OK;
+  if (!V || !I || !W_dec || !out || !aligned16(W_dec) || !aligned16(out) || (b_dec && !aligned16(b_dec)))
+    return fail(STK_EINVAL, "stk_decode_forward: null or unaligned (16-byte) pointer");
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaErrorInvalidValue;
+  if (dtype == STK_F32) e = stk::launch_decode(V, I, static_cast<const float*>(W_dec), b_dec, out, B, (int)k, F, d, s);
+  if (dtype == STK_F16) e = stk::launch_decode(V, I, static_cast<const __half*>(W_dec), b_dec, out, B, (int)k, F, d, s);
+  if (dtype == STK_BF16)
+    e = stk::launch_decode(V, I, static_cast<const __nv_bfloat16*>(W_dec), b_dec, out, B, (int)k, F, d, s);
+  if (e != cudaSuccess) return cuda_fail(e, "decode_kernel launch");
+  return STK_OK;
+}
+
 int stk_profile_begin(int64_t max_launches) {
   if (max_launches < 1) return fail(STK_EINVAL, "max_launches must be >= 1");
   std::lock_guard<std::mutex> lk(g_prof.mu);

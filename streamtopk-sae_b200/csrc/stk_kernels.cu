@@ -1240,6 +1240,139 @@ cudaError_t launch_candidates_out(const uint64_t* partials, int L, int m_tiles, 
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Decoder gather-GEMM (the consumer of (V, I)): one CTA per (row, slice of
+// 8 x kDecThreads features of d); each thread owns 8 consecutive outputs and
+// walks the row's k codes, loading 16 bytes of the selected W_dec row per
+// code -- coalesced across the CTA -- with four codes in flight at a time.
+// The row's codes are staged in shared memory.  HBM-bound: B * k * d *
+// sizeof(T) gathered bytes (rows repeated across the batch hit in L2).
+// (Splitting a row's codes over four thread groups with a shared-memory sum
+// measured slower at B = 4096.)
+// ---------------------------------------------------------------------------
+constexpr int kDecThreads = 128;
+constexpr int kDecMaxK = 1024;
+
+template <typename T>
+__device__ __forceinline__ void dec_load8(const T* __restrict__ p, float (&w)[8]);
+template <>
+__device__ __forceinline__ void dec_load8<__nv_bfloat16>(const __nv_bfloat16* __restrict__ p, float (&w)[8]) {
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    w[2 * i] = __uint_as_float(q[i] << 16);
+    w[2 * i + 1] = __uint_as_float(q[i] & 0xffff0000u);
+  }
+}
+template <>
+__device__ __forceinline__ void dec_load8<__half>(const __half* __restrict__ p, float (&w)[8]) {
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    w[2 * i] = f.x;
+    w[2 * i + 1] = f.y;
+  }
+}
+template <>
+__device__ __forceinline__ void dec_load8<float>(const float* __restrict__ p, float (&w)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  const float4 c = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+  w[4] = c.x; w[5] = c.y; w[6] = c.z; w[7] = c.w;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kDecThreads) decode_kernel(const float* __restrict__ V, const int32_t* __restrict__ I,
+                                                             const T* __restrict__ W, const float* __restrict__ bias,
+                                                             float* __restrict__ out, int64_t B, int k, int64_t F,
+                                                             int64_t d) {
+  __shared__ float sv[kDecMaxK];
+  __shared__ int32_t si[kDecMaxK];
+  const int64_t col = ((int64_t)blockIdx.x * kDecThreads + threadIdx.x) * 8;
+  const bool active = col < d;
+  const bool full = col + 8 <= d;
+  for (int64_t b = blockIdx.y; b < B; b += gridDim.y) {
+    __syncthreads();  // the previous row's codes are no longer read
+    for (int j = threadIdx.x; j < k; j += blockDim.x) {
+      const int32_t ix = I[b * k + j];
+      const bool ok = ix >= 0 && (int64_t)ix < F;
+      sv[j] = ok ? V[b * k + j] : 0.f;
+      si[j] = ok ? ix : -1;
+    }
+    __syncthreads();
+    if (!active) continue;
+    float acc[8];
+    if (bias != nullptr && full) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(bias + col));
+      const float4 c = __ldg(reinterpret_cast<const float4*>(bias + col) + 1);
+      acc[0] = a.x; acc[1] = a.y; acc[2] = a.z; acc[3] = a.w;
+      acc[4] = c.x; acc[5] = c.y; acc[6] = c.z; acc[7] = c.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = (bias != nullptr && col + e < d) ? bias[col + e] : 0.f;
+    }
+    int j = 0;
+    if (full) {
+      for (; j + 4 <= k; j += 4) {
+        float w[4][8];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int32_t ix = si[j + q];
+          if (ix >= 0) {
+            dec_load8<T>(W + (int64_t)ix * d + col, w[q]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) w[q][e] = 0.f;
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] = fmaf(sv[j + q], w[q][e], acc[e]);
+      }
+      for (; j < k; ++j) {
+        const int32_t ix = si[j];
+        if (ix < 0) continue;
+        float w[8];
+        dec_load8<T>(W + (int64_t)ix * d + col, w);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = fmaf(sv[j], w[e], acc[e]);
+      }
+      float4* o = reinterpret_cast<float4*>(out + b * d + col);
+      o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    } else {
+      for (; j < k; ++j) {
+        const int32_t ix = si[j];
+        if (ix < 0) continue;
+        for (int e = 0; e < 8 && col + e < d; ++e) acc[e] = fmaf(sv[j], to_f32(W[(int64_t)ix * d + col + e]), acc[e]);
+      }
+      for (int e = 0; e < 8 && col + e < d; ++e) out[b * d + col + e] = acc[e];
+    }
+  }
+}
+
+template <typename T>
+cudaError_t launch_decode(const float* V, const int32_t* I, const T* W_dec, const float* b_dec, float* out, int64_t B,
+                          int k, int64_t F, int64_t d, cudaStream_t stream) {
+  if (B <= 0 || d <= 0) return cudaSuccess;
+  if (k < 0 || k > kDecMaxK) return cudaErrorInvalidValue;
+  const int64_t slices = (d + 8 * kDecThreads - 1) / (8 * kDecThreads);
+  if (slices > 65535) return cudaErrorInvalidValue;
+  const unsigned rows = (unsigned)(B < 65535 ? B : 65535);
+  decode_kernel<T><<<dim3((unsigned)slices, rows), kDecThreads, 0, stream>>>(V, I, W_dec, b_dec, out, B, k, F, d);
+  return cudaGetLastError();
+}
+template cudaError_t launch_decode<float>(const float*, const int32_t*, const float*, const float*, float*, int64_t,
+                                          int, int64_t, int64_t, cudaStream_t);
+template cudaError_t launch_decode<__half>(const float*, const int32_t*, const __half*, const float*, float*, int64_t,
+                                           int, int64_t, int64_t, cudaStream_t);
+template cudaError_t launch_decode<__nv_bfloat16>(const float*, const int32_t*, const __nv_bfloat16*, const float*,
+                                                  float*, int64_t, int, int64_t, int64_t, cudaStream_t);
+
 cudaError_t read_and_clear_device_error(unsigned* out, cudaStream_t stream) {
   unsigned zero = 0;
   cudaError_t e = cudaMemcpyFromSymbolAsync(out, g_device_error, sizeof(unsigned), 0, cudaMemcpyDeviceToHost, stream);

@@ -245,6 +245,15 @@ template <int L>
 cudaError_t launch_finish(const FinishArgs& fa, int grid, cudaStream_t stream);
 
 
+// SAE decoder over the encoder's sparse codes (no reference counterpart):
+// out[b][:] = b_dec[:] + sum_j V[b][j] * W_dec[I[b][j]][:], W_dec (F, d) in T
+// (float, __half or __nv_bfloat16), fp32 accumulation and output; b_dec may be
+// null; indices < 0 (padding) or >= F are skipped.  d % 8 == 0 for 16-bit W_dec
+// (d % 4 for fp32) and 16-byte aligned W_dec / out / b_dec.
+template <typename T>
+cudaError_t launch_decode(const float* V, const int32_t* I, const T* W_dec, const float* b_dec, float* out, int64_t B,
+                          int k, int64_t F, int64_t d, cudaStream_t stream);
+
 // Exact top-k of rows over F <= kFullSortMaxF features by a whole-row sort,
 // any 1 <= k <= F (dtype: 0 fp32, 1 fp16, 2 bf16; grid.x = B must fit).
 constexpr int kFullSortMaxF = 4096;

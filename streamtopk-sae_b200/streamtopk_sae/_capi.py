@@ -25,7 +25,7 @@ EXPORTS = (
     "stk_exchange_bytes", "stk_exchange_create", "stk_exchange_ipc_handle", "stk_exchange_connect",
     "stk_exchange_forward", "stk_exchange_destroy",
     "stk_workspace_bytes_fp8", "stk_exact_forward_fp8", "stk_quantize_rows_fp8",
-    "stk_approx_cand_workspace_bytes", "stk_approx_forward_cand",
+    "stk_approx_cand_workspace_bytes", "stk_approx_forward_cand", "stk_decode_forward",
 )
 IPC_HANDLE_BYTES = 64
 
@@ -99,6 +99,8 @@ def load():
         L.stk_quantize_rows_fp8.argtypes = [vp, i32, vp, vp, i64, i64, vp]
         L.stk_approx_cand_workspace_bytes.restype = i32
         L.stk_approx_cand_workspace_bytes.argtypes = [i64, i64, i64, i64, i64, i32, ctypes.POINTER(sz)]
+        L.stk_decode_forward.restype = i32
+        L.stk_decode_forward.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, i64, i32, vp]
         L.stk_approx_forward_cand.restype = i32
         L.stk_approx_forward_cand.argtypes = [vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32, vp, sz,
                                               vp]
