@@ -471,8 +471,9 @@ __device__ __forceinline__ uint64_t& top_slot(uint32_t top, int s, int r) {
 // stk_smem) or in global memory (app_g).  Kept out of line: it runs rarely and
 // is large.
 template <int L, int A, bool APP_SMEM>
-__device__ __noinline__ float merge_survivors(uint32_t top_off, uint32_t app_off, const uint64_t* __restrict__ app_g,
-                                              int r, int n, int kth, float floor_thr) {
+__device__ __forceinline__ float merge_survivors_impl(uint32_t top_off, uint32_t app_off,
+                                                      const uint64_t* __restrict__ app_g, int r, int n, int kth,
+                                                      float floor_thr) {
   static_assert(A == 16 || A == 32, "append slots");
 #define TOP(s) top_slot(top_off, (s), r)
   uint64_t a[A];
@@ -526,6 +527,13 @@ __device__ __noinline__ float merge_survivors(uint32_t top_off, uint32_t app_off
   const uint64_t kk = TOP(kth);
 #undef TOP
   return kk ? fmaxf(key_value(kk), floor_thr) : floor_thr;
+}
+
+// Out of line (the hot loop stays small: the instruction cache matters).
+template <int L, int A, bool APP_SMEM>
+__device__ __noinline__ float merge_survivors(uint32_t top_off, uint32_t app_off, const uint64_t* __restrict__ app_g,
+                                              int r, int n, int kth, float floor_thr) {
+  return merge_survivors_impl<L, A, APP_SMEM>(top_off, app_off, app_g, r, n, kth, floor_thr);
 }
 
 // Key i of a list held in tensor memory occupies 32-bit columns 2i (low half)
@@ -717,6 +725,17 @@ struct RowTopK {
     cnt = 0;
   }
 
+  // flush() without the call: for callers that hold many keys in registers
+  // across it (a call would make them spill around the loop).
+  __device__ __forceinline__ void flush_inline() {
+    if constexpr (TOPT) {
+      flush();
+    } else {
+      thr = merge_survivors_impl<L, A, APP_SMEM>(top, app_s, app_g, r, cnt, kth, floor_thr);
+      cnt = 0;
+    }
+  }
+
   __device__ __forceinline__ void push(uint64_t key) {
     if constexpr (APP_SMEM)
       smem_keys(app_s)[cnt * kRows + r] = key;
@@ -767,7 +786,7 @@ struct RowTopK {
 #pragma unroll
     for (int j = 0; j < N; ++j) s += (j < n && keys[j] != kEmptyKey && key_value(keys[j]) > thr) ? 1 : 0;
     if (__any_sync(0xffffffffu, cnt + s > A)) {
-      flush();
+      flush_inline();
       s = 0;
 #pragma unroll
       for (int j = 0; j < N; ++j) s += (j < n && keys[j] != kEmptyKey && key_value(keys[j]) > thr) ? 1 : 0;

@@ -612,11 +612,13 @@ __global__ void __launch_bounds__((MODE & 3) == kModeTF32 ? kFusedThreads + 64 :
       if constexpr (FP8) load_bias_tile<NT>(p.w_scale, cur.ft, cur.width(), p.F, lane, scur);
     }
     while (cur.valid(g)) {
-      TileWalk<NT, PAIR> nxt = cur;
-      nxt.next(g, rank);
-      if (nxt.valid(g)) {
-        load_bias_tile<NT>(p.bias, nxt.ft, nxt.width(), p.F, lane, bnext);
-        if constexpr (FP8) load_bias_tile<NT>(p.w_scale, nxt.ft, nxt.width(), p.F, lane, snext);
+      {  // the next tile's bias, prefetched (its walker is not kept: registers)
+        TileWalk<NT, PAIR> nxt = cur;
+        nxt.next(g, rank);
+        if (nxt.valid(g)) {
+          load_bias_tile<NT>(p.bias, nxt.ft, nxt.width(), p.F, lane, bnext);
+          if constexpr (FP8) load_bias_tile<NT>(p.w_scale, nxt.ft, nxt.width(), p.F, lane, snext);
+        }
       }
       if (cur.first_of_unit()) {
         acc.init(list_s, app_s, app_cta, r, p.k);
@@ -808,7 +810,7 @@ __global__ void __launch_bounds__((MODE & 3) == kModeTF32 ? kFusedThreads + 64 :
         bcur[c] = bnext[c];
         if constexpr (FP8) scur[c] = snext[c];
       }
-      cur = nxt;
+      cur.next(g, rank);
       ++tile;
     }
     if (!ok && lane == 0) {
