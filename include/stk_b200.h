@@ -90,6 +90,35 @@ STK_API int stk_exact_forward(const void* X, const void* W, const float* b, floa
                       void* stream);
 
 /*
+ * Pipelined exact encode for loops that encode batch after batch of one shape
+ * (serving, activation sweeps): each batch gets exactly stk_exact_forward's
+ * result for its inputs (same op, reference streamtopk_exact.cu:788-833; the
+ * pipelining has no counterpart there).  One launch per batch: the score
+ * kernel of batch s also finishes batch s - 1 (while its first W_enc tile
+ * streams in), so a batch's V / I are complete, in stream order, once the next
+ * batch has been submitted or after stk_pipeline_flush.  Read a batch's
+ * results only after that point.
+ * The pipeline keeps its per-batch lists in a workspace of
+ * stk_pipeline_workspace_bytes (two halves, used by alternate batches); the
+ * caller allocates it and keeps it for the pipeline's lifetime.  Submit and
+ * flush on one stream (or order the streams).  Shapes that do not pipeline
+ * (k > 64, several rounds of units per CTA, unaligned operands:
+ * stk_pipeline_pipelined() == 0) run each batch as stk_exact_forward
+ * (complete at once).  X, W, b, V, I per batch as in stk_exact_forward;
+ * k <= 128; B >= 1.
+ */
+typedef struct stk_pipeline stk_pipeline;
+STK_API int stk_pipeline_workspace_bytes(int64_t B, int64_t d, int64_t F, int64_t k, int dtype, int flags,
+                                         size_t* bytes);
+STK_API int stk_pipeline_create(stk_pipeline** out, int64_t B, int64_t d, int64_t F, int64_t k, int dtype, int flags,
+                                void* workspace, size_t workspace_bytes);
+STK_API int stk_pipeline_submit(stk_pipeline* p, const void* X, const void* W, const float* b, float* V, int32_t* I,
+                                void* stream);
+STK_API int stk_pipeline_flush(stk_pipeline* p, void* stream);
+STK_API int stk_pipeline_pipelined(const stk_pipeline* p);
+STK_API int stk_pipeline_destroy(stk_pipeline* p);
+
+/*
  * Approximate (per-128-feature-tile top-c candidates) encode, final top-k
  * included.  Replaces streamtopk_cuda_approx_forward + the torch.topk/gather
  * that follows it (reference: streamtopk_sae/csrc/cuda/streamtopk_approx.cu:

@@ -340,9 +340,11 @@ int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t 
   // One unit per CTA and every CTA resident (one per SM): the fused kernel
   // meets at a grid barrier and finishes the rows itself, no second launch.
   pl->fin_fused = pl->tc && pl->grid.units <= pl->ctas && !(flags & STK_FLAG_SEPARATE_FINISH);
-  // With the fused finish each row list carries its last survivors as a sorted
-  // second run (no final merge in the score kernel).
-  pl->pitch = (pl->fin_fused && !std::getenv("STK_FULL_FLUSH")) ? pl->L + stk::kAppendMax : pl->L;
+  // With one unit per CTA (the fused finish, or a pipelined step's separate
+  // finish) each row list carries its last survivors as a sorted second run
+  // (no final merge in the score kernel).
+  pl->pitch = (pl->tc && pl->grid.units <= pl->ctas && !std::getenv("STK_FULL_FLUSH")) ? pl->L + stk::kAppendMax
+                                                                                        : pl->L;
   pl->ws_partials = (partial_bytes(pl->grid, pl->pitch) + 255) & ~size_t(255);
   // Without the pilot (several units per CTA, e.g. B > 256), the units of an
   // M tile share their rising thresholds as a floor instead.  Not for the
@@ -379,7 +381,7 @@ bool fused_override(int L, int* nt, int* stages, int* app, int* app_smem, int* t
 
 int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint64_t* partials, uint64_t* app,
               int64_t B, int64_t d, int64_t F, int64_t k, int dtype, uint32_t index_offset,
-              const stk::FinishArgs* fin, cudaStream_t stream) {
+              const stk::FinishArgs* fin, cudaStream_t stream, const stk::FinishArgs* prev_fin = nullptr) {
   // Defaults: 256-feature tiles, append slots in shared memory where 3
   // pipeline stages still fit.  When a CTA's unit fits in one such tile (F
   // small per CTA, e.g. one shard of a multi-GPU encode) 128-feature tiles
@@ -496,6 +498,12 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
     if (pl.shared_floor) p.row_floor = reinterpret_cast<uint32_t*>(base + kSyncBytes);
     cudaError_t me = cudaMemsetAsync(base, 0, pl.ws_sync, stream);
     if (me != cudaSuccess) return cuda_fail(me, "cudaMemsetAsync(sync)");
+  }
+  p.prev_finish = 0;
+  std::memset(&p.pfin, 0, sizeof p.pfin);
+  if (prev_fin) {
+    p.prev_finish = 1;
+    p.pfin = *prev_fin;
   }
   if (fin) {
     p.finish = 1;
@@ -1203,6 +1211,185 @@ int stk_exchange_destroy(stk_exchange* x) {
   cudaSetDevice(prev);
   delete x;
   return rc;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Pipelined exact encode: batch after batch of one shape, one launch per batch.
+// The score kernel of batch s also finishes batch s - 1: its four epilogue
+// warps select and write the previous batch's rows from the lists that batch
+// left, while the CTA's producer streams the first W_enc tile (they would wait
+// for it anyway).  The finish step (grid barrier, row selection) then costs
+// nothing on the critical path, and the lists of consecutive batches live in
+// the two halves of the pipeline's workspace.  A batch's V / I are complete
+// once the next batch has been submitted, or after stk_pipeline_flush (a
+// standalone finish kernel for the last batch).  Shapes whose units are not
+// all resident at once (several rounds of units per CTA, CTA pairs), or
+// unaligned operands, or k > 64, run as stk_exact_forward does (complete at once).
+// ---------------------------------------------------------------------------
+struct stk_pipeline {
+  int64_t B, d, F, k;
+  int dtype, flags, device;
+  char* ws;
+  size_t half;                 // bytes of one half of the workspace
+  unsigned long long step;     // batches submitted so far
+  bool piped;                  // the shape pipelines (one unit per CTA on the tcgen05 path)
+  bool pending;                // a batch waits for its finish
+  stk::FinishArgs pending_fin; // its finish (lists in its half, its V / I)
+  int pending_L;
+};
+
+namespace {
+int pipeline_plan(const void* X, const void* W, const stk_pipeline* pp, Plan* pl) {
+  return plan(X, W, pp->B, pp->d, pp->F, pp->k, pp->dtype, pp->flags | STK_FLAG_SEPARATE_FINISH, pl);
+}
+// L = 128 (k > 64) is left out: its finish takes longer than the first tile's
+// loads and would delay the score kernel.
+bool pipelines(const Plan& pl) {
+  return pl.tc && !pl.pair && !pl.cand && !pl.fp8 && pl.L <= 64 && pl.grid.units <= pl.ctas;
+}
+
+int pipeline_check(int64_t B, int64_t d, int64_t F, int64_t k, int dtype, int flags) {
+  int rc = check_common("stk_pipeline", B, d, F, dtype);
+  if (rc) return rc;
+  if (!(k >= 1 && k <= F)) return fail(STK_EINVAL, "k out of range");
+  if (d > 4096 && !(flags & STK_FLAG_ANY_D)) return fail(STK_EINVAL, "d exceeds D_MAX=4096");
+  if (!(flags & STK_FLAG_ANY_K) && !ref_k(k))
+    return fail(STK_EINVAL, "streamtopk_cuda_exact: unsupported k=" + std::to_string(k) +
+                                ". Supported: 1,2,4,8,16,32,64,128.");
+  if (k > 128) return fail(STK_EINVAL, "stk_pipeline: k must be <= 128");
+  if (B < 1) return fail(STK_EINVAL, "stk_pipeline: B must be >= 1");
+  return STK_OK;
+}
+
+// Bytes of one half: the larger of the pipelined plan's and the one-call
+// plan's workspace (a batch that cannot pipeline runs as one call in a half).
+int pipeline_half(int64_t B, int64_t d, int64_t F, int64_t k, int dtype, int flags, size_t* half) {
+  Plan a, b;
+  const int f = flags | (dtype == STK_F32 ? STK_FLAG_TF32 : 0);
+  int rc = plan(nullptr, nullptr, B, d, F, k, dtype, f | STK_FLAG_SEPARATE_FINISH, &a);
+  if (rc) return rc;
+  rc = plan(nullptr, nullptr, B, d, F, k, dtype, f, &b);
+  if (rc) return rc;
+  *half = ((a.ws > b.ws ? a.ws : b.ws) + 255) & ~size_t(255);
+  if (*half == 0) *half = 256;
+  return STK_OK;
+}
+
+int pipeline_device(const stk_pipeline* pp) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != pp->device) return fail(STK_EINVAL, "current device is not the pipeline's device");
+  return STK_OK;
+}
+
+int pipeline_flush(stk_pipeline* pp, cudaStream_t s) {
+  if (!pp->pending) return STK_OK;
+  pp->pending = false;
+  return run_finish(pp->pending_L, pp->pending_fin, s);
+}
+}  // namespace
+
+extern "C" {
+
+int stk_pipeline_workspace_bytes(int64_t B, int64_t d, int64_t F, int64_t k, int dtype, int flags, size_t* bytes) {
+  if (!bytes) return fail(STK_EINVAL, "bytes is NULL");
+  int rc = pipeline_check(B, d, F, k, dtype, flags);
+  if (rc) return rc;
+  size_t half = 0;
+  rc = pipeline_half(B, d, F, k, dtype, flags, &half);
+  if (rc) return rc;
+  *bytes = 2 * half;
+  return STK_OK;
+}
+
+int stk_pipeline_create(stk_pipeline** out, int64_t B, int64_t d, int64_t F, int64_t k, int dtype, int flags,
+                        void* workspace, size_t workspace_bytes) {
+  if (!out) return fail(STK_EINVAL, "out is NULL");
+  *out = nullptr;
+  int rc = pipeline_check(B, d, F, k, dtype, flags);
+  if (rc) return rc;
+  size_t half = 0;
+  rc = pipeline_half(B, d, F, k, dtype, flags, &half);
+  if (rc) return rc;
+  if (workspace == nullptr || workspace_bytes < 2 * half || !aligned16(workspace))
+    return fail(STK_ENOSPACE, "stk_pipeline_create: workspace too small or unaligned (need " +
+                                  std::to_string(2 * half) + " bytes, 16-byte aligned)");
+  Plan pl;
+  stk_pipeline* pp = new stk_pipeline();
+  pp->B = B;
+  pp->d = d;
+  pp->F = F;
+  pp->k = k;
+  pp->dtype = dtype;
+  pp->flags = flags;
+  cudaGetDevice(&pp->device);
+  pp->ws = static_cast<char*>(workspace);
+  pp->half = half;
+  pp->step = 0;
+  pp->pending = false;
+  rc = pipeline_plan(nullptr, nullptr, pp, &pl);
+  if (rc) {
+    delete pp;
+    return rc;
+  }
+  pp->piped = pipelines(pl);
+  *out = pp;
+  return STK_OK;
+}
+
+int stk_pipeline_submit(stk_pipeline* pp, const void* X, const void* W, const float* b, float* V, int32_t* I,
+                        void* stream) {
+  if (!pp) return fail(STK_EINVAL, "pipeline is NULL");
+  int rc = pipeline_device(pp);
+  if (rc) return rc;
+  if (!X || !W || !b || !V || !I) return fail(STK_EINVAL, "stk_pipeline_submit: null pointer");
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Plan pl;
+  rc = pipeline_plan(X, W, pp, &pl);
+  if (rc) return rc;
+  char* half = pp->ws + (size_t)(pp->step & 1ull) * pp->half;
+  if (!pipelines(pl) || pl.ws > pp->half) {
+    // Not pipelined: the pending batch first, then this one as one call.
+    rc = pipeline_flush(pp, s);
+    if (rc) return rc;
+    rc = encode(X, W, b, V, I, nullptr, pp->B, pp->d, pp->F, pp->k, pp->dtype, pp->flags, 0u, half, pp->half, s);
+    if (rc) return rc;
+    ++pp->step;
+    return STK_OK;
+  }
+  uint64_t* partials = reinterpret_cast<uint64_t*>(half);
+  uint64_t* app = reinterpret_cast<uint64_t*>(half + pl.ws_partials);
+  const stk::FinishArgs fa = finish_args(partials, pl.grid.segs, (int64_t)pl.grid.m_tiles * stk::kRows, pl.pitch,
+                                         pl.pitch - pl.L, pp->B, pp->k, V, I, nullptr, nullptr);
+  const bool merge_prev = pp->pending && pp->pending_L == pl.L;
+  if (pp->pending && !merge_prev) {
+    rc = pipeline_flush(pp, s);
+    if (rc) return rc;
+  }
+  rc = run_fused(pl, X, W, b, partials, app, pp->B, pp->d, pp->F, pp->k, pp->dtype, 0u, nullptr, s,
+                 merge_prev ? &pp->pending_fin : nullptr);
+  if (rc) return rc;
+  pp->pending = true;
+  pp->pending_fin = fa;
+  pp->pending_L = pl.L;
+  ++pp->step;
+  return STK_OK;
+}
+
+int stk_pipeline_flush(stk_pipeline* pp, void* stream) {
+  if (!pp) return fail(STK_EINVAL, "pipeline is NULL");
+  int rc = pipeline_device(pp);
+  if (rc) return rc;
+  return pipeline_flush(pp, static_cast<cudaStream_t>(stream));
+}
+
+int stk_pipeline_pipelined(const stk_pipeline* pp) { return pp && pp->piped ? 1 : 0; }
+
+int stk_pipeline_destroy(stk_pipeline* pp) {
+  delete pp;
+  return STK_OK;
 }
 
 }  // extern "C"

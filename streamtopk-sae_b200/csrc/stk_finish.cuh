@@ -76,15 +76,25 @@ __device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsign
 
 __device__ __forceinline__ bool list_on(uint32_t mask, int s) { return s >= 32 || ((mask >> s) & 1u); }
 
+// Barrier over the threads that run a finish: the whole CTA, or (pipelined
+// encode) the score kernel's four epilogue warps, which finish the previous
+// step's rows while the CTA's producer streams the first tile (named barrier 1).
+struct SyncCta {
+  __device__ static __forceinline__ void sync() { __syncthreads(); }
+};
+struct SyncEpilogue {
+  __device__ static __forceinline__ void sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+};
+
 // Best L keys of row b over nlists lists, written to sm.best[0..L) descending
 // with empty keys after the last one.  List s of row b starts at
 // lists[(s * stride + b) * pitch]: L keys descending (empty keys 0 at the end),
 // then, if tail > 0, a second descending run of `tail` keys (the score kernel's
 // last survivors, stored without a final merge).  Lists s < 32 whose bit is
 // clear in list_mask count as empty.  Every thread of the CTA calls it
-// (nthreads = blockDim.x, at most kFinishMaxWarps warps); it ends with a
-// __syncthreads.  Lists must be 16-byte aligned.
-template <int L>
+// (nthreads = the threads that S synchronises, at most kFinishMaxWarps warps);
+// it ends with S::sync().  Lists must be 16-byte aligned.
+template <int L, class S = SyncCta>
 __device__ void select_row(const uint64_t* __restrict__ lists, int nlists, int64_t stride, int pitch, int tail,
                            int64_t b, int k, uint32_t list_mask, FinishSmem& sm, int tid, int nthreads) {
   const bool use_heads = nlists <= kFinishMaxLists;
@@ -140,7 +150,7 @@ __device__ void select_row(const uint64_t* __restrict__ lists, int nlists, int64
                                                lists + ((int64_t)s * stride + b) * pitch + j))
                                          : 0ull;
     }
-  __syncthreads();
+  S::sync();
   if (m > 1) {
     for (int t = tid; t < P; t += nthreads) {
       const uint64_t key = sm.cand[t];
@@ -159,7 +169,7 @@ __device__ void select_row(const uint64_t* __restrict__ lists, int nlists, int64
     }
   }
   if (kth != 0ull) atomicMax(reinterpret_cast<unsigned long long*>(&sm.tau), (unsigned long long)kth);
-  __syncthreads();
+  S::sync();
   const uint64_t tau = sm.tau;
   auto keep4 = [&](const uint64_t (&kk)[4]) {
 #pragma unroll
@@ -204,7 +214,7 @@ __device__ void select_row(const uint64_t* __restrict__ lists, int nlists, int64
         if (!take4(ps + L + q)) break;
     }
   }
-  __syncthreads();
+  S::sync();
   const int C = use_heads ? sm.cnt : kFinishCap + 1;
   if (C <= kFinishCap) {
     for (int i = tid; i < C; i += nthreads) {
@@ -214,7 +224,7 @@ __device__ void select_row(const uint64_t* __restrict__ lists, int nlists, int64
       if (r < L) sm.best[r] = key;
     }
     for (int i = C + tid; i < L; i += nthreads) sm.best[i] = 0ull;
-    __syncthreads();
+    S::sync();
     return;
   }
   // Fold: warp w merges runs w, w + nw, ... (every list's L-key run, then
@@ -253,7 +263,7 @@ __device__ void select_row(const uint64_t* __restrict__ lists, int nlists, int64
   uint64_t* red = sm.cand;  // [nw][L]
 #pragma unroll
   for (int e = 0; e < E; ++e) red[warp * L + e * 32 + lane] = acc[e];
-  __syncthreads();
+  S::sync();
   if (warp == 0) {
     for (int w = 1; w < nw; ++w) {
       uint64_t u[E];
@@ -264,7 +274,7 @@ __device__ void select_row(const uint64_t* __restrict__ lists, int nlists, int64
 #pragma unroll
     for (int e = 0; e < E; ++e) sm.best[e * 32 + lane] = acc[e];
   }
-  __syncthreads();
+  S::sync();
 }
 
 // Writes the row's result from sm.best: V/I (first k; empty keys as
@@ -304,7 +314,7 @@ __device__ __forceinline__ void publish_row(const ExchangeDev& ex, const FinishS
 // CTA calls it.  With the exchange, all of this CTA's rows are published
 // before any wait, so CTAs that run at the same time on different GPUs never
 // wait on each other in a cycle.
-template <int L>
+template <int L, class S = SyncCta>
 __device__ void finish_rows(const FinishArgs& fa, FinishSmem& sm, int64_t row0, int64_t row_step, int tid,
                             int nthreads) {
   unsigned long long step = 0;
@@ -314,19 +324,19 @@ __device__ void finish_rows(const FinishArgs& fa, FinishSmem& sm, int64_t row0, 
     slot = (int)(step & 1ull);
   }
   for (int64_t b = row0; b < fa.rows; b += row_step) {
-    select_row<L>(fa.lists, fa.nlists, fa.stride, fa.pitch, fa.tail, b, fa.k, 0xffffffffu, sm, tid, nthreads);
+    select_row<L, S>(fa.lists, fa.nlists, fa.stride, fa.pitch, fa.tail, b, fa.k, 0xffffffffu, sm, tid, nthreads);
     if (fa.use_ex)
       publish_row<L>(fa.ex, sm, slot, step + 1ull, b, tid);
     else
       write_row<L>(fa, sm, b, tid, nthreads);
-    __syncthreads();
+    S::sync();
   }
   if (!fa.use_ex) return;
   const ExchangeDev& ex = fa.ex;
   const unsigned long long t0 = global_timer_ns();
   for (int64_t b = row0; b < fa.rows; b += row_step) {
     if (tid == 0) sm.valid = 0u;
-    __syncthreads();
+    S::sync();
     if (tid < ex.world) {
       const unsigned long long* f = ex.flag + ((int64_t)slot * ex.world + tid) * ex.max_rows + b;
       bool ok = true;
@@ -342,11 +352,11 @@ __device__ void finish_rows(const FinishArgs& fa, FinishSmem& sm, int64_t row0, 
       else
         raise_device_error(kErrExchangeTimeout);
     }
-    __syncthreads();
-    select_row<L>(ex.recv + (int64_t)slot * ex.world * ex.max_rows * L, ex.world, ex.max_rows, L, 0, b, fa.k, sm.valid,
+    S::sync();
+    select_row<L, S>(ex.recv + (int64_t)slot * ex.world * ex.max_rows * L, ex.world, ex.max_rows, L, 0, b, fa.k, sm.valid,
                   sm, tid, nthreads);
     write_row<L>(fa, sm, b, tid, nthreads);
-    __syncthreads();
+    S::sync();
   }
   // Every CTA of this step has passed its waits: the last one advances the step.
   if (tid == 0) {

@@ -592,6 +592,17 @@ __global__ void __launch_bounds__((MODE & 3) == kModeTF32 ? kFusedThreads + 64 :
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    if constexpr (!PAIR && !CAND) {
+      // Pipelined encode: the previous step's rows, from the lists that step's
+      // score kernel left (complete: it ran before this grid in the stream),
+      // while this CTA's first tile streams in.  CTA c takes rows c,
+      // c + gridDim.x, ...; the shared memory of the top lists / append slots
+      // is not in use before the first tile's epilogue.
+      static_assert(PAIR || CAND || Cfg::kBarOff - Cfg::kTopOff >= (int)sizeof(FinishSmem), "finish scratch");
+      if (p.prev_finish)
+        finish_rows<L, SyncEpilogue>(p.pfin, *reinterpret_cast<FinishSmem*>(smem + Cfg::kTopOff), blockIdx.x,
+                                     gridDim.x, threadIdx.x - kFirstEpiWarp * 32, kEpilogueWarps * 32);
+    }
     const int q = warp & 3;
     const int r = q * 32 + lane;
     const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);

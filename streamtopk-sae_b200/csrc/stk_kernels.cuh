@@ -105,6 +105,8 @@ struct FusedParams {
   int cand_c;            // 16 or 32
   const float* x_scale;  // FP8: [B] per-row dequantization scale of X
   const float* w_scale;  // FP8: [F] per-feature dequantization scale of W (scores = x_s * w_s * acc + b)
+  int prev_finish;       // pipelined encode: the epilogue warps first finish the previous step's rows (pfin)
+  FinishArgs pfin;
 };
 
 struct SimtParams {

@@ -26,6 +26,8 @@ EXPORTS = (
     "stk_exchange_forward", "stk_exchange_destroy",
     "stk_workspace_bytes_fp8", "stk_exact_forward_fp8", "stk_quantize_rows_fp8",
     "stk_approx_cand_workspace_bytes", "stk_approx_forward_cand", "stk_decode_forward",
+    "stk_pipeline_workspace_bytes", "stk_pipeline_create", "stk_pipeline_submit", "stk_pipeline_flush",
+    "stk_pipeline_pipelined", "stk_pipeline_destroy",
 )
 IPC_HANDLE_BYTES = 64
 
@@ -104,6 +106,18 @@ def load():
         L.stk_approx_forward_cand.restype = i32
         L.stk_approx_forward_cand.argtypes = [vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i32, i32, vp, sz,
                                               vp]
+        L.stk_pipeline_workspace_bytes.restype = i32
+        L.stk_pipeline_workspace_bytes.argtypes = [i64, i64, i64, i64, i32, i32, ctypes.POINTER(sz)]
+        L.stk_pipeline_create.restype = i32
+        L.stk_pipeline_create.argtypes = [ctypes.POINTER(vp), i64, i64, i64, i64, i32, i32, vp, sz]
+        L.stk_pipeline_submit.restype = i32
+        L.stk_pipeline_submit.argtypes = [vp, vp, vp, vp, vp, vp, vp]
+        L.stk_pipeline_flush.restype = i32
+        L.stk_pipeline_flush.argtypes = [vp, vp]
+        L.stk_pipeline_pipelined.restype = i32
+        L.stk_pipeline_pipelined.argtypes = [vp]
+        L.stk_pipeline_destroy.restype = i32
+        L.stk_pipeline_destroy.argtypes = [vp]
         _lib = L
     return _lib
 
