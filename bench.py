@@ -383,6 +383,19 @@ def run_b200(args, cfg):
         step = lambda x: stk.topk_sae_cuda_approx(x, W, b, k, cfg["c"])  # noqa: E731
     else:
         step = lambda x: stk.topk_sae_cuda_exact(x, W, b, k)  # noqa: E731
+    # Steps of the timed loop: the pipelined encode where it applies (each
+    # batch finished by the next batch's score kernel, the last by flush()),
+    # else one call per batch.  deferred: a batch's V/I are complete only after
+    # the next submit / flush.
+    pipe = None
+    flush = lambda: None  # noqa: E731
+    submit, deferred = step, False
+    if world > 1:
+        submit, flush, deferred = enc.submit, enc.flush, True
+    elif not fp8 and cfg["mode"] == "exact" and not args.no_pipeline:
+        pipe = stk.EncodePipeline(B, d, F, k, dtype, device=dev)
+        submit = lambda x: pipe.submit(x, W, b)  # noqa: E731
+        flush, deferred = pipe.flush, True
 
     stream = torch.cuda.current_stream(dev)
     from streamtopk_sae.graph import CapturedEncode
@@ -392,7 +405,8 @@ def run_b200(args, cfg):
             dist.barrier(device_ids=[local])
 
     for _ in range(max(args.warmup, 3)):
-        step(X)
+        submit(X)
+    flush()
     torch.cuda.synchronize(dev)
     assert _capi.device_error(stream.cuda_stream) == 0
 
@@ -412,13 +426,15 @@ def run_b200(args, cfg):
         with ClockSampler(local) as clk:
             e0.record(stream)
             for _ in range(args.steps):
-                step(X)
+                submit(X)
+            flush()
             e1.record(stream)
             torch.cuda.synchronize(dev)
         el_ms = e0.elapsed_time(e1)
         with _capi.KernelTimer(max_launches=args.steps * 4 + 16) as kt:
             for _ in range(args.steps):
-                step(X)
+                submit(X)
+            flush()
             torch.cuda.synchronize(dev)
         launches = sum(kt.launches.values())
     else:
@@ -431,7 +447,7 @@ def run_b200(args, cfg):
         # programmatically dependent kernels); a second, instrumented graph of
         # the same G steps gives the per-kernel durations afterwards.
         G = next(g for g in (8, 4, 2, 1) if args.steps % g == 0)
-        timed = CapturedEncode(step, X, steps=G, warmup=0)
+        timed = CapturedEncode(submit, X, steps=G, warmup=0, finish=flush)
         barrier()
         torch.cuda.synchronize(dev)
         with ClockSampler(local) as clk:
@@ -445,7 +461,7 @@ def run_b200(args, cfg):
         timed.close()
         del timed
         with _capi.KernelTimer(max_launches=G * 4 + 16) as kt:
-            inst = CapturedEncode(step, X, steps=G, warmup=0)   # event nodes around each library kernel
+            inst = CapturedEncode(submit, X, steps=G, warmup=0, finish=flush)   # event nodes around each kernel
             barrier()
             for _ in range(4):
                 inst.replay()
@@ -465,7 +481,8 @@ def run_b200(args, cfg):
     value = B * args.steps / (el_ms / 1e3)
 
     # ---------------- parity of the timed step (one more, untimed, call on every rank)
-    Vp, Ip = step(X)
+    Vp, Ip = submit(X)
+    flush()
     torch.cuda.synchronize(dev)
     parity = None
     if rank == 0:
@@ -489,15 +506,18 @@ def run_b200(args, cfg):
     overlap = not args.e2e_serial
     graphs = []
     if world == 1:
-        # The public op called eagerly on a device buffer (two when overlapped).
+        # The public API called eagerly on a device buffer (two when overlapped):
+        # the pipelined encode (or the one-call op where it does not apply).
         Xd2 = [torch.empty_like(X) for _ in range(2 if overlap else 1)]
-        runs = [(lambda xd: (lambda: step(xd)))(xd) for xd in Xd2]
+        runs = [(lambda xd: (lambda: submit(xd)))(xd) for xd in Xd2]
+        e2e_deferred = deferred
     else:
         # One CUDA graph of one encode step per input buffer (graph.CapturedEncode:
         # its static X is the buffer the host copy lands in).
         graphs = [CapturedEncode(step, X, steps=1, warmup=1 if i == 0 else 0) for i in range(2 if overlap else 1)]
         Xd2 = [g_.X for g_ in graphs]
         runs = [g_.replay for g_ in graphs]
+        e2e_deferred = False
 
     if overlap:
         # A serving loop: X of step i+1 is uploaded on a copy stream while the
@@ -507,12 +527,24 @@ def run_b200(args, cfg):
         copied = [torch.cuda.Event(), torch.cuda.Event()]
         consumed = [torch.cuda.Event(), torch.cuda.Event()]
         readback = [torch.cuda.Event(), torch.cuda.Event()]
+        flushed = torch.cuda.Event()
+
+        def read_back(VI, after, slot):
+            V, I = VI
+            d2h.wait_event(after)
+            with torch.cuda.stream(d2h):
+                V.record_stream(d2h)
+                I.record_stream(d2h)
+                Vh.copy_(V, non_blocking=True)
+                Ih.copy_(I, non_blocking=True)
+                readback[slot].record(d2h)
 
         def e2e_run(n):
             h2d.wait_stream(stream)
             with torch.cuda.stream(h2d):
                 Xd2[0].copy_(Xh, non_blocking=True)
                 copied[0].record(h2d)
+            pending = None
             for i in range(n):
                 cur = i & 1
                 if i + 1 < n:
@@ -524,21 +556,27 @@ def run_b200(args, cfg):
                 stream.wait_event(copied[cur])
                 if world > 1 and i >= 2:
                     stream.wait_event(readback[cur])  # V/I of this graph's previous replay are read
-                V, I = runs[cur]()            # the public op / the captured ShardedEncoder.encode
+                V, I = runs[cur]()            # the public API / the captured ShardedEncoder.encode
                 consumed[cur].record(stream)
-                d2h.wait_event(consumed[cur])
-                with torch.cuda.stream(d2h):
-                    V.record_stream(d2h)
-                    I.record_stream(d2h)
-                    Vh.copy_(V, non_blocking=True)
-                    Ih.copy_(I, non_blocking=True)
-                    readback[cur].record(d2h)
+                if e2e_deferred:
+                    # Pipelined: step i-1's rows were finished by step i's launch.
+                    if pending is not None:
+                        read_back(pending, consumed[cur], cur)
+                    pending = (V, I)
+                else:
+                    read_back((V, I), consumed[cur], cur)
+            if pending is not None:
+                flush()
+                flushed.record(stream)
+                read_back(pending, flushed, 0)
             stream.wait_stream(d2h)
     else:
         def e2e_run(n):
             for _ in range(n):
                 Xd2[0].copy_(Xh, non_blocking=True)
                 V, I = runs[0]()
+                if e2e_deferred:
+                    flush()
                 Vh.copy_(V, non_blocking=True)
                 Ih.copy_(I, non_blocking=True)
 
@@ -590,12 +628,15 @@ def run_b200(args, cfg):
             "config": config_dict(args, cfg), "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": Xh.numel() * Xh.element_size() * world,
                     "d2h_bytes_per_step": (Vh.numel() * 4 + Ih.numel() * 4) * world,
-                    "path": (("streamtopk_sae.topk_sae_cuda_exact" if world == 1 else
+                    "path": (((("streamtopk_sae.EncodePipeline.submit (each batch finished by the next batch's launch)"
+                                if deferred else "streamtopk_sae.topk_sae_cuda_exact")) if world == 1 else
                               "streamtopk_sae.shard.ShardedEncoder.encode in CUDA graphs (graph.CapturedEncode)") +
                              (", X of step i+1 uploaded on a copy stream during step i, V/I read back on another"
                               if overlap else ", copies and kernels serialised on one stream"))},
             "parity": parity,
             "gpu_launches": launches, "graph_steps": G, "clocks": clk.summary(),
+            "timed_api": ("ShardedEncoder.submit x G + flush, CUDA graph" if world > 1 else
+                          "EncodePipeline.submit x K + flush" if deferred else "one call per step"),
             "exchange": (None if world == 1 else
                          "direct peer stores over NVLink (stk_exchange_*)" if enc.transport in ("p2p", "auto") else
                          "NCCL all_gather_into_tensor + merge kernel" +
@@ -696,6 +737,8 @@ def main():
     ap.add_argument("--dtype", default=None, choices=["bf16", "fp16", "fp32", "fp8"],
                     help="input dtype override (config 2 is a dtype sweep); fp8: E4M3 W_enc with per-feature "
                          "scales and X quantized per row on every call (streamtopk_sae.fp8; N=1, exact)")
+    ap.add_argument("--no-pipeline", action="store_true",
+                    help="N=1: time the one-call op (topk_sae_cuda_exact) instead of the pipelined encode")
     ap.add_argument("--e2e-serial", action="store_true",
                     help="e2e: serialise each step's copies and kernels on one stream (default: the X upload "
                          "of step i+1 overlaps the kernels of step i on a copy stream)")

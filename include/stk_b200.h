@@ -292,6 +292,19 @@ STK_API int stk_exchange_forward(stk_exchange* ex, const void* X, const void* W_
 STK_API int stk_exchange_destroy(stk_exchange* ex);
 
 /*
+ * The pipelined encode (stk_pipeline_*, above) for one rank of the F-sharded encode over a connected
+ * peer exchange (stk_exchange_*): W / b are this rank's rows [index_offset,
+ * index_offset + F_shard) and each batch's V / I are the global top-k,
+ * identical on every rank (as stk_exchange_forward).  Every rank submits and
+ * flushes the same batches in the same order; the cross-GPU publish, wait and
+ * merge of batch s run in the score kernel of batch s + 1 (or the flush).
+ * The exchange must outlive the pipeline.
+ */
+STK_API int stk_pipeline_create_sharded(stk_pipeline** out, stk_exchange* ex, int64_t B, int64_t d, int64_t F_shard,
+                                        int64_t k, int64_t index_offset, int dtype, int flags, void* workspace,
+                                        size_t workspace_bytes);
+
+/*
  * Profiling hook (no reference counterpart).  stk_profile_begin arms CUDA
  * events around each kernel launched by the calls that follow (up to
  * max_launches launches, any thread); stk_profile_end synchronises them and

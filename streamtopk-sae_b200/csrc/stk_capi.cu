@@ -1238,6 +1238,8 @@ struct stk_pipeline {
   bool pending;                // a batch waits for its finish
   stk::FinishArgs pending_fin; // its finish (lists in its half, its V / I)
   int pending_L;
+  stk_exchange* ex;            // F-sharded encode: the peer exchange of the finish (else null)
+  int64_t index_offset;        // F-sharded encode: this rank's first feature
 };
 
 namespace {
@@ -1329,6 +1331,8 @@ int stk_pipeline_create(stk_pipeline** out, int64_t B, int64_t d, int64_t F, int
   pp->half = half;
   pp->step = 0;
   pp->pending = false;
+  pp->ex = nullptr;
+  pp->index_offset = 0;
   rc = pipeline_plan(nullptr, nullptr, pp, &pl);
   if (rc) {
     delete pp;
@@ -1336,6 +1340,30 @@ int stk_pipeline_create(stk_pipeline** out, int64_t B, int64_t d, int64_t F, int
   }
   pp->piped = pipelines(pl);
   *out = pp;
+  return STK_OK;
+}
+
+int stk_pipeline_create_sharded(stk_pipeline** out, stk_exchange* x, int64_t B, int64_t d, int64_t F_shard,
+                                int64_t k, int64_t index_offset, int dtype, int flags, void* workspace,
+                                size_t workspace_bytes) {
+  if (!out) return fail(STK_EINVAL, "out is NULL");
+  *out = nullptr;
+  if (!x) return fail(STK_EINVAL, "exchange is NULL");
+  for (int p = 0; p < x->dev.world; ++p)
+    if (!x->dev.peer_recv[p]) return fail(STK_EINVAL, "exchange is not connected");
+  if (k < 1 || k > 128 || list_len(k) != x->L) return fail(STK_EINVAL, "k does not match the exchange");
+  if (B > x->dev.max_rows) return fail(STK_EINVAL, "B exceeds the exchange's max_rows");
+  if (F_shard < 1) return fail(STK_EINVAL, "stk_pipeline_create_sharded: F_shard must be >= 1");
+  if (index_offset < 0 || index_offset + F_shard > 0x7fffffffLL)
+    return fail(STK_EINVAL, "index_offset + F_shard must fit int32 indices");
+  int device = 0;
+  cudaGetDevice(&device);
+  if (device != x->device) return fail(STK_EINVAL, "current device is not the exchange's device");
+  int rc = stk_pipeline_create(out, B, d, F_shard, k, dtype, flags | STK_FLAG_ANY_K | STK_FLAG_ANY_D, workspace,
+                               workspace_bytes);
+  if (rc) return rc;
+  (*out)->ex = x;
+  (*out)->index_offset = index_offset;
   return STK_OK;
 }
 
@@ -1354,7 +1382,16 @@ int stk_pipeline_submit(stk_pipeline* pp, const void* X, const void* W, const fl
     // Not pipelined: the pending batch first, then this one as one call.
     rc = pipeline_flush(pp, s);
     if (rc) return rc;
-    rc = encode(X, W, b, V, I, nullptr, pp->B, pp->d, pp->F, pp->k, pp->dtype, pp->flags, 0u, half, pp->half, s);
+    if (pp->ex) {
+      Plan one;
+      rc = plan(X, W, pp->B, pp->d, pp->F, pp->k, pp->dtype, pp->flags, &one);
+      if (rc) return rc;
+      if (one.ws > pp->half) return fail(STK_ENOSPACE, "stk_pipeline_submit: workspace too small");
+      rc = score_and_finish(one, X, W, b, V, I, nullptr, pp->B, pp->d, pp->F, pp->k, pp->dtype,
+                            (uint32_t)pp->index_offset, &pp->ex->dev, half, s);
+    } else {
+      rc = encode(X, W, b, V, I, nullptr, pp->B, pp->d, pp->F, pp->k, pp->dtype, pp->flags, 0u, half, pp->half, s);
+    }
     if (rc) return rc;
     ++pp->step;
     return STK_OK;
@@ -1362,14 +1399,15 @@ int stk_pipeline_submit(stk_pipeline* pp, const void* X, const void* W, const fl
   uint64_t* partials = reinterpret_cast<uint64_t*>(half);
   uint64_t* app = reinterpret_cast<uint64_t*>(half + pl.ws_partials);
   const stk::FinishArgs fa = finish_args(partials, pl.grid.segs, (int64_t)pl.grid.m_tiles * stk::kRows, pl.pitch,
-                                         pl.pitch - pl.L, pp->B, pp->k, V, I, nullptr, nullptr);
+                                         pl.pitch - pl.L, pp->B, pp->k, V, I, nullptr,
+                                         pp->ex ? &pp->ex->dev : nullptr);
   const bool merge_prev = pp->pending && pp->pending_L == pl.L;
   if (pp->pending && !merge_prev) {
     rc = pipeline_flush(pp, s);
     if (rc) return rc;
   }
-  rc = run_fused(pl, X, W, b, partials, app, pp->B, pp->d, pp->F, pp->k, pp->dtype, 0u, nullptr, s,
-                 merge_prev ? &pp->pending_fin : nullptr);
+  rc = run_fused(pl, X, W, b, partials, app, pp->B, pp->d, pp->F, pp->k, pp->dtype, (uint32_t)pp->index_offset,
+                 nullptr, s, merge_prev ? &pp->pending_fin : nullptr);
   if (rc) return rc;
   pp->pending = true;
   pp->pending_fin = fa;

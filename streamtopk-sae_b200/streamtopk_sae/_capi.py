@@ -27,7 +27,7 @@ EXPORTS = (
     "stk_workspace_bytes_fp8", "stk_exact_forward_fp8", "stk_quantize_rows_fp8",
     "stk_approx_cand_workspace_bytes", "stk_approx_forward_cand", "stk_decode_forward",
     "stk_pipeline_workspace_bytes", "stk_pipeline_create", "stk_pipeline_submit", "stk_pipeline_flush",
-    "stk_pipeline_pipelined", "stk_pipeline_destroy",
+    "stk_pipeline_pipelined", "stk_pipeline_destroy", "stk_pipeline_create_sharded",
 )
 IPC_HANDLE_BYTES = 64
 
@@ -116,6 +116,8 @@ def load():
         L.stk_pipeline_flush.argtypes = [vp, vp]
         L.stk_pipeline_pipelined.restype = i32
         L.stk_pipeline_pipelined.argtypes = [vp]
+        L.stk_pipeline_create_sharded.restype = i32
+        L.stk_pipeline_create_sharded.argtypes = [ctypes.POINTER(vp), vp, i64, i64, i64, i64, i64, i32, i32, vp, sz]
         L.stk_pipeline_destroy.restype = i32
         L.stk_pipeline_destroy.argtypes = [vp]
         _lib = L

@@ -13,6 +13,10 @@ all capturable) and replays it.
     V, I = step(X_new)        # copies X_new into the static buffer, replays
 
 Outputs are the graph's own tensors (overwritten by the next replay).
+
+A pipelined encode (``EncodePipeline.submit`` / ``ShardedEncoder.submit``)
+finishes each batch in the next batch's launch: pass its ``flush`` as
+``finish``, called once after the captured steps, so every replay is complete.
 """
 from __future__ import annotations
 
@@ -20,7 +24,7 @@ import torch
 
 
 class CapturedEncode:
-    def __init__(self, fn, X_example, steps: int = 1, warmup: int = 3):
+    def __init__(self, fn, X_example, steps: int = 1, warmup: int = 3, finish=None):
         if steps < 1:
             raise ValueError("steps must be >= 1")
         self.fn = fn
@@ -32,12 +36,16 @@ class CapturedEncode:
             with torch.cuda.stream(side):
                 for _ in range(warmup):
                     fn(self.X)
+                if finish is not None:
+                    finish()
             torch.cuda.current_stream(self.X.device).wait_stream(side)
         torch.cuda.synchronize(self.X.device)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
             for _ in range(steps):
                 out = fn(self.X)
+            if finish is not None:
+                finish()
         self.V, self.I = out
 
     def replay(self):

@@ -222,6 +222,7 @@ class ShardedEncoder:
         self.max_rows = int(max_rows)
         self.exchange = None
         self.fallback_reason = None
+        self._pipe = None       # (handle, key, workspace) of the pipelined encode (submit / flush)
 
     def _peer_exchange(self, B, device):
         if self.exchange is not None and self.exchange.max_rows < B:
@@ -246,12 +247,77 @@ class ShardedEncoder:
             _capi.device_error(torch.cuda.current_stream(dev).cuda_stream)
 
     def close(self):
-        """Release the p2p exchange (collective); a no-op for the NCCL transport."""
+        """Release the pipeline and the p2p exchange (collective); a no-op for the NCCL transport."""
+        self._drop_pipeline()
         if self.exchange is not None:
             self.exchange.close()
             self.exchange = None
 
+    # ------------------------------------------------------------ pipelined encode
+    def _drop_pipeline(self):
+        if self._pipe is not None:
+            torch.cuda.synchronize(self.W.device)
+            _capi.load().stk_pipeline_destroy(self._pipe[0])
+            self._pipe = None
+
+    def _pipeline(self, X):
+        B, d = X.shape
+        key = (B, d, X.dtype)
+        if self._pipe is not None and self._pipe[1] == key:
+            return self._pipe[0]
+        if self.transport not in ("p2p", "auto") or self.W.shape[0] == 0 or self.world == 1:
+            return None
+        if self._pipe is not None:  # another shape: finish its last batch first
+            self.flush()
+            self._drop_pipeline()
+        ex = self._peer_exchange(B, X.device)
+        if ex is None:
+            return None
+        lib = _capi.load()
+        code = _DTYPE_CODE[X.dtype]
+        flags = _capi.STK_FLAG_ANY_K | _capi.STK_FLAG_ANY_D
+        nbytes = ctypes.c_size_t(0)
+        _capi.check(lib.stk_pipeline_workspace_bytes(B, d, self.W.shape[0], self.k, code, flags,
+                                                     ctypes.byref(nbytes)))
+        with torch.cuda.device(X.device):
+            ws = torch.empty(int(nbytes.value), dtype=torch.uint8, device=X.device)
+            h = ctypes.c_void_p()
+            _capi.check(lib.stk_pipeline_create_sharded(ctypes.byref(h), ex.handle, B, d, self.W.shape[0], self.k,
+                                                        self.f_offset, code, flags, ws.data_ptr(),
+                                                        int(nbytes.value)))
+        self._pipe = (h, key, ws)
+        return h
+
+    def submit(self, X):
+        """Pipelined encode of one batch (p2p transport): returns its (V, I),
+        complete in stream order once the next batch is submitted or after
+        ``flush()``.  Every rank submits the same batches in the same order.
+        Without the p2p exchange this is ``encode`` (complete at once)."""
+        X = X.contiguous()
+        _require(X.dim() == 2 and X.shape[1] == self.W.shape[1], "W_enc d-dim mismatch")
+        _require(X.dtype == self.W.dtype, "W_enc dtype must match X")
+        B = X.shape[0]
+        h = self._pipeline(X) if B > 0 else None
+        if h is None:
+            return self.encode(X)
+        V = torch.empty((B, self.k), dtype=torch.float32, device=X.device)
+        I = torch.empty((B, self.k), dtype=torch.int32, device=X.device)
+        with torch.cuda.device(X.device):
+            stream = torch.cuda.current_stream(X.device).cuda_stream
+            _capi.check(_capi.load().stk_pipeline_submit(h, X.data_ptr(), self.W.data_ptr(), self.b.data_ptr(),
+                                                         V.data_ptr(), I.data_ptr(), stream))
+        return V, I
+
+    def flush(self):
+        """Finish the last submitted batch (no-op if none is pending)."""
+        if self._pipe is None:
+            return
+        dev = self.W.device
+        with torch.cuda.device(dev):
+            _capi.check(_capi.load().stk_pipeline_flush(self._pipe[0], torch.cuda.current_stream(dev).cuda_stream))
+
     def encode(self, X):
+        self.flush()  # a pending pipelined batch uses the exchange first
         X = X.contiguous()
         _require(X.dim() == 2 and X.shape[1] == self.W.shape[1], "W_enc d-dim mismatch")
         _require(X.dtype == self.W.dtype, "W_enc dtype must match X")

@@ -6,7 +6,9 @@ transports of the per-rank key lists are checked:
   * "p2p":  stk_exchange_forward (publish kernel with peer stores into the
     other rank's receive buffer over CUDA IPC, bounded wait, final merge),
     eagerly and replayed from a CUDA graph (both receive slots), with an empty
-    shard, and with a batch larger than the exchange was sized for.
+    shard, and with a batch larger than the exchange was sized for;
+  * "p2p" pipelined (ShardedEncoder.submit / flush): each batch finished by
+    the next batch's score kernel, eagerly, mixed with encode, and in a graph.
 A failure test makes one rank skip a step: the other rank's final merge gives
 up after its (short) wait limit and reports device error 3.  Skipped when
 fewer than 2 GPUs are visible.  NCCL's NVLS is off for the child processes.
@@ -140,6 +142,45 @@ def _worker_p2p_timeout(rank, world, port, q):
         dist.destroy_process_group()
 
 
+def _worker_p2p_pipeline(rank, world, port, q):
+    """Pipelined submit / flush over the exchange: each batch is finished by the
+    next batch's score kernel (cross-GPU publish, wait and merge included)."""
+    dist, dev = _init(rank, world, port)
+    try:
+        import streamtopk_sae as stk
+        from streamtopk_sae import _capi, shard
+        from streamtopk_sae.graph import CapturedEncode
+        ok = []
+        for (B, d, F, k) in ((128, 2048, 65536, 64), (100, 768, 50000, 32)):
+            X, W, b = stk.make_inputs(B, d, F, dtype=torch.bfloat16, seed=9, device=dev, w_init="unit_rows")
+            f0, f1 = shard.shard_bounds(F, world, rank)
+            enc = shard.ShardedEncoder(W[f0:f1].clone(), b[f0:f1].clone(), F, f0, k, transport="p2p", max_rows=B)
+            Xs = [stk.make_inputs(B, d, 8, dtype=torch.bfloat16, seed=40 + i, device=dev)[0] for i in range(5)]
+            outs = [enc.submit(x) for x in Xs[:4]]
+            enc.flush()
+            mixed = enc.submit(Xs[4])
+            after = enc.encode(Xs[0])   # flushes the pending batch first
+            torch.cuda.synchronize()
+            for x, got in zip(Xs[:4] + [Xs[4], Xs[0]], outs + [mixed, after]):
+                ok.append(_same(got, stk.topk_sae_cuda_exact(x, W, b, k)))
+            g = CapturedEncode(enc.submit, Xs[0], steps=3, warmup=2, finish=enc.flush)
+            for seed in (21, 22):
+                Xn = stk.make_inputs(B, d, 8, dtype=torch.bfloat16, seed=seed, device=dev)[0]
+                V, I = g(Xn)
+                torch.cuda.synchronize()
+                ok.append(_same((V, I), stk.topk_sae_cuda_exact(Xn, W, b, k)))
+            g.close()
+            ok.append(_capi.device_error(torch.cuda.current_stream().cuda_stream) == 0)
+            enc.close()
+        q.put((rank, ok))
+    except Exception as e:
+        q.put((rank, repr(e)))
+        raise
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def _run(target, extra):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -178,3 +219,7 @@ def test_two_gpu_p2p_graph_empty_shard_and_growth():
 
 def test_two_gpu_p2p_missing_rank_times_out():
     _run(_worker_p2p_timeout, ())
+
+
+def test_two_gpu_p2p_pipelined_submit_flush():
+    _run(_worker_p2p_pipeline, ())
