@@ -282,6 +282,7 @@ struct Plan {
   size_t ws_split;  // TF32: X's residual X - trunc13(X), 256-byte aligned
   size_t ws_q;      // fp8: X quantized (B x d bytes, 256-aligned), then its row scales
   size_t ws;
+  bool presync;     // pipelined encode: the sync region is already zero (cleared by an earlier batch's finish)
 };
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -297,6 +298,7 @@ int plan(const void* X, const void* W, int64_t B, int64_t d, int64_t F, int64_t 
   int rc = device_sms(&sms);
   if (rc) return rc;
   pl->L = list_len(k);
+  pl->presync = false;
   const bool aligned = (X == nullptr || aligned16(X)) && (W == nullptr || aligned16(W));
   // fp32 inputs run on tensor cores (3-pass TF32) by default up to d =
   // kTf32DefaultMaxD, where its accuracy is shown against float64 to hold the
@@ -496,8 +498,10 @@ int run_fused(const Plan& pl, const void* X, const void* W, const float* b, uint
       p.pilot_hist = reinterpret_cast<uint32_t*>(base + kSyncBytes);
     }
     if (pl.shared_floor) p.row_floor = reinterpret_cast<uint32_t*>(base + kSyncBytes);
-    cudaError_t me = cudaMemsetAsync(base, 0, pl.ws_sync, stream);
-    if (me != cudaSuccess) return cuda_fail(me, "cudaMemsetAsync(sync)");
+    if (!pl.presync) {
+      cudaError_t me = cudaMemsetAsync(base, 0, pl.ws_sync, stream);
+      if (me != cudaSuccess) return cuda_fail(me, "cudaMemsetAsync(sync)");
+    }
   }
   p.prev_finish = 0;
   std::memset(&p.pfin, 0, sizeof p.pfin);
@@ -1238,6 +1242,8 @@ struct stk_pipeline {
   bool pending;                // a batch waits for its finish
   stk::FinishArgs pending_fin; // its finish (lists in its half, its V / I)
   int pending_L;
+  int pending_half;
+  bool clean[2];               // the half's sync region is zero (its last batch's finish cleared it)
   stk_exchange* ex;            // F-sharded encode: the peer exchange of the finish (else null)
   int64_t index_offset;        // F-sharded encode: this rank's first feature
 };
@@ -1289,7 +1295,10 @@ int pipeline_device(const stk_pipeline* pp) {
 int pipeline_flush(stk_pipeline* pp, cudaStream_t s) {
   if (!pp->pending) return STK_OK;
   pp->pending = false;
-  return run_finish(pp->pending_L, pp->pending_fin, s);
+  int rc = run_finish(pp->pending_L, pp->pending_fin, s);
+  if (rc) return rc;
+  if (pp->pending_fin.zero) pp->clean[pp->pending_half] = true;
+  return STK_OK;
 }
 }  // namespace
 
@@ -1331,6 +1340,8 @@ int stk_pipeline_create(stk_pipeline** out, int64_t B, int64_t d, int64_t F, int
   pp->half = half;
   pp->step = 0;
   pp->pending = false;
+  pp->pending_half = 0;
+  pp->clean[0] = pp->clean[1] = false;
   pp->ex = nullptr;
   pp->index_offset = 0;
   rc = pipeline_plan(nullptr, nullptr, pp, &pl);
@@ -1377,7 +1388,8 @@ int stk_pipeline_submit(stk_pipeline* pp, const void* X, const void* W, const fl
   Plan pl;
   rc = pipeline_plan(X, W, pp, &pl);
   if (rc) return rc;
-  char* half = pp->ws + (size_t)(pp->step & 1ull) * pp->half;
+  const int h = (int)(pp->step & 1ull);
+  char* half = pp->ws + (size_t)h * pp->half;
   if (!pipelines(pl) || pl.ws > pp->half) {
     // Not pipelined: the pending batch first, then this one as one call.
     rc = pipeline_flush(pp, s);
@@ -1393,6 +1405,7 @@ int stk_pipeline_submit(stk_pipeline* pp, const void* X, const void* W, const fl
       rc = encode(X, W, b, V, I, nullptr, pp->B, pp->d, pp->F, pp->k, pp->dtype, pp->flags, 0u, half, pp->half, s);
     }
     if (rc) return rc;
+    pp->clean[h] = false;
     ++pp->step;
     return STK_OK;
   }
@@ -1401,16 +1414,25 @@ int stk_pipeline_submit(stk_pipeline* pp, const void* X, const void* W, const fl
   const stk::FinishArgs fa = finish_args(partials, pl.grid.segs, (int64_t)pl.grid.m_tiles * stk::kRows, pl.pitch,
                                          pl.pitch - pl.L, pp->B, pp->k, V, I, nullptr,
                                          pp->ex ? &pp->ex->dev : nullptr);
+  stk::FinishArgs fz = fa;  // this batch's finish also clears its sync region
+  if (pl.ws_sync) {
+    fz.zero = reinterpret_cast<uint32_t*>(half + pl.ws_partials + pl.ws_app);
+    fz.zero_words = (int64_t)(pl.ws_sync / 4);
+  }
   const bool merge_prev = pp->pending && pp->pending_L == pl.L;
   if (pp->pending && !merge_prev) {
     rc = pipeline_flush(pp, s);
     if (rc) return rc;
   }
+  pl.presync = pp->clean[h];
   rc = run_fused(pl, X, W, b, partials, app, pp->B, pp->d, pp->F, pp->k, pp->dtype, (uint32_t)pp->index_offset,
                  nullptr, s, merge_prev ? &pp->pending_fin : nullptr);
   if (rc) return rc;
+  if (merge_prev && pp->pending_fin.zero) pp->clean[pp->pending_half] = true;
+  pp->clean[h] = false;
   pp->pending = true;
-  pp->pending_fin = fa;
+  pp->pending_fin = fz;
+  pp->pending_half = h;
   pp->pending_L = pl.L;
   ++pp->step;
   return STK_OK;

@@ -314,6 +314,15 @@ __device__ __forceinline__ void publish_row(const ExchangeDev& ex, const FinishS
 // CTA calls it.  With the exchange, all of this CTA's rows are published
 // before any wait, so CTAs that run at the same time on different GPUs never
 // wait on each other in a cycle.
+// Clears fa.zero (pipelined encode): part of CTA `cta` of `ctas`, `nthreads`
+// threads, 16-byte stores.
+__device__ __forceinline__ void clear_sync_region(const FinishArgs& fa, int cta, int ctas, int tid, int nthreads) {
+  if (fa.zero == nullptr) return;
+  uint4* z = reinterpret_cast<uint4*>(fa.zero);
+  const int64_t n = fa.zero_words / 4;
+  for (int64_t i = (int64_t)cta * nthreads + tid; i < n; i += (int64_t)ctas * nthreads) z[i] = make_uint4(0u, 0u, 0u, 0u);
+}
+
 template <int L, class S = SyncCta>
 __device__ void finish_rows(const FinishArgs& fa, FinishSmem& sm, int64_t row0, int64_t row_step, int tid,
                             int nthreads) {

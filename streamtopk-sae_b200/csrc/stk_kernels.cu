@@ -599,9 +599,11 @@ __global__ void __launch_bounds__((MODE & 3) == kModeTF32 ? kFusedThreads + 64 :
       // c + gridDim.x, ...; the shared memory of the top lists / append slots
       // is not in use before the first tile's epilogue.
       static_assert(PAIR || CAND || Cfg::kBarOff - Cfg::kTopOff >= (int)sizeof(FinishSmem), "finish scratch");
-      if (p.prev_finish)
+      if (p.prev_finish) {
         finish_rows<L, SyncEpilogue>(p.pfin, *reinterpret_cast<FinishSmem*>(smem + Cfg::kTopOff), blockIdx.x,
                                      gridDim.x, threadIdx.x - kFirstEpiWarp * 32, kEpilogueWarps * 32);
+        clear_sync_region(p.pfin, blockIdx.x, gridDim.x, threadIdx.x - kFirstEpiWarp * 32, kEpilogueWarps * 32);
+      }
     }
     const int q = warp & 3;
     const int r = q * 32 + lane;
@@ -975,6 +977,7 @@ __global__ void __launch_bounds__(kFinishThreads, 2) finish_kernel(const FinishA
   __shared__ FinishSmem sm;
   asm volatile("griddepcontrol.wait;" ::: "memory");
   finish_rows<L>(fa, sm, blockIdx.x, gridDim.x, threadIdx.x, blockDim.x);
+  clear_sync_region(fa, blockIdx.x, gridDim.x, threadIdx.x, blockDim.x);
 }
 
 // ---------------------------------------------------------------------------

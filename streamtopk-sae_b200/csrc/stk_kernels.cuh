@@ -77,6 +77,8 @@ struct FinishArgs {
   uint64_t* keys_out;  // (rows, L) or null: the row's top k, then further real keys descending, then empty keys
   int use_ex;
   ExchangeDev ex;
+  uint32_t* zero;      // pipelined encode: the finished batch's sync region (counters, pilot histogram), cleared
+  int64_t zero_words;  // after its rows for the batch after next (a multiple of 4 words); or null
 };
 
 struct FusedParams {
