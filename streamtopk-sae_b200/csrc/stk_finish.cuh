@@ -310,10 +310,6 @@ __device__ __forceinline__ void publish_row(const ExchangeDev& ex, const FinishS
   st_release_sys_u64(ex.peer_flag[p] + at, tag);
 }
 
-// Finishes rows row0, row0 + row_step, ... < fa.rows.  Every thread of the
-// CTA calls it.  With the exchange, all of this CTA's rows are published
-// before any wait, so CTAs that run at the same time on different GPUs never
-// wait on each other in a cycle.
 // Clears fa.zero (pipelined encode): part of CTA `cta` of `ctas`, `nthreads`
 // threads, 16-byte stores.
 __device__ __forceinline__ void clear_sync_region(const FinishArgs& fa, int cta, int ctas, int tid, int nthreads) {
@@ -323,9 +319,20 @@ __device__ __forceinline__ void clear_sync_region(const FinishArgs& fa, int cta,
   for (int64_t i = (int64_t)cta * nthreads + tid; i < n; i += (int64_t)ctas * nthreads) z[i] = make_uint4(0u, 0u, 0u, 0u);
 }
 
+// Finishes rows row0, row0 + row_step, ... < fa.rows.  Every thread of the
+// CTA (or of the group S synchronises) calls it.  Two phases, which the
+// pipelined encode runs apart (the first while the next batch's first tile
+// streams, the second after that batch's last tile):
+//   finish_rows_local: each row's select over this GPU's lists, then its V / I
+//     (or keys) -- or, with the exchange, its publication to every rank;
+//   finish_rows_world (exchange only): the bounded wait for the other ranks'
+//     copies of these rows, the select over the world's lists, V / I.
+// With the exchange, all of a CTA's rows are published before any wait, so
+// CTAs that run at the same time on different GPUs never wait on each other
+// in a cycle.  finish_rows_local returns the exchange's step (0 without it).
 template <int L, class S = SyncCta>
-__device__ void finish_rows(const FinishArgs& fa, FinishSmem& sm, int64_t row0, int64_t row_step, int tid,
-                            int nthreads) {
+__device__ unsigned long long finish_rows_local(const FinishArgs& fa, FinishSmem& sm, int64_t row0, int64_t row_step,
+                                                int tid, int nthreads) {
   unsigned long long step = 0;
   int slot = 0;
   if (fa.use_ex) {
@@ -340,7 +347,14 @@ __device__ void finish_rows(const FinishArgs& fa, FinishSmem& sm, int64_t row0, 
       write_row<L>(fa, sm, b, tid, nthreads);
     S::sync();
   }
+  return step;
+}
+
+template <int L, class S = SyncCta>
+__device__ void finish_rows_world(const FinishArgs& fa, FinishSmem& sm, int64_t row0, int64_t row_step, int tid,
+                                  int nthreads, unsigned long long step) {
   if (!fa.use_ex) return;
+  const int slot = (int)(step & 1ull);
   const ExchangeDev& ex = fa.ex;
   const unsigned long long t0 = global_timer_ns();
   for (int64_t b = row0; b < fa.rows; b += row_step) {
@@ -362,8 +376,8 @@ __device__ void finish_rows(const FinishArgs& fa, FinishSmem& sm, int64_t row0, 
         raise_device_error(kErrExchangeTimeout);
     }
     S::sync();
-    select_row<L, S>(ex.recv + (int64_t)slot * ex.world * ex.max_rows * L, ex.world, ex.max_rows, L, 0, b, fa.k, sm.valid,
-                  sm, tid, nthreads);
+    select_row<L, S>(ex.recv + (int64_t)slot * ex.world * ex.max_rows * L, ex.world, ex.max_rows, L, 0, b, fa.k,
+                     sm.valid, sm, tid, nthreads);
     write_row<L>(fa, sm, b, tid, nthreads);
     S::sync();
   }
@@ -377,6 +391,13 @@ __device__ void finish_rows(const FinishArgs& fa, FinishSmem& sm, int64_t row0, 
       ex.state[0] = step + 1ull;
     }
   }
+}
+
+template <int L, class S = SyncCta>
+__device__ void finish_rows(const FinishArgs& fa, FinishSmem& sm, int64_t row0, int64_t row_step, int tid,
+                            int nthreads) {
+  const unsigned long long step = finish_rows_local<L, S>(fa, sm, row0, row_step, tid, nthreads);
+  finish_rows_world<L, S>(fa, sm, row0, row_step, tid, nthreads, step);
 }
 
 }  // namespace stk

@@ -592,17 +592,21 @@ __global__ void __launch_bounds__((MODE & 3) == kModeTF32 ? kFusedThreads + 64 :
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // Pipelined encode: the previous step's rows, from the lists that step's
+    // score kernel left (complete: it ran before this grid in the stream),
+    // while this CTA's first tile streams in.  CTA c takes rows c,
+    // c + gridDim.x, ...; the shared memory of the top lists / append slots is
+    // not in use before the first tile's epilogue.  Over the peer exchange this
+    // includes the publication, the wait for the other ranks' rows and the
+    // world select.  (Moving the wait and the world select after the last tile
+    // measured no faster on 2 GPUs.)
+    static_assert(PAIR || CAND || Cfg::kBarOff - Cfg::kTopOff >= (int)sizeof(FinishSmem), "finish scratch");
     if constexpr (!PAIR && !CAND) {
-      // Pipelined encode: the previous step's rows, from the lists that step's
-      // score kernel left (complete: it ran before this grid in the stream),
-      // while this CTA's first tile streams in.  CTA c takes rows c,
-      // c + gridDim.x, ...; the shared memory of the top lists / append slots
-      // is not in use before the first tile's epilogue.
-      static_assert(PAIR || CAND || Cfg::kBarOff - Cfg::kTopOff >= (int)sizeof(FinishSmem), "finish scratch");
       if (p.prev_finish) {
+        const int etid = threadIdx.x - kFirstEpiWarp * 32;
         finish_rows<L, SyncEpilogue>(p.pfin, *reinterpret_cast<FinishSmem*>(smem + Cfg::kTopOff), blockIdx.x,
-                                     gridDim.x, threadIdx.x - kFirstEpiWarp * 32, kEpilogueWarps * 32);
-        clear_sync_region(p.pfin, blockIdx.x, gridDim.x, threadIdx.x - kFirstEpiWarp * 32, kEpilogueWarps * 32);
+                                     gridDim.x, etid, kEpilogueWarps * 32);
+        clear_sync_region(p.pfin, blockIdx.x, gridDim.x, etid, kEpilogueWarps * 32);
       }
     }
     const int q = warp & 3;
