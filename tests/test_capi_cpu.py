@@ -102,3 +102,26 @@ def test_p2p_transport_rejects_custom_kernels():
         shard.ShardedEncoder(W, b, 128, 0, 8, transport="p2p", shard_fn=lambda *a: None)
     with pytest.raises(RuntimeError, match="transport must be"):
         shard.ShardedEncoder(W, b, 128, 0, 8, transport="mpi")
+
+
+def test_pipeline_argument_checks():
+    """The pipelined encode validates its arguments before touching the device."""
+    lib = _capi.load()
+    n = ctypes.c_size_t(0)
+    assert lib.stk_pipeline_workspace_bytes(128, 64, 1000, 0, _capi.STK_BF16, 0, ctypes.byref(n)) == _capi.STK_EINVAL
+    assert "k out of range" in lib.stk_last_error().decode()
+    assert lib.stk_pipeline_workspace_bytes(128, 64, 1000, 3, _capi.STK_BF16, 0, ctypes.byref(n)) == _capi.STK_EINVAL
+    assert "unsupported k=3" in lib.stk_last_error().decode()
+    assert lib.stk_pipeline_workspace_bytes(0, 64, 1000, 8, _capi.STK_BF16, 0, ctypes.byref(n)) == _capi.STK_EINVAL
+    assert "B must be >= 1" in lib.stk_last_error().decode()
+    h = ctypes.c_void_p()
+    assert lib.stk_pipeline_create(ctypes.byref(h), 128, 64, 1000, 256, _capi.STK_BF16, _capi.STK_FLAG_ANY_K,
+                                   None, 0) == _capi.STK_EINVAL
+    assert lib.stk_pipeline_submit(None, None, None, None, None, None, None) == _capi.STK_EINVAL
+    assert "pipeline is NULL" in lib.stk_last_error().decode()
+    assert lib.stk_pipeline_flush(None, None) == _capi.STK_EINVAL
+    assert lib.stk_pipeline_pipelined(None) == 0
+    assert lib.stk_pipeline_destroy(None) == _capi.STK_OK
+    assert lib.stk_pipeline_create_sharded(ctypes.byref(h), None, 128, 64, 1000, 8, 0, _capi.STK_BF16, 0,
+                                           None, 0) == _capi.STK_EINVAL
+    assert "exchange is NULL" in lib.stk_last_error().decode()
