@@ -35,7 +35,8 @@ constexpr size_t kAppendBytesPerCta = (size_t)kAppendMax * kRows * 8;
 // that holds its k-th largest histogrammed score as filter floor.
 constexpr int kPilotBits = 12;
 constexpr int kPilotChunks = 2;  // default sampled 32-feature chunks per CTA
-constexpr int kPilotGroup = 8;   // scores per histogrammed group maximum
+constexpr int kPilotGroup = 16;  // scores per histogrammed group maximum (8: 2-4 % slower at cfg2 / one N = 8
+                                 // shard -- twice the global atomics for about the same bound)
 constexpr int kPilotBins = 1 << kPilotBits;
 constexpr uint32_t kPilotTopSlack = 8;  // bins (one octave) the bound's window reaches above a CTA's own top
 constexpr unsigned long long kPilotWaitNs = 200000;  // give up (no floor) after 200 us
