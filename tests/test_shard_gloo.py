@@ -83,6 +83,11 @@ def _worker(rank, world, port, F, k, out_q, transport="nccl"):
         else:
             enc = shard.ShardedEncoder(W[f0:f1], b[f0:f1], F, f0, k, shard_fn=cpu_shard_fn, merge_fn=cpu_merge_fn)
         V, I = enc.encode(X)
+        # The pipelined submit / flush falls back to encode without the p2p
+        # exchange: same result, complete at once.
+        Vs, Is = enc.submit(X)
+        enc.flush()
+        assert torch.equal(V, Vs) and torch.equal(I, Is)
         if transport == "auto":
             assert enc.transport == "nccl" and enc.fallback_reason, (enc.transport, enc.fallback_reason)
             V2, I2 = enc.encode(X)     # later steps stay on the fallback path
