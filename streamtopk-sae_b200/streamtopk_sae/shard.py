@@ -226,6 +226,8 @@ class ShardedEncoder:
 
     def _peer_exchange(self, B, device):
         if self.exchange is not None and self.exchange.max_rows < B:
+            self.flush()
+            self._drop_pipeline()  # it holds the exchange being replaced
             self.exchange.close()
             self.exchange = None
         if self.exchange is None:
