@@ -245,6 +245,7 @@ def time_reference_single(cfg, budget_s=10.0):
     t = statistics.median(ts)
     rows_s = cfg["B"] / t * (f_s / cfg["F"])
     return {"value": rows_s, "unit": "rows/s", "cores": 1, "kind": "reference",
+            "extrapolated": {"measured_F": f_s, "reported_F": cfg["F"], "how": "x F_sample/F (linear in F)"},
             "sample": f"reference topk_sae_cpu (oracle/_ref, 1 thread as shipped: no OpenMP) on all "
                       f"{cfg['B']} rows x {f_s} of {cfg['F']} features, fp32 upcast, median of 3; "
                       f"rows/s scaled by F_sample/F (cost is linear in F); host has {os.cpu_count()} cores"}
@@ -298,6 +299,8 @@ def run_reference(args, cfg):
                                    f"{f_s} of {cfg['F']} features per step (fp32 upcast); rows/s scaled by "
                                    f"F_sample/F (cost is linear in F)"},
         "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "extrapolated": {"measured_F": f_s, "reported_F": cfg["F"],
+                         "how": "rows/s on an F sample x F_sample/F (the CPU op's cost is linear in F)"},
     }
     print(json.dumps(line))
     return 0
