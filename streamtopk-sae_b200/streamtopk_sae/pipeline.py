@@ -43,7 +43,7 @@ class EncodePipeline:
             _capi.check(lib.stk_pipeline_create(ctypes.byref(h), self.B, self.d, self.F, self.k, code, self.flags,
                                                 self.workspace.data_ptr(), int(nbytes.value)))
         self._handle = h
-        self._keep = []  # the pending batch's inputs, alive until its finish is enqueued
+        self._keep = []  # the pending batch's V / I (written by the next launch), alive until then
 
     @property
     def pipelined(self) -> bool:

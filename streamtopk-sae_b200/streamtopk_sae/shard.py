@@ -223,6 +223,7 @@ class ShardedEncoder:
         self.exchange = None
         self.fallback_reason = None
         self._pipe = None       # (handle, key, workspace) of the pipelined encode (submit / flush)
+        self._pending = None    # the pending batch's (V, I): written by the next launch, kept alive until then
 
     def _peer_exchange(self, B, device):
         if self.exchange is not None and self.exchange.max_rows < B:
@@ -308,6 +309,7 @@ class ShardedEncoder:
             stream = torch.cuda.current_stream(X.device).cuda_stream
             _capi.check(_capi.load().stk_pipeline_submit(h, X.data_ptr(), self.W.data_ptr(), self.b.data_ptr(),
                                                          V.data_ptr(), I.data_ptr(), stream))
+        self._pending = (V, I)
         return V, I
 
     def flush(self):
@@ -317,6 +319,7 @@ class ShardedEncoder:
         dev = self.W.device
         with torch.cuda.device(dev):
             _capi.check(_capi.load().stk_pipeline_flush(self._pipe[0], torch.cuda.current_stream(dev).cuda_stream))
+        self._pending = None
 
     def encode(self, X):
         self.flush()  # a pending pipelined batch uses the exchange first
