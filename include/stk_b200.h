@@ -102,7 +102,8 @@ STK_API int stk_exact_forward(const void* X, const void* W, const float* b, floa
  * stk_pipeline_workspace_bytes (two halves, used by alternate batches); the
  * caller allocates it and keeps it for the pipeline's lifetime.  Submit and
  * flush on one stream (or order the streams), from one host thread at a time
- * (a pipeline holds host state: the pending batch).  Shapes that do not pipeline
+ * (a pipeline holds host state: the pending batch).  stk_pipeline_destroy
+ * does not finish a pending batch: flush first, or its V / I stay unwritten.  Shapes that do not pipeline
  * (k > 64, several rounds of units per CTA, unaligned operands:
  * stk_pipeline_pipelined() == 0) run each batch as stk_exact_forward
  * (complete at once).  X, W, b, V, I per batch as in stk_exact_forward;
